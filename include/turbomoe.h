@@ -1,0 +1,172 @@
+/*
+ * turbomoe.h -- C ABI of libturbomoe.so, the B200 (sm_100a) kernels behind the
+ * FP8 mixture-of-experts hot path of Turbo-LLM (router + expert FFN).
+ *
+ * Conventions
+ *   - Every pointer argument is DEVICE memory unless stated otherwise.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every entry point returns 0 (TM_OK) on success or a negative TM_ERR_*
+ *     code; tm_last_error() returns a thread-local message for the last failure.
+ *     Argument errors are reported before anything is launched.
+ *   - The library never allocates on these paths.  The caller owns every buffer,
+ *     including one workspace per stream sized by tm_workspace_bytes() and
+ *     zeroed once by tm_workspace_init().  Kernels keep the workspace's
+ *     counters self-resetting, so consecutive calls (and CUDA-graph replays)
+ *     need no further initialisation.  Calls that share a workspace must be
+ *     ordered on one stream.
+ *   - Activations ("act") are fp32, fp16 or bf16 (tm_dtype); expert weights are
+ *     FP8 e4m3 with one fp32 `weight_scale_inv` per 128x128 block.
+ *
+ * Reference interfaces (kaushikharsh99/Turbo-LLM, paths inside that project):
+ *   The reference is pure Python; its "plugin boundary" is the class swap in
+ *   runtime/engine.py:14-21 (RouterExecutor, MoEExecutor, ExpertLoader).  The
+ *   Python drop-ins in turbo-llm_b200/{execution,loader} call this ABI through
+ *   ctypes; each function below names the reference code it replaces.
+ */
+#ifndef TURBOMOE_H
+#define TURBOMOE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TM_ABI_VERSION 1
+
+#define TM_OK 0
+#define TM_ERR_INVALID (-1)     /* bad argument (null pointer, shape, dtype) */
+#define TM_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define TM_ERR_WORKSPACE (-3)   /* workspace too small */
+#define TM_ERR_UNSUPPORTED (-4) /* shape outside what the kernels implement */
+
+typedef enum { TM_DTYPE_F32 = 0, TM_DTYPE_F16 = 1, TM_DTYPE_BF16 = 2 } tm_dtype;
+
+/* Device-side status bits written into the workspace (tm_workspace_status). */
+#define TM_STATUS_BAD_EXPERT_ID 1u  /* a top-k index was outside [0, n_experts) */
+
+int tm_abi_version(void);
+const char *tm_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* K0: FP8 block dequantisation.
+ * Replaces ExpertLoader.dequantize_weight (loader/expert_loader.py:127-160).
+ * out[r,c] = cast(w[r,c]) * cast(scale_inv[r/128, c/128]) evaluated exactly as
+ * the reference does in out_dtype: for fp32 one RN fp32 multiply; for fp16 and
+ * bf16 both operands are first rounded to out_dtype, the product is formed in
+ * fp32 and rounded to out_dtype (round-to-nearest-even).  rows, cols must be
+ * multiples of 128.  w: uint8 e4m3 [rows, cols] row-major; scale_inv fp32
+ * [rows/128, cols/128]; out [rows, cols] of out_dtype. */
+int tm_dequant_fp8_block(const uint8_t *w, const float *scale_inv, int64_t rows,
+                         int64_t cols, void *out, int out_dtype, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* K5: packed, device-resident expert layout (replaces the slot cache of
+ * ExpertLoader.load_expert / load_expert_dynamic, loader/expert_loader.py:269-576,
+ * and the RAM tier cache/ram_cache.py:6-101: every expert is uploaded once).
+ *
+ * Per expert (H = hidden, I = intermediate):
+ *   w13: gate and up interleaved in 16-byte column chunks,
+ *        [I/32][H/16][2 (gate, up)][32 rows][16 bytes]          = 2*I*H bytes
+ *   s13: [I/128][2][H/128] fp32                                  = 2*(I/128)*(H/128)
+ *   w2 : down, [H/32][I/16][32 rows][16 bytes]                   = H*I bytes
+ *   s2 : [H/128][I/128] fp32
+ * Experts are stacked: expert e starts at e * tm_packed_*(...). */
+int64_t tm_packed_w13_bytes(int hidden, int inter);
+int64_t tm_packed_s13_floats(int hidden, int inter);
+int64_t tm_packed_w2_bytes(int hidden, int inter);
+int64_t tm_packed_s2_floats(int hidden, int inter);
+
+/* Pack n_experts experts from checkpoint layout.  gate/up: [n, I, H] e4m3
+ * (row-major, as <expert>.gate_proj.weight); gate_s/up_s: [n, I/128, H/128];
+ * down: [n, H, I]; down_s: [n, H/128, I/128].  Outputs are the first n
+ * experts of the packed arrays above.  H and I must be multiples of 128. */
+int tm_pack_experts(const uint8_t *gate, const float *gate_s, const uint8_t *up,
+                    const float *up_s, const uint8_t *down, const float *down_s,
+                    int n_experts, int hidden, int inter, uint8_t *w13, float *s13,
+                    uint8_t *w2, float *s2, void *stream);
+
+/* Dequantise one packed expert back to dense [I,H], [I,H], [H,I] tensors of
+ * out_dtype with the arithmetic of tm_dequant_fp8_block.  Backs
+ * ExpertLoader.load_expert's return value (loader/expert_loader.py:362-576);
+ * not on the hot path.  Any of the three outputs may be NULL. */
+int tm_unpack_expert(const uint8_t *w13, const float *s13, const uint8_t *w2,
+                     const float *s2, int hidden, int inter, void *gate_out,
+                     void *up_out, void *down_out, int out_dtype, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Workspace: routing plan, intermediate activations and counters for one
+ * MoE layer call with at most max_tokens tokens. */
+int64_t tm_workspace_bytes(int64_t max_tokens, int n_experts, int top_k, int hidden,
+                           int inter, int shared_inter);
+int tm_workspace_init(void *ws, int64_t ws_bytes, void *stream);
+/* Copy the device status word (TM_STATUS_* bits) to *host_status and clear it;
+ * synchronises `stream`. */
+int tm_workspace_status(void *ws, int64_t ws_bytes, uint32_t *host_status, void *stream);
+/* Byte offsets (within the workspace) of the routing plan written by
+ * tm_router_topk / tm_route_plan for a call with `tokens` tokens, in this
+ * order: meta (int32 [n_active, pairs, tokens]), counts (int32 [E]), offsets
+ * (int32 [E+1]), act_list (int32 [n_active], ascending expert ids), slot_token
+ * (int32 [T*k]), slot_pair (int32 [T*k], pair = token*k + rank), pair_slot
+ * (int32 [T*k]), status (uint32).  Lets a caller inspect or reuse the plan
+ * (the reference builds the same grouping implicitly in execution/moe.py:132,164). */
+int tm_plan_offsets(int64_t tokens, int n_experts, int top_k, int64_t *out8);
+
+/* ------------------------------------------------------------------------ */
+/* K1: fused router.  Replaces RouterExecutor.compute_routing
+ * (execution/router.py:15-42) and the implicit grouping of
+ * MoEExecutor.execute_layer (execution/moe.py:132,164-165).
+ *   logits = x @ router_w^T, fp32 accumulation, rounded to act dtype;
+ *   p = softmax(logits) in fp32; top_k by value (ties: lower expert id first);
+ *   w = p / sum(p_topk) in fp32, stored in act dtype; idx stored as int64.
+ * Also writes the routing plan into the workspace: per-expert counts and
+ * offsets, the list of active experts (ascending) and the stable permutation
+ * (experts ascending, tokens ascending within an expert), which the expert
+ * kernels consume.  x: [tokens, hidden] act; router_w: [n_experts, hidden] act;
+ * topk_idx: [tokens, top_k] int64; topk_w: [tokens, top_k] act;
+ * logits_out: optional [tokens, n_experts] act (NULL to skip). */
+int tm_router_topk(const void *x, int64_t tokens, int hidden, int act_dtype,
+                   const void *router_w, int n_experts, int top_k, int64_t *topk_idx,
+                   void *topk_w, void *logits_out, void *ws, int64_t ws_bytes,
+                   void *stream);
+
+/* Build only the routing plan from caller-supplied top-k indices (used when
+ * MoEExecutor.execute_layer receives indices that did not come from
+ * tm_router_topk).  Indices outside [0, n_experts) are skipped and flagged
+ * with TM_STATUS_BAD_EXPERT_ID. */
+int tm_route_plan(const int64_t *topk_idx, int64_t tokens, int top_k, int n_experts,
+                  void *ws, int64_t ws_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* K2: gate+up dequant-GEMV with SwiGLU for the tokens of every active expert
+ * (and the shared expert when sh_w13 != NULL).  Replaces the gate/up/SiLU part
+ * of moe_seq (execution/moe.py:15-17), of the multi-token loop
+ * (execution/moe.py:168-172) and of the shared expert (moe.py:74-77,191-194).
+ * Needs the plan of tm_router_topk / tm_route_plan in `ws`.  Writes
+ * h = silu(x G^T) * (x U^T) (fp32) into the workspace.  sh_gate_w: [hidden]
+ * act, the shared expert's sigmoid-gate row (mlp.shared_expert_gate.weight);
+ * required when sh_w13 != NULL.  hidden % 512 == 0, inter % 256 == 0,
+ * shared_inter % 256 == 0. */
+int tm_moe_decode_gateup(const void *x, int64_t tokens, int hidden, int inter,
+                         int n_experts, int top_k, int act_dtype, const uint8_t *w13,
+                         const float *s13, const uint8_t *sh_w13, const float *sh_s13,
+                         int shared_inter, const void *sh_gate_w, void *ws,
+                         int64_t ws_bytes, void *stream);
+
+/* K3: down dequant-GEMV with the routing-weighted combine (+ the
+ * sigmoid-gated shared expert, + an optional residual).  Replaces moe_seq's
+ * down projection and weighted sum (execution/moe.py:18-19), the weighted
+ * scatter-add of the multi-token path (moe.py:173-176) and the shared-expert
+ * add (moe.py:79-85,196-202).  out[t] = residual[t] + sum_k topk_w[t,k] *
+ * down_{idx[t,k]}(h) + gate_sh[t] * down_sh(h_sh).  residual may be NULL;
+ * out: [tokens, hidden] act. */
+int tm_moe_decode_down_combine(int64_t tokens, int hidden, int inter, int n_experts,
+                               int top_k, int act_dtype, const void *topk_w,
+                               const uint8_t *w2, const float *s2, const uint8_t *sh_w2,
+                               const float *sh_s2, int shared_inter, const void *residual,
+                               void *out, void *ws, int64_t ws_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TURBOMOE_H */

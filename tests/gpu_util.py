@@ -1,0 +1,45 @@
+"""Helpers shared by the GPU parity tests."""
+import torch
+
+from oracle import moe_oracle as O
+
+
+def packed_from_layer(lw, device="cuda"):
+    """(routed PackedExperts, shared PackedExperts|None, shared gate [H]|None)
+    for LayerWeights ``lw`` (any device), packed by tm_pack_experts."""
+    from turbomoe import ops
+    d = lambda t: t.to(device)
+    experts = ops.pack_experts(d(lw.gate), d(lw.gate_s), d(lw.up), d(lw.up_s), d(lw.down), d(lw.down_s))
+    shared = gate = None
+    if lw.sh_gate is not None:
+        shared = ops.pack_experts(d(lw.sh_gate), d(lw.sh_gate_s), d(lw.sh_up), d(lw.sh_up_s),
+                                  d(lw.sh_down), d(lw.sh_down_s))
+        gate = d(lw.sh_router).reshape(-1)
+    return experts, shared, gate
+
+
+def workspace_for(shape, device="cuda"):
+    from turbomoe import ops
+    return ops.Workspace(device, shape.experts, shape.top_k, shape.hidden, shape.inter, shape.shared_inter)
+
+
+def run_moe(lw, shape, x, idx, w, ws=None, residual=None):
+    from turbomoe import ops
+    experts, shared, gate = packed_from_layer(lw)
+    ws = ws or workspace_for(shape)
+    g = gate.to(x.dtype) if gate is not None else None
+    return ops.moe_experts(x.cuda(), idx.cuda(), w.cuda(), experts, ws, shared=shared, shared_gate_w=g,
+                           residual=residual)
+
+
+def oracle_fp32(lw, x, idx, w):
+    """The reference algorithm evaluated in fp32 (loader dtype fp32, fp32 act):
+    the precision the kernels compute in."""
+    layer = O.OracleLayer(lw, torch.float32)
+    return O.execute_layer(layer, x.float().cpu(), idx.cpu(), w.float().cpu())
+
+
+def assert_close(out, ref, maxabs, cos, what=""):
+    m, c = O.compare(out.cpu(), ref.cpu())
+    assert m <= maxabs and c >= cos, f"{what}: max-abs {m:.3e} (<= {maxabs}), cos {c:.7f} (>= {cos})"
+    return m, c

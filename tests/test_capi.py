@@ -1,0 +1,85 @@
+"""The C-ABI library loads and exports every symbol include/turbomoe.h declares.
+
+CPU only: nothing here launches a kernel.  Argument validation happens on
+the host before any launch, so the error paths are testable without a GPU.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+from turbomoe import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    txt = open(os.path.join(REPO, "include", "turbomoe.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(tm_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_library_built_and_loads():
+    assert os.path.exists(_lib.LIB_PATH), "run __graft_entry__.build() first"
+    L = _lib.lib()
+    assert L.tm_abi_version() == 1
+
+
+def test_every_declared_symbol_exported_and_bound():
+    L = ctypes.CDLL(_lib.LIB_PATH)
+    syms = header_symbols()
+    assert len(syms) >= 16
+    for s in syms:
+        assert hasattr(L, s), f"{s} declared in include/turbomoe.h but not exported"
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature in turbomoe/_lib.py"
+    assert set(_lib.SIGNATURES) == set(syms)
+
+
+def test_packed_sizes():
+    L = _lib.lib()
+    H, I = 2048, 768
+    assert L.tm_packed_w13_bytes(H, I) == 2 * H * I
+    assert L.tm_packed_w2_bytes(H, I) == H * I
+    assert L.tm_packed_s13_floats(H, I) == 2 * 6 * 16
+    assert L.tm_packed_s2_floats(H, I) == 16 * 6
+
+
+def test_workspace_bytes_monotone_and_header_fixed():
+    L = _lib.lib()
+    a = L.tm_workspace_bytes(1, 128, 8, 2048, 768, 0)
+    b = L.tm_workspace_bytes(64, 128, 8, 2048, 768, 0)
+    c = L.tm_workspace_bytes(64, 256, 8, 2048, 512, 512)
+    assert 0 < a < b and c > 0
+    assert L.tm_workspace_bytes(0, 128, 8, 2048, 768, 0) == -1
+    # the plan regions sit at the same offsets whatever the expert sizes are
+    o1 = (ctypes.c_int64 * 8)()
+    assert L.tm_plan_offsets(64, 128, 8, o1) == 0
+    assert list(o1)[1] > list(o1)[0]
+
+
+def test_argument_errors_reported_without_launch():
+    L = _lib.lib()
+    # rows not a multiple of 128 -> TM_ERR_INVALID before any CUDA call
+    rc = L.tm_dequant_fp8_block(16, 16, 100, 128, 16, 0, None)
+    assert rc == _lib.TM_ERR_INVALID
+    assert b"multiples of 128" in L.tm_last_error()
+    rc = L.tm_dequant_fp8_block(None, 16, 128, 128, 16, 0, None)
+    assert rc == _lib.TM_ERR_INVALID
+    # workspace too small
+    rc = L.tm_route_plan(256, 4, 8, 128, 256, 16, None)
+    assert rc == _lib.TM_ERR_WORKSPACE
+    assert b"workspace" in L.tm_last_error()
+    # unaligned workspace
+    rc = L.tm_route_plan(256, 4, 8, 128, 257, 1 << 30, None)
+    assert rc == _lib.TM_ERR_INVALID
+    # unknown act dtype
+    rc = L.tm_unpack_expert(16, 16, 16, 16, 512, 256, None, None, None, 7, None)
+    assert rc == _lib.TM_ERR_INVALID
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from turbomoe import ops
+    with pytest.raises(_lib.TurboMoEError):
+        ops.dequant_fp8_block(torch.zeros(128, 128, dtype=torch.uint8), torch.ones(1, 1))

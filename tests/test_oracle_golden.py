@@ -1,0 +1,104 @@
+"""Pin the oracle (oracle/moe_oracle.py) to the reference's own outputs.
+
+The fixtures under tests/golden/ were produced by importing and running the
+reference (ExpertLoader.dequantize_weight, RouterExecutor.compute_routing,
+MoEExecutor.execute_layer) on seeded synthetic checkpoints; see
+tests/golden/make_golden.py.  CPU only.
+"""
+import numpy as np
+import pytest
+import torch
+
+from golden_util import DTYPES, case_layer, case_x, fixture, meta
+from oracle import moe_oracle as O
+
+
+def _same_bits(a, b):
+    a = a.contiguous()
+    b = b.contiguous()
+    assert a.dtype == b.dtype and a.shape == b.shape
+    if a.dtype == torch.float32:
+        ia, ib = a.view(torch.int32), b.view(torch.int32)
+    else:
+        ia, ib = a.view(torch.int16), b.view(torch.int16)
+    nan = torch.isnan(a.float()) & torch.isnan(b.float())
+    return bool(((ia == ib) | nan).all())
+
+
+def test_fp8_table_matches_torch_cast():
+    tab = O.fp8_e4m3_table()
+    allb = torch.arange(256, dtype=torch.uint8)
+    t = allb.view(torch.float8_e4m3fn).float().numpy()
+    both_nan = np.isnan(tab) & np.isnan(t)
+    assert np.all((tab == t) | both_nan)
+    assert np.isnan(tab[0x7F]) and np.isnan(tab[0xFF]) and tab[0x7E] == 448.0
+    assert tab[0x01] == 2.0 ** -9 and tab[0x80] == 0.0 and np.signbit(tab[0x80])
+
+
+@pytest.mark.parametrize("mat", ["gate_proj", "down_proj", "allbits"])
+@pytest.mark.parametrize("dn", ["fp32", "bf16", "fp16"])
+def test_dequant_matches_reference(mat, dn):
+    fx = fixture("dequant")
+    w = fx[f"{mat}.w"].view(torch.float8_e4m3fn)
+    s = fx[f"{mat}.s"]
+    out = O.dequantize_weight(w, s, DTYPES[dn])
+    assert _same_bits(out, fx[f"{mat}.out_{dn}"])
+    if dn == "fp32":
+        assert _same_bits(O.dequant_fp32_exact(w, s), fx[f"{mat}.out_fp32"])
+
+
+SMALL = [("q3_small", 1), ("q3_small", 5), ("q3_small", 64), ("q3_small_fp16", 1),
+         ("q3_small_fp16", 33), ("q35_small", 1), ("q35_small", 64)]
+
+
+def _run_case(name, T):
+    shape, lw, info = case_layer(name)
+    fx = fixture(name)
+    x = case_x(name, T, fx)
+    layer = O.OracleLayer(lw, DTYPES[info["dtype"]])
+    logits = O.router_logits(x, layer.router)
+    idx, w = O.compute_routing(x, layer.router, shape.top_k)
+    y = O.execute_layer(layer, x, idx, w)
+    return fx, logits, idx, w, y
+
+
+def _check(fx, T, logits, idx, w, y):
+    if f"T{T}.rows" in fx:
+        rows = fx[f"T{T}.rows"]
+        assert _same_bits(logits[rows], fx[f"T{T}.logits_rows"])
+        y_ref, y = fx[f"T{T}.y_rows"], y[rows]
+    else:
+        assert _same_bits(logits, fx[f"T{T}.logits"])
+        y_ref = fx[f"T{T}.y"]
+    assert torch.equal(idx, fx[f"T{T}.idx"].long())
+    assert _same_bits(w, fx[f"T{T}.w"])
+    maxabs, cos = O.compare(y, y_ref)
+    # same torch ops in the same order on the same CPU: expect identical bits
+    assert maxabs == 0.0, (maxabs, cos)
+
+
+@pytest.mark.parametrize("name,T", SMALL)
+def test_layer_matches_reference_small(name, T):
+    fx, logits, idx, w, y = _run_case(name, T)
+    _check(fx, T, logits, idx, w, y)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name,T", [("q3_c0", 1), ("q3_c1", 2048), ("q35_c3", 64)])
+def test_layer_matches_reference_full(name, T):
+    fx, logits, idx, w, y = _run_case(name, T)
+    _check(fx, T, logits, idx, w, y)
+
+
+def test_routing_groups_order():
+    """The grouping order execute_layer uses: experts ascending, tokens ascending."""
+    idx = torch.tensor([[3, 1], [1, 0], [3, 2], [0, 1]])
+    g = O.routing_groups(idx, 4)
+    assert g["counts"].tolist() == [2, 3, 1, 2]
+    assert g["offsets"].tolist() == [0, 2, 5, 6, 8]
+    assert g["tokens"].tolist() == [1, 3, 0, 1, 3, 2, 0, 2]
+    assert g["kpos"].tolist() == [1, 0, 1, 0, 1, 1, 0, 0]
+
+
+def test_golden_meta_records_torch():
+    assert "torch" in meta() and meta()["cases"]

@@ -1,0 +1,86 @@
+"""Build libturbomoe.so in-tree with nvcc for sm_100a.
+
+    python -m turbomoe.build            (from turbo-llm_b200/)
+    python turbo-llm_b200/turbomoe/build.py
+
+Each ``csrc/*.cu`` is compiled to an object under ``_build/`` (skipped when the
+object is newer than the source and every header), then linked into
+``turbomoe/libturbomoe.so`` next to this file.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG_DIR)               # turbo-llm_b200/
+REPO = os.path.dirname(ROOT)
+CSRC = os.path.join(ROOT, "csrc")
+BUILD = os.path.join(ROOT, "_build")
+LIB = os.path.join(PKG_DIR, "libturbomoe.so")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
+              "--expt-relaxed-constexpr", "-I" + os.path.join(REPO, "include")]
+
+
+def nvcc() -> str:
+    for c in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if c and os.path.exists(c):
+            return c
+    raise RuntimeError("nvcc not found")
+
+
+def _headers():
+    return glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(REPO, "include", "*.h"))
+
+
+def _stale(obj, src, deps):
+    if not os.path.exists(obj):
+        return True
+    t = os.path.getmtime(obj)
+    return any(os.path.getmtime(p) > t for p in [src, *deps])
+
+
+def build(verbose: bool = False, ptxas_info: bool = False, jobs: int | None = None) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    deps = _headers()
+    cc = nvcc()
+    todo = []
+    objs = []
+    for s in srcs:
+        o = os.path.join(BUILD, os.path.basename(s)[:-3] + ".o")
+        objs.append(o)
+        if _stale(o, s, deps) or ptxas_info:
+            extra = ["-Xptxas", "-v"] if ptxas_info else []
+            todo.append([cc, *ARCH, *NVCC_FLAGS, *extra, "-c", s, "-o", o])
+
+    def run(cmd):
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        return cmd, r
+
+    failed = []
+    with cf.ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 1)) as ex:
+        for cmd, r in ex.map(run, todo):
+            if verbose or ptxas_info or r.returncode:
+                sys.stdout.write(r.stdout)
+                sys.stderr.write(r.stderr)
+            if r.returncode:
+                failed.append(cmd[-3])
+    if failed:
+        raise RuntimeError(f"nvcc failed for {failed}")
+    if todo or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
+        cmd = [cc, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("link of libturbomoe.so failed")
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose=True, ptxas_info="-v" in sys.argv))

@@ -1,0 +1,290 @@
+"""Tensor-level wrappers over the C ABI (device memory owned by PyTorch).
+
+Every function launches on ``torch.cuda.current_stream()`` and requires CUDA
+tensors; there is no CPU path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import (TM_DTYPE_BF16, TM_DTYPE_F16, TM_DTYPE_F32, TurboMoEError, check, lib)
+
+DTYPE_CODE = {torch.float32: TM_DTYPE_F32, torch.float16: TM_DTYPE_F16, torch.bfloat16: TM_DTYPE_BF16}
+
+
+def _code(dtype):
+    try:
+        return DTYPE_CODE[dtype]
+    except KeyError:
+        raise TurboMoEError(f"unsupported activation dtype {dtype}") from None
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise TurboMoEError("turbomoe kernels need CUDA tensors (there is no CPU fallback)")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _u8(t):
+    return t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t
+
+
+# ------------------------------------------------------------------ K0 ----
+def dequant_fp8_block(w: torch.Tensor, scale: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+    """``ExpertLoader.dequantize_weight`` on the device (bit-exact, see K0)."""
+    _need_cuda(w, scale)
+    w = _u8(w).contiguous()
+    scale = scale.float().contiguous()
+    M, N = w.shape
+    out = torch.empty(M, N, dtype=dtype, device=w.device)
+    check(lib().tm_dequant_fp8_block(w.data_ptr(), scale.data_ptr(), M, N, out.data_ptr(), _code(dtype),
+                                     _stream(w)), "tm_dequant_fp8_block")
+    return out
+
+
+# ------------------------------------------------------------------ K5 ----
+@dataclass
+class PackedExperts:
+    """Device-resident packed experts of one layer (or the shared expert)."""
+    w13: torch.Tensor   # uint8 [E * 2*I*H]
+    s13: torch.Tensor   # fp32  [E * 2*(I/128)*(H/128)]
+    w2: torch.Tensor    # uint8 [E * H*I]
+    s2: torch.Tensor    # fp32  [E * (H/128)*(I/128)]
+    n_experts: int
+    hidden: int
+    inter: int
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.w13, self.s13, self.w2, self.s2))
+
+    def expert_views(self, e: int):
+        L = lib()
+        H, I = self.hidden, self.inter
+        n13, ns13 = L.tm_packed_w13_bytes(H, I), L.tm_packed_s13_floats(H, I)
+        n2, ns2 = L.tm_packed_w2_bytes(H, I), L.tm_packed_s2_floats(H, I)
+        return (self.w13[e * n13:(e + 1) * n13], self.s13[e * ns13:(e + 1) * ns13],
+                self.w2[e * n2:(e + 1) * n2], self.s2[e * ns2:(e + 1) * ns2])
+
+
+def alloc_packed(n_experts: int, hidden: int, inter: int, device) -> PackedExperts:
+    L = lib()
+    e = n_experts
+    return PackedExperts(
+        torch.empty(e * L.tm_packed_w13_bytes(hidden, inter), dtype=torch.uint8, device=device),
+        torch.empty(e * L.tm_packed_s13_floats(hidden, inter), dtype=torch.float32, device=device),
+        torch.empty(e * L.tm_packed_w2_bytes(hidden, inter), dtype=torch.uint8, device=device),
+        torch.empty(e * L.tm_packed_s2_floats(hidden, inter), dtype=torch.float32, device=device),
+        n_experts, hidden, inter)
+
+
+def pack_experts(gate, gate_s, up, up_s, down, down_s, out: PackedExperts | None = None,
+                 first: int = 0) -> PackedExperts:
+    """Pack stacked checkpoint tensors (``gate/up [n, I, H]``, ``down [n, H, I]``
+    e4m3 plus their ``[n, ., .]`` fp32 scales, all on the device) into
+    ``out`` starting at expert ``first`` (a new PackedExperts when ``out`` is None)."""
+    if gate.dim() == 2:
+        gate, gate_s, up, up_s, down, down_s = (t.unsqueeze(0) for t in (gate, gate_s, up, up_s, down, down_s))
+    _need_cuda(gate, gate_s, up, up_s, down, down_s)
+    n, I, H = gate.shape
+    if out is None:
+        out = alloc_packed(n, H, I, gate.device)
+    if first + n > out.n_experts or out.hidden != H or out.inter != I:
+        raise TurboMoEError("pack_experts: destination shape mismatch")
+    L = lib()
+    ts = [_u8(t).contiguous() for t in (gate, up, down)]
+    ss = [s.float().contiguous() for s in (gate_s, up_s, down_s)]
+    o13 = first * L.tm_packed_w13_bytes(H, I)
+    os13 = first * L.tm_packed_s13_floats(H, I)
+    o2 = first * L.tm_packed_w2_bytes(H, I)
+    os2 = first * L.tm_packed_s2_floats(H, I)
+    check(L.tm_pack_experts(ts[0].data_ptr(), ss[0].data_ptr(), ts[1].data_ptr(), ss[1].data_ptr(),
+                            ts[2].data_ptr(), ss[2].data_ptr(), n, H, I,
+                            out.w13[o13:].data_ptr(), out.s13[os13:].data_ptr(),
+                            out.w2[o2:].data_ptr(), out.s2[os2:].data_ptr(), _stream(gate)),
+          "tm_pack_experts")
+    return out
+
+
+def unpack_expert(p: PackedExperts, e: int, dtype, which=("gate", "up", "down")):
+    """Dense dequantised (gate [I,H], up [I,H], down [H,I]) of expert ``e``."""
+    H, I = p.hidden, p.inter
+    w13, s13, w2, s2 = p.expert_views(e)
+    dev = w13.device
+    g = torch.empty(I, H, dtype=dtype, device=dev) if "gate" in which else None
+    u = torch.empty(I, H, dtype=dtype, device=dev) if "up" in which else None
+    d = torch.empty(H, I, dtype=dtype, device=dev) if "down" in which else None
+    check(lib().tm_unpack_expert(w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(), H, I,
+                                 _ptr(g), _ptr(u), _ptr(d), _code(dtype), _stream(w13)),
+          "tm_unpack_expert")
+    return g, u, d
+
+
+# ----------------------------------------------------------- workspace ----
+class Workspace:
+    """One caller-owned workspace per device for a model shape; grows with T.
+
+    The routing plan written by ``router_topk`` / ``route_plan`` lives here and
+    is consumed by ``moe_gateup`` / ``moe_down_combine`` of the same layer call,
+    so all of them must use the same Workspace on the same stream.
+    """
+
+    def __init__(self, device, n_experts, top_k, hidden, inter, shared_inter=0):
+        self.device = torch.device(device)
+        self.E, self.k, self.H, self.I, self.Is = n_experts, top_k, hidden, inter, shared_inter
+        self.buf = None
+        self.capacity_tokens = 0
+        # the top-k tensor the current plan was built from (a strong reference, so
+        # its memory cannot be recycled into a look-alike) and its version counter
+        self.plan_idx = None
+        self.plan_version = -1
+
+    def nbytes_for(self, tokens, top_k=None):
+        return lib().tm_workspace_bytes(tokens, self.E, top_k or self.k, self.H, self.I, self.Is)
+
+    def ensure(self, tokens, top_k=None) -> torch.Tensor:
+        need = self.nbytes_for(tokens, top_k)
+        if need < 0:
+            raise TurboMoEError("invalid workspace shape")
+        if self.buf is None or self.buf.numel() < need:
+            if torch.cuda.is_current_stream_capturing():
+                raise TurboMoEError("workspace must be sized (ensure) before CUDA graph capture")
+            cap = max(need, 2 * (self.buf.numel() if self.buf is not None else 0))
+            self.buf = torch.empty(cap, dtype=torch.uint8, device=self.device)
+            check(lib().tm_workspace_init(self.buf.data_ptr(), cap, _stream(self.buf)), "tm_workspace_init")
+            self.plan_idx = None
+        return self.buf
+
+    def status(self) -> int:
+        import ctypes
+        v = ctypes.c_uint32(0)
+        check(lib().tm_workspace_status(self.buf.data_ptr(), self.buf.numel(), ctypes.byref(v),
+                                        _stream(self.buf)), "tm_workspace_status")
+        return int(v.value)
+
+
+def _set_plan(ws: Workspace, idx: torch.Tensor):
+    ws.plan_idx = idx
+    ws.plan_version = idx._version
+
+
+def plan_matches(ws: Workspace, idx: torch.Tensor) -> bool:
+    return ws.plan_idx is idx and ws.plan_version == idx._version
+
+
+# ------------------------------------------------------------------ K1 ----
+def router_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int, ws: Workspace,
+                want_logits: bool = False):
+    """Fused router: returns ``(idx int64 [T,k], w [T,k] act dtype[, logits [T,E]])``
+    and leaves the routing plan for these indices in ``ws``."""
+    _need_cuda(x, router_w)
+    if x.dtype != router_w.dtype:
+        raise TurboMoEError(f"router weight dtype {router_w.dtype} != hidden dtype {x.dtype}")
+    x = x.contiguous()
+    router_w = router_w.contiguous()
+    T, H = x.shape
+    E = router_w.shape[0]
+    buf = ws.ensure(T, top_k)
+    idx = torch.empty(T, top_k, dtype=torch.int64, device=x.device)
+    w = torch.empty(T, top_k, dtype=x.dtype, device=x.device)
+    logits = torch.empty(T, E, dtype=x.dtype, device=x.device) if want_logits else None
+    check(lib().tm_router_topk(x.data_ptr(), T, H, _code(x.dtype), router_w.data_ptr(), E, top_k,
+                               idx.data_ptr(), w.data_ptr(), _ptr(logits), buf.data_ptr(), buf.numel(),
+                               _stream(x)), "tm_router_topk")
+    _set_plan(ws, idx)
+    return (idx, w, logits) if want_logits else (idx, w)
+
+
+def read_plan(ws: Workspace, tokens: int, top_k: int):
+    """Copy the routing plan of the last router/plan call out of ``ws`` (host
+    tensors; synchronises).  Returns dict(n_active, counts [E], offsets [E+1],
+    experts (ascending active ids), slot_token, slot_pair, pair_slot)."""
+    import ctypes
+    off = (ctypes.c_int64 * 8)()
+    check(lib().tm_plan_offsets(tokens, ws.E, top_k, off), "tm_plan_offsets")
+    b = ws.buf
+    P = tokens * top_k
+
+    def i32(o, n):
+        return b[o:o + 4 * n].view(torch.int32).cpu()
+
+    meta = i32(off[0], 3)
+    na = int(meta[0])
+    return {"n_active": na, "pairs": int(meta[1]), "tokens": int(meta[2]),
+            "counts": i32(off[1], ws.E), "offsets": i32(off[2], ws.E + 1),
+            "experts": i32(off[3], na), "slot_token": i32(off[4], P), "slot_pair": i32(off[5], P),
+            "pair_slot": i32(off[6], P)}
+
+
+def route_plan(idx: torch.Tensor, n_experts: int, ws: Workspace):
+    _need_cuda(idx)
+    src = idx
+    idx = idx.to(torch.int64).contiguous()
+    T, k = idx.shape
+    buf = ws.ensure(T, k)
+    check(lib().tm_route_plan(idx.data_ptr(), T, k, n_experts, buf.data_ptr(), buf.numel(), _stream(idx)),
+          "tm_route_plan")
+    _set_plan(ws, src)
+
+
+# --------------------------------------------------------------- K2/K3 ----
+def moe_gateup(x: torch.Tensor, top_k: int, packed: PackedExperts, ws: Workspace,
+               shared: PackedExperts | None = None, shared_gate_w: torch.Tensor | None = None):
+    """K2 alone: gate+up + SwiGLU for the plan already in ``ws`` (h stays in ``ws``)."""
+    T, H = x.shape
+    Is = shared.inter if shared is not None else 0
+    if shared is not None and shared_gate_w is None:
+        raise TurboMoEError("shared expert needs its gate weight")
+    sgw = shared_gate_w.reshape(-1).to(x.dtype).contiguous() if shared is not None else None
+    buf = ws.buf
+    check(lib().tm_moe_decode_gateup(x.data_ptr(), T, H, packed.inter, packed.n_experts, top_k, _code(x.dtype),
+                                     packed.w13.data_ptr(), packed.s13.data_ptr(),
+                                     _ptr(shared.w13) if shared else None, _ptr(shared.s13) if shared else None,
+                                     Is, _ptr(sgw), buf.data_ptr(), buf.numel(), _stream(x)),
+          "tm_moe_decode_gateup")
+
+
+def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out: torch.Tensor,
+                     shared: PackedExperts | None = None, residual: torch.Tensor | None = None):
+    """K3 alone: down projection + weighted combine into ``out`` (after K2)."""
+    T, H = out.shape
+    k = w.shape[1]
+    Is = shared.inter if shared is not None else 0
+    buf = ws.buf
+    check(lib().tm_moe_decode_down_combine(T, H, packed.inter, packed.n_experts, k, _code(out.dtype), w.data_ptr(),
+                                           packed.w2.data_ptr(), packed.s2.data_ptr(),
+                                           _ptr(shared.w2) if shared else None, _ptr(shared.s2) if shared else None,
+                                           Is, _ptr(residual), out.data_ptr(), buf.data_ptr(), buf.numel(),
+                                           _stream(out)), "tm_moe_decode_down_combine")
+
+
+def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Workspace,
+                shared: PackedExperts | None = None, shared_gate_w: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed experts (+ sigmoid-gated shared expert, + residual) for tokens
+    ``x [T,H]`` routed by ``idx/w [T,k]``.  Reuses the plan in ``ws`` when it
+    was built from this very ``idx`` tensor; otherwise builds it."""
+    _need_cuda(x, idx, w)
+    x = x.contiguous()
+    T, H = x.shape
+    k = idx.shape[1]
+    if not plan_matches(ws, idx):
+        route_plan(idx, packed.n_experts, ws)
+    ws.ensure(T, k)
+    if w.dtype != x.dtype:
+        w = w.to(x.dtype)
+    w = w.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    moe_gateup(x, k, packed, ws, shared, shared_gate_w)
+    moe_down_combine(w, packed, ws, out, shared, residual.contiguous() if residual is not None else None)
+    return out
