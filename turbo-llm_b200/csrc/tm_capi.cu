@@ -1,6 +1,11 @@
 // C-ABI plumbing: error reporting, workspace layout, workspace init/status.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <string.h>
+
+#include <mutex>
+#include <unordered_map>
+#include <utility>
 
 #include "tm_common.cuh"
 
@@ -30,6 +35,32 @@ int cuda_check(cudaError_t e, const char *what) {
 
 static int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("TM_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+int ensure_smem(const void *kernel, size_t dynamic_smem) {
+  static std::mutex mu;
+  static std::unordered_map<const void *, std::pair<size_t, size_t>> seen;  // static bytes, opted-in max
+  std::lock_guard<std::mutex> g(mu);
+  auto it = seen.find(kernel);
+  if (it == seen.end()) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return cuda_check(e, "cudaFuncGetAttributes");
+    it = seen.emplace(kernel, std::make_pair((size_t)fa.sharedSizeBytes, (size_t)0)).first;
+  }
+  if (it->second.first + dynamic_smem <= 48 * 1024 || dynamic_smem <= it->second.second) return TM_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dynamic_smem);
+  if (e != cudaSuccess) return cuda_check(e, "cudaFuncSetAttribute(max dynamic smem)");
+  it->second.second = dynamic_smem;
+  return TM_OK;
+}
+
 WsLayout ws_layout(int64_t tokens, int n_experts, int top_k, int hidden, int inter,
                    int shared_inter) {
   WsLayout L;
@@ -44,6 +75,7 @@ WsLayout ws_layout(int64_t tokens, int n_experts, int top_k, int hidden, int int
     return o;
   };
   L.status = take(4);
+  L.trace = take(kTraceBytes);  // right after the status word: offset independent of the shapes
   L.meta = take(8 * 4);
   L.router_cnt = take((kMaxTokenTiles + 1) * 4);
   L.k2_cnt = take((E + 1) * kMaxRG * 4);
@@ -53,6 +85,7 @@ WsLayout ws_layout(int64_t tokens, int n_experts, int top_k, int hidden, int int
   L.counts = take(E * 4);
   L.offsets = take((E + 1) * 4);
   L.act_list = take(E * 4);
+  L.act_rec = take(E * 16);
   L.slot_token = take(P * 4);
   L.slot_pair = take(P * 4);
   L.pair_slot = take(P * 4);
@@ -80,9 +113,10 @@ int ws_check(void *ws, int64_t ws_bytes, int64_t tokens, int n_experts, int top_
   TM_REQUIRE(tokens >= 1, "tokens must be >= 1 (got %lld)", (long long)tokens);
   TM_REQUIRE(n_experts >= 1 && n_experts <= 1024, "n_experts %d outside [1, 1024]", n_experts);
   TM_REQUIRE(top_k >= 1 && top_k <= 32 && top_k <= n_experts, "top_k %d outside [1, min(32, E)]", top_k);
-  TM_REQUIRE(hidden >= 128 && hidden <= 32 * kMaxRGo, "hidden %d outside [128, %d]", hidden, 32 * kMaxRGo);
-  TM_REQUIRE(inter >= 0 && inter <= 32 * kMaxRG && shared_inter >= 0 && shared_inter <= 32 * kMaxRG,
-             "inter (%d) and shared_inter (%d) must be <= %d", inter, shared_inter, 32 * kMaxRG);
+  TM_REQUIRE(hidden >= 128 && hidden <= kRows * kMaxRGo, "hidden %d outside [128, %d]", hidden,
+             kRows * kMaxRGo);
+  TM_REQUIRE(inter >= 0 && inter <= kRows * kMaxRG && shared_inter >= 0 && shared_inter <= kRows * kMaxRG,
+             "inter (%d) and shared_inter (%d) must be <= %d", inter, shared_inter, kRows * kMaxRG);
   *L = ws_layout(tokens, n_experts, top_k, hidden, inter, shared_inter);
   if (ws_bytes < L->total)
     return fail(TM_ERR_WORKSPACE, "workspace has %lld bytes, call needs %lld", (long long)ws_bytes,
@@ -113,6 +147,11 @@ extern "C" int tm_plan_offsets(int64_t tokens, int n_experts, int top_k, int64_t
   for (int i = 0; i < 8; ++i) out8[i] = v[i];
   return TM_OK;
 }
+
+#ifdef TM_TRACE
+// Trace builds only: byte offset of the trace region in the workspace.
+extern "C" int64_t tm_trace_offset(void) { return ws_layout(1, 1, 1, 128, 0, 0).trace; }
+#endif
 
 extern "C" int tm_workspace_init(void *ws, int64_t ws_bytes, void *stream) {
   TM_REQUIRE(ws != nullptr && ws_bytes > 0, "workspace is NULL or empty");

@@ -29,22 +29,60 @@ int cuda_check(cudaError_t e, const char *what);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Opt `kernel` into `dynamic_smem` bytes of dynamic shared memory when its
+// static plus dynamic shared memory exceeds the default 48 KB (cached per
+// kernel; a host-side attribute, legal during stream capture).
+int ensure_smem(const void *kernel, size_t dynamic_smem);
+
+// Programmatic dependent launch is on unless TM_PDL=0 is set in the
+// environment (read once; a launch-mode switch for measurements).
+bool pdl_enabled();
+
+// Launch with programmatic stream serialisation (PDL): the kernel may start
+// while the previous kernel of the stream finishes; it must call pdl_wait()
+// before touching anything that kernel writes.
+template <typename Kern, typename... Args>
+int launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const char *what,
+               Args... args) {
+  int rc = ensure_smem(reinterpret_cast<const void *>(kernel), smem);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, args...), what);
+}
+
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // ------------------------------------------------------------- act dtype ----
 template <typename T> struct Act;
+// Act<T>::ld_cg reads through L2 (never a possibly stale L1 line): used for
+// every activation an earlier kernel of the same step wrote.
 template <> struct Act<float> {
-  static __device__ __forceinline__ float load(const float *p) { return *p; }
+  static __device__ __forceinline__ float ld_cg(const float *p) { return __ldcg(p); }
   static __device__ __forceinline__ float to_f(float v) { return v; }
   static __device__ __forceinline__ float from_f(float v) { return v; }
   static __device__ __forceinline__ float round(float v) { return v; }
 };
 template <> struct Act<__half> {
+  static __device__ __forceinline__ __half ld_cg(const __half *p) {
+    return __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short *>(p)));
+  }
   static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
   static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
   static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
 };
 template <> struct Act<__nv_bfloat16> {
+  static __device__ __forceinline__ __nv_bfloat16 ld_cg(const __nv_bfloat16 *p) {
+    return __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short *>(p)));
+  }
   static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
   static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
   static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
@@ -97,14 +135,162 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t v) {
 }
 
 // ----------------------------------------------------------- memory ops ----
-// Streaming 16-byte load of read-only weights (no L1 allocation).
+// Streaming 16-byte load of read-only weights (no L1 allocation).  `volatile`
+// keeps the loads where the kernel issues them (all of a tile up front), so
+// they are in flight together instead of being sunk next to their first use.
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
   uint4 r;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
 }
+
+// ------------------------------------------- TMA bulk copies + mbarriers ----
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make the initialised barrier visible to the async (TMA) proxy.
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// One contiguous global -> shared copy by the TMA unit (no multicast);
+// completion is signalled on `bar` as transaction bytes.  src, dst 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void tma_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses (after a
+// CTA barrier: everyone's) before a following TMA write into the same bytes.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` for at most ~`max_ns` nanoseconds of
+// wall time (globaltimer).  Returns false on timeout; the caller records an
+// error and abandons the work instead of hanging the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint64_t max_ns = 1000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > max_ns) return false;
+  }
+}
+
+// ------------------------------------------ programmatic dependent launch ----
+// Kernels launched with cudaLaunchAttributeProgrammaticStreamSerialization may
+// start while the previous kernel in the stream still runs.  pdl_wait() blocks
+// until that kernel has completed and its writes are visible; everything
+// before it must touch only data no earlier kernel of the step writes
+// (weights).  pdl_trigger() lets the next kernel start launching.  Both are
+// no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// --------------------------------------------- warp-level tensor-core MMA ----
+// Decode GEMVs run on mma.sync m16n8k16 (f16 x f16 -> f32): the 16-row packed
+// chunk (16 rows x 16 bytes) is exactly one 16x16 A tile.  ldmatrix hands lane
+// l bytes [4t, 4t+4) of row l/4 (t = l%4); mapping those four columns to the
+// fragment's logical k = {2t, 2t+1, 2t+8, 2t+9} is a fixed permutation of the
+// chunk's 16 columns, applied identically to the activations (B), so the dot
+// products are unchanged and no register shuffling is needed.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// Four e4m3 bytes (one ldmatrix word) -> two f16x2 words: bytes 0,1 -> lo, 2,3 -> hi.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t v, uint32_t &lo, uint32_t &hi) {
+  asm("{\n\t.reg .b16 p, q;\n\tmov.b32 {p, q}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, p;\n\tcvt.rn.f16x2.e4m3x2 %1, q;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
+}
+
+// d += A(16x16 f16) * B(16x8 f16), fp32 accumulators.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Exponent s so that maxabs * 2^-s lies in [2^13, 2^14): activations scaled by
+// 2^-s are f16-representable exactly (bf16 / f16 inputs) with ample headroom
+// for the fp32 accumulators; results are scaled back by 2^s (exact).
+__device__ __forceinline__ int f16_shift(float maxabs) {
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 0;
+  int e;
+  frexpf(maxabs, &e);
+  return max(-100, min(100, e - 14));
+}
+
+// ------------------------------------------------------------- tracing ----
+// Builds with -DTM_TRACE record (kernel, event, CTA, globaltimer) per CTA into
+// a workspace region, to reconstruct kernel timelines inside CUDA graphs.
+// Product builds compile every hook to nothing and reserve no space.
+#ifdef TM_TRACE
+constexpr int64_t kTraceCap = 1 << 18;
+constexpr int64_t kTraceBytes = 16 + kTraceCap * 16;
+__device__ __forceinline__ void trace_event(uint32_t *tr, int kid, int ev) {
+  if (tr && threadIdx.x == 0) {
+    const unsigned i = atomicAdd(tr, 1u);
+    if (i < kTraceCap) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      uint64_t *e = reinterpret_cast<uint64_t *>(tr + 4) + 2 * i;
+      e[0] = ((uint64_t)kid << 56) | ((uint64_t)ev << 48) | (uint64_t)(blockIdx.x + blockIdx.y * gridDim.x);
+      e[1] = t;
+    }
+  }
+}
+#define TM_TRACE_EVENT(tr, kid, ev) ::tmoe::trace_event(tr, kid, ev)
+#else
+constexpr int64_t kTraceBytes = 0;
+#define TM_TRACE_EVENT(tr, kid, ev) ((void)0)
+#endif
+enum { kTrRouter = 1, kTrGateUp = 2, kTrDown = 3, kTrDownT1 = 4, kTrPlan = 5 };
+enum { kTrEnter = 0, kTrWaited = 1, kTrData = 2, kTrExit = 3 };
 
 // L2-coherent loads for data written by other CTAs of the same grid.
 __device__ __forceinline__ float ld_cg(const float *p) { return __ldcg(p); }
@@ -123,9 +309,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 // counters) depends only on the model shape, never on the token count, so the
 // counters stay where tm_workspace_init zeroed them whatever T a call uses;
 // the regions after it are laid out for the call's token count.
+// Row-group height of the packed expert layout (tm_pack_experts): weights are
+// stored as [row group][16-byte column chunk][rows of the group][16 bytes].
+constexpr int kRows = 16;
+
 constexpr int kMaxTokenTiles = 4096;
-constexpr int kMaxRG = 64;    // inter, shared_inter <= 2048 (row groups of 32)
-constexpr int kMaxRGo = 512;  // hidden <= 16384
+constexpr int kMaxRG = 128;    // inter, shared_inter <= 2048 (row groups of kRows)
+constexpr int kMaxRGo = 1024;  // hidden <= 16384 (row groups of kRows)
 
 // The header and the plan regions depend only on (T, E, top_k), so the router
 // (which does not know the expert sizes) and the expert kernels agree on them.
@@ -137,12 +327,14 @@ struct WsLayout {
   int64_t router_cnt;  // int32[kMaxTokenTiles + 1]: token-tile counters + tile-done counter
   int64_t k2_cnt;      // int32 [(E + 1) * kMaxRG]
   int64_t k3_cnt;      // int32 [kMaxRGo]
+  int64_t trace;       // kTraceBytes (0 in product builds)
   int64_t header_end;
   // per-call regions
   int64_t logits;      // fp32 [T][E] (act-rounded logits)
   int64_t counts;      // int32 [E]
   int64_t offsets;     // int32 [E + 1]
   int64_t act_list;    // int32 [E]
+  int64_t act_rec;     // int4 [E]: {expert, count, first slot, 0} per active expert
   int64_t slot_token;  // int32 [P]
   int64_t slot_pair;   // int32 [P]
   int64_t pair_slot;   // int32 [P]

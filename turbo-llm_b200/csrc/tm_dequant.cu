@@ -63,20 +63,20 @@ __global__ void k0_dequant(const uint8_t *__restrict__ w, const float *__restric
 }
 
 // ---------------------------------------------------------------- pack ----
-// w13 unit u (16 bytes) -> (e, rg, kc, mat, lane); row = rg*32+lane, col = kc*16
+// w13 unit u (16 bytes) -> (e, rg, kc, mat, r); row = rg*kRows+r, col = kc*16
 __global__ void k5_pack_w13(const uint8_t *__restrict__ gate, const uint8_t *__restrict__ up,
                             int n, int H, int I, uint8_t *__restrict__ w13) {
-  const int KC = H / 16, RG = I / 32;
-  const int64_t units = (int64_t)n * RG * KC * 2 * 32;
+  const int KC = H / 16, RG = I / kRows;
+  const int64_t units = (int64_t)n * RG * KC * 2 * kRows;
   for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units;
        u += (int64_t)gridDim.x * blockDim.x) {
     int64_t t = u;
-    const int lane = t % 32; t /= 32;
+    const int lane = t % kRows; t /= kRows;
     const int mat = t % 2; t /= 2;
     const int kc = t % KC; t /= KC;
     const int rg = t % RG; t /= RG;
     const int64_t e = t;
-    const int64_t r = rg * 32 + lane;
+    const int64_t r = rg * kRows + lane;
     const uint8_t *src = (mat ? up : gate) + (e * I + r) * H + (int64_t)kc * 16;
     reinterpret_cast<uint4 *>(w13)[u] = *reinterpret_cast<const uint4 *>(src);
   }
@@ -97,19 +97,19 @@ __global__ void k5_pack_s13(const float *__restrict__ gs, const float *__restric
   }
 }
 
-// w2 unit u -> (e, rgo, kc, lane); row = rgo*32+lane (0..H), col = kc*16 (0..I)
+// w2 unit u -> (e, rgo, kc, r); row = rgo*kRows+r (0..H), col = kc*16 (0..I)
 __global__ void k5_pack_w2(const uint8_t *__restrict__ down, int n, int H, int I,
                            uint8_t *__restrict__ w2) {
-  const int KC = I / 16, RG = H / 32;
-  const int64_t units = (int64_t)n * RG * KC * 32;
+  const int KC = I / 16, RG = H / kRows;
+  const int64_t units = (int64_t)n * RG * KC * kRows;
   for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units;
        u += (int64_t)gridDim.x * blockDim.x) {
     int64_t t = u;
-    const int lane = t % 32; t /= 32;
+    const int lane = t % kRows; t /= kRows;
     const int kc = t % KC; t /= KC;
     const int rg = t % RG; t /= RG;
     const int64_t e = t;
-    const int64_t r = rg * 32 + lane;
+    const int64_t r = rg * kRows + lane;
     const uint8_t *src = down + (e * H + r) * I + (int64_t)kc * 16;
     reinterpret_cast<uint4 *>(w2)[u] = *reinterpret_cast<const uint4 *>(src);
   }
@@ -124,7 +124,7 @@ __global__ void k5_unpack_w13(const uint8_t *__restrict__ w13, const float *__re
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int r = i / KC, kc = i % KC;
-    const int64_t u = (((int64_t)(r / 32) * KC + kc) * 2 + mat) * 32 + (r % 32);
+    const int64_t u = (((int64_t)(r / kRows) * KC + kc) * 2 + mat) * kRows + (r % kRows);
     const uint4 v = reinterpret_cast<const uint4 *>(w13)[u];
     const float sc = s13[((r / 128) * 2 + mat) * HB + (kc * 16) / 128];
     dq16<TO>(v, sc, out + (int64_t)r * H + kc * 16);
@@ -139,7 +139,7 @@ __global__ void k5_unpack_w2(const uint8_t *__restrict__ w2, const float *__rest
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int r = i / KC, kc = i % KC;
-    const int64_t u = ((int64_t)(r / 32) * KC + kc) * 32 + (r % 32);
+    const int64_t u = ((int64_t)(r / kRows) * KC + kc) * kRows + (r % kRows);
     const uint4 v = reinterpret_cast<const uint4 *>(w2)[u];
     const float sc = s2[(r / 128) * IB + (kc * 16) / 128];
     dq16<TO>(v, sc, out + (int64_t)r * I + kc * 16);

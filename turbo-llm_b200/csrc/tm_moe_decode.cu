@@ -3,50 +3,81 @@
 //
 // Reference: moe_seq (execution/moe.py:7-20), the multi-token loop of
 // MoEExecutor.execute_layer (moe.py:157-180) and the shared expert
-// (moe.py:73-85, 191-202).  Weights stream from the packed layout of
-// tm_pack_experts; every lane owns one weight row and reads 16 bytes per
-// column chunk, so a warp reads 512 contiguous bytes per instruction.  The
-// activations a lane needs are the same for all lanes (same columns), so they
-// come from shared memory as broadcasts.  Block scales are uniform per warp
-// (32 rows and 128 columns sit inside one 128x128 block).
+// (moe.py:73-85, 191-202).
+//
+// A decode layer is latency-bound long before it is bandwidth-bound (38 MB in
+// ~6 us), so each kernel keeps its chain of dependent memory round trips
+// short and has no serial tail:
+//   K2: a CTA owns one expert's 16 gate + 16 up rows over the whole hidden
+//       dimension (one contiguous 32*H-byte tile of the packed layout, ONE TMA
+//       bulk copy), so it produces final h = silu(g) * u itself;
+//   K3 (one token): a CTA owns 16 output rows for every routed expert at once
+//       (k tiles of 16*I bytes in flight together), combines them in shared
+//       memory in top-k order and writes the output;
+//   K3 (more tokens): a CTA owns (expert, 16 output rows); the last CTA of
+//       each row group combines the experts.
+// Lanes own weight rows (16 rows x 16 bytes = 256 contiguous bytes per
+// chunk; two chunks per warp instruction, conflict-free), the activations
+// they multiply come from shared memory as broadcasts, and block scales are
+// per 16-column chunk (128x128 blocks).  Kernels are chained with
+// programmatic dependent launch.
 #include "tm_common.cuh"
 
 namespace tmoe {
 
-constexpr int kK2Warps = 4;       // K2: 4 warps x 128 columns = 512 columns per CTA
+constexpr int kK2Warps = 4;                // K2: warps split the hidden dimension in 4
 constexpr int kK2Threads = kK2Warps * 32;
-constexpr int kK3Threads = 64;    // K3: 2 warps, one per half of the reduction dimension
+constexpr int kK3Warps = 4;                // K3 general: 4 warps x 2 half-warps = 8 K slices
+constexpr int kK3Threads = kK3Warps * 32;
+constexpr int kK3T1Warps = 8;              // K3 one token: one warp per routed expert
+constexpr int kK3T1Threads = kK3T1Warps * 32;
+constexpr int kK3T1MaxExperts = 16;        // routed + shared experts the one-token path holds
 constexpr int kCombineInKernelMaxT = 64;
 
 struct PlanView {
-  const int *meta, *counts, *offsets, *act_list, *slot_token, *pair_slot;
+  const int *meta;
+  const int4 *act_rec;  // {expert, count, first slot, 0} per active expert
+  const int *slot_token, *pair_slot;
+  uint32_t *status;
+  uint32_t *trace;  // trace builds only
 };
 
 static PlanView plan_view(void *ws, const WsLayout &L) {
-  return PlanView{ws_ptr<int>(ws, L.meta),     ws_ptr<int>(ws, L.counts),
-                  ws_ptr<int>(ws, L.offsets),  ws_ptr<int>(ws, L.act_list),
-                  ws_ptr<int>(ws, L.slot_token), ws_ptr<int>(ws, L.pair_slot)};
+  return PlanView{ws_ptr<int>(ws, L.meta),       ws_ptr<int4>(ws, L.act_rec),
+                  ws_ptr<int>(ws, L.slot_token), ws_ptr<int>(ws, L.pair_slot),
+                  ws_ptr<uint32_t>(ws, L.status), kTraceBytes ? ws_ptr<uint32_t>(ws, L.trace) : nullptr};
 }
 
-// Accumulate 16 weights (one 16-byte chunk) times 16 broadcast activations.
-__device__ __forceinline__ float dot16(const float (&w)[16], const float *xr) {
-  const float4 a = *reinterpret_cast<const float4 *>(xr);
-  const float4 b = *reinterpret_cast<const float4 *>(xr + 4);
-  const float4 c = *reinterpret_cast<const float4 *>(xr + 8);
-  const float4 d = *reinterpret_cast<const float4 *>(xr + 12);
-  float s = w[0] * a.x;
-  s = fmaf(w[1], a.y, s); s = fmaf(w[2], a.z, s); s = fmaf(w[3], a.w, s);
-  s = fmaf(w[4], b.x, s); s = fmaf(w[5], b.y, s); s = fmaf(w[6], b.z, s); s = fmaf(w[7], b.w, s);
-  s = fmaf(w[8], c.x, s); s = fmaf(w[9], c.y, s); s = fmaf(w[10], c.z, s); s = fmaf(w[11], c.w, s);
-  s = fmaf(w[12], d.x, s); s = fmaf(w[13], d.y, s); s = fmaf(w[14], d.z, s); s = fmaf(w[15], d.w, s);
+__device__ __forceinline__ int4 ld_cg4(const int4 *p) { return __ldcg(p); }
+
+// All threads wait for phase `parity` of `bar`; the outcome is CTA-uniform.
+// On timeout the status word is flagged and the CTA waits once more (bounded)
+// for its copies to land before it may exit.
+__device__ __forceinline__ bool tile_ready(uint64_t *bar, uint32_t *status, uint32_t parity = 0) {
+  const bool ok = mbar_wait_bounded(bar, parity);
+  if (__syncthreads_or(!ok)) {
+    if (threadIdx.x == 0) {
+      atomicOr(status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(bar, parity);
+    }
+    __syncthreads();
+    return false;
+  }
+  return true;
+}
+
+// acc += (16 e4m3 weights of `v`) . x[0..16) for one token, x in shared memory.
+__device__ __forceinline__ float dot_chunk(const uint4 &v, const float *x) {
+  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+  float s = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float w0, w1, w2, w3;
+    e4m3x4_to_f32(wv[q], w0, w1, w2, w3);
+    const float4 xv = *reinterpret_cast<const float4 *>(x + q * 4);
+    s = fmaf(w0, xv.x, s); s = fmaf(w1, xv.y, s); s = fmaf(w2, xv.z, s); s = fmaf(w3, xv.w, s);
+  }
   return s;
-}
-
-__device__ __forceinline__ void decode16(const uint4 &v, float (&w)[16]) {
-  e4m3x4_to_f32(v.x, w[0], w[1], w[2], w[3]);
-  e4m3x4_to_f32(v.y, w[4], w[5], w[6], w[7]);
-  e4m3x4_to_f32(v.z, w[8], w[9], w[10], w[11]);
-  e4m3x4_to_f32(v.w, w[12], w[13], w[14], w[15]);
 }
 
 // ===================================================================== K2 ====
@@ -58,166 +89,357 @@ template <typename TA> struct GateUpArgs {
   const float *sh_s13;
   const TA *sh_gate_w;
   PlanView pl;
-  int *k2_cnt;
-  float *gu_part, *sh_gu_part, *shg_part, *sh_w, *h, *sh_h;
-  int T, H, I, Is, E, P, KQ, RG, RGs;
-  int routed_ctas;  // max_active * RG * KQ
+  float *sh_w, *h, *sh_h;
+  int T, H, I, Is, E, P, RG, RGs;
+  int routed_ctas;  // max_active * RG
 };
 
 template <typename TA, int kNT>
-__global__ void __launch_bounds__(kK2Threads, 4) k2_gateup(GateUpArgs<TA> a) {
-  __shared__ __align__(16) float xs[kNT][512];
-  __shared__ float red[kK2Warps][kNT][2][32];
+__global__ void __launch_bounds__(kK2Threads) k2_gateup(GateUpArgs<TA> a) {
+  extern __shared__ __align__(128) uint8_t k2_smem[];
+  const int tile_bytes = 32 * a.H;                                   // [H/16 chunks][2][16 rows][16 B]
+  uint8_t *wtile = k2_smem;
+  float *xs = reinterpret_cast<float *>(k2_smem + tile_bytes);       // [kNT][H]
+  float *ssc = xs + kNT * a.H;                                       // [2][H/128] block scales
+  __shared__ float red[kK2Warps][kNT][32];
   __shared__ float gred[kK2Warps][kNT];
-  __shared__ int s_last;
+  __shared__ __align__(8) uint64_t bar;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrEnter);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();  // the routing plan and x come from earlier kernels
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrWaited);
   int b = blockIdx.x;
   bool shared_expert;
-  int aidx, rg, kq, n, slot0, I, RG;
+  int rg, n, slot0, I;
   const uint8_t *wbase;
   const float *sbase;
   if (b < a.routed_ctas) {
     shared_expert = false;
-    aidx = b / (a.RG * a.KQ);
-    const int rem = b % (a.RG * a.KQ);
-    rg = rem / a.KQ;
-    kq = rem % a.KQ;
-    if (aidx >= a.pl.meta[kMetaNActive]) return;
-    const int e = a.pl.act_list[aidx];
-    n = a.pl.counts[e];
-    slot0 = a.pl.offsets[e];
+    const int aidx = b / a.RG;
+    rg = b % a.RG;
+    const int n_active = ld_cg(a.pl.meta + kMetaNActive);
+    const int4 rec = ld_cg4(a.pl.act_rec + aidx);  // issued together with n_active
+    if (aidx >= n_active) return;
+    n = rec.y;
+    slot0 = rec.z;
     I = a.I;
-    RG = a.RG;
-    wbase = a.w13 + (int64_t)e * 2 * a.I * a.H;
-    sbase = a.s13 + (int64_t)e * 2 * (a.I / 128) * (a.H / 128);
+    wbase = a.w13 + (int64_t)rec.x * 2 * a.I * a.H;
+    sbase = a.s13 + (int64_t)rec.x * 2 * (a.I / 128) * (a.H / 128);
   } else {
     shared_expert = true;
-    b -= a.routed_ctas;
-    aidx = a.E;
-    rg = b / a.KQ;
-    kq = b % a.KQ;
+    rg = b - a.routed_ctas;
     n = a.T;
     slot0 = 0;
     I = a.Is;
-    RG = a.RGs;
     wbase = a.sh_w13;
     sbase = a.sh_s13;
   }
-  const int KC = a.H / 16, HB = a.H / 128;
-  const int c0 = kq * 512 + w * 128;  // this warp's 128 columns
-  // issue all 16 weight loads of this warp's tile (8 chunks x gate/up)
-  uint4 wv[8][2];
-  {
-    const uint8_t *p = wbase + ((int64_t)rg * KC + c0 / 16) * 1024 + lane * 16;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      wv[i][0] = ldg_stream(p + i * 1024);
-      wv[i][1] = ldg_stream(p + i * 1024 + 512);
-    }
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar, tile_bytes);
+    tma_bulk_g2s(wtile, wbase + (int64_t)rg * tile_bytes, tile_bytes, &bar);
   }
-  const int ib = (rg * 32) / 128;
-  const float sg = sbase[(ib * 2 + 0) * HB + c0 / 128];
-  const float su = sbase[(ib * 2 + 1) * HB + c0 / 128];
-  float *part = shared_expert ? a.sh_gu_part : a.gu_part;
-  const int nslots = shared_expert ? a.T : a.P;
+  pdl_trigger();
+  const int HB = a.H / 128, KC = a.H / 16;
+  const int ib = (rg * kRows) / 128;
+  for (int i = tid; i < 2 * HB; i += kK2Threads) ssc[i] = __ldg(sbase + ib * 2 * HB + i);
+  const int mat = lane >> 4;               // lanes 0-15: gate rows, 16-31: up rows
+  const int cpw = KC / kK2Warps;           // chunks per warp
+  const int kc0 = w * cpw;
+  const uint8_t *wl = wtile + kc0 * 512 + lane * 16;
+  const float *sl = ssc + mat * HB;
 
   for (int tg = 0; tg < n; tg += kNT) {
     const int nt = min(kNT, n - tg);
-    __syncthreads();  // xs / red reuse across groups
-    for (int i = tid; i < nt * 512; i += kK2Threads) {
-      const int j = i >> 9, c = i & 511;
-      const int t = shared_expert ? (tg + j) : a.pl.slot_token[slot0 + tg + j];
-      xs[j][c] = Act<TA>::to_f(a.x[(int64_t)t * a.H + kq * 512 + c]);
-    }
-    __syncthreads();
-    float ag[kNT], au[kNT];
+    if (tg) __syncthreads();  // xs / red reuse across token groups
+    {
+      // x rows as 16-byte vectors: all of a thread's loads are independent
+      constexpr int V = 16 / sizeof(TA);
+      const int vpt = a.H / V;
+      int tok[kNT];
 #pragma unroll
-    for (int j = 0; j < kNT; ++j) { ag[j] = 0.f; au[j] = 0.f; }
+      for (int j = 0; j < kNT; ++j)
+        tok[j] = (j >= nt) ? 0 : (shared_expert || a.T == 1) ? (tg + j) : ld_cg(a.pl.slot_token + slot0 + tg + j);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t gw[4] = {wv[i][0].x, wv[i][0].y, wv[i][0].z, wv[i][0].w};
-      const uint32_t uw[4] = {wv[i][1].x, wv[i][1].y, wv[i][1].z, wv[i][1].w};
+      for (int j = 0; j < kNT; ++j) {
+        if (j < nt) {
+          const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (int64_t)tok[j] * a.H);
+          for (int v = tid; v < vpt; v += kK2Threads) {
+            const uint4 q = __ldcg(src + v);
+            const TA *qe = reinterpret_cast<const TA *>(&q);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {  // 4 columns per 32-bit word
-        float g0, g1, g2, g3, u0, u1, u2, u3;
-        e4m3x4_to_f32(gw[q], g0, g1, g2, g3);
-        e4m3x4_to_f32(uw[q], u0, u1, u2, u3);
-#pragma unroll
-        for (int j = 0; j < kNT; ++j) {
-          if (j < nt) {
-            const float4 xv = *reinterpret_cast<const float4 *>(&xs[j][w * 128 + i * 16 + q * 4]);
-            ag[j] = fmaf(g0, xv.x, ag[j]); ag[j] = fmaf(g1, xv.y, ag[j]);
-            ag[j] = fmaf(g2, xv.z, ag[j]); ag[j] = fmaf(g3, xv.w, ag[j]);
-            au[j] = fmaf(u0, xv.x, au[j]); au[j] = fmaf(u1, xv.y, au[j]);
-            au[j] = fmaf(u2, xv.z, au[j]); au[j] = fmaf(u3, xv.w, au[j]);
+            for (int u = 0; u < V; ++u) xs[j * a.H + v * V + u] = Act<TA>::to_f(qe[u]);
           }
         }
       }
     }
-#pragma unroll
-    for (int j = 0; j < kNT; ++j) {
-      red[w][j][0][lane] = ag[j] * sg;
-      red[w][j][1][lane] = au[j] * su;
+    if (tg == 0) {
+      if (!tile_ready(&bar, a.pl.status)) return;
+      TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrData);
+    } else {
+      __syncthreads();
     }
+    float acc[kNT];
+#pragma unroll
+    for (int j = 0; j < kNT; ++j) acc[j] = 0.f;
+    for (int blk = 0; blk < cpw / 8; ++blk) {  // 8 chunks = one 128-column scale block
+      float bacc[kNT];
+#pragma unroll
+      for (int j = 0; j < kNT; ++j) bacc[j] = 0.f;
+#pragma unroll 4
+      for (int i = 0; i < 8; ++i) {
+        const int kc = blk * 8 + i;
+        const uint4 v = *reinterpret_cast<const uint4 *>(wl + kc * 512);
+#pragma unroll
+        for (int j = 0; j < kNT; ++j)
+          if (j < nt) bacc[j] += dot_chunk(v, xs + j * a.H + (kc0 + kc) * 16);
+      }
+      const float sc = sl[(kc0 + blk * 8) / 8];
+#pragma unroll
+      for (int j = 0; j < kNT; ++j) acc[j] = fmaf(bacc[j], sc, acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < kNT; ++j) red[w][j][lane] = acc[j];
     if (shared_expert && rg == 0) {
-      // partial shared-gate logit over this CTA's 512 columns (moe.py:81-83)
+      // shared-gate logit (moe.py:81-83): this warp's quarter of the columns
       for (int j = 0; j < nt; ++j) {
         float s = 0.f;
-        for (int c = lane; c < 128; c += 32)
-          s = fmaf(xs[j][w * 128 + c], Act<TA>::to_f(a.sh_gate_w[c0 + c]), s);
+        for (int c = kc0 * 16 + lane; c < (kc0 + cpw) * 16; c += 32)
+          s = fmaf(xs[j * a.H + c], Act<TA>::to_f(__ldg(a.sh_gate_w + c)), s);
         s = warp_sum(s);
         if (lane == 0) gred[w][j] = s;
       }
     }
     __syncthreads();
-    for (int i = tid; i < nt * 64; i += kK2Threads) {
-      const int j = i >> 6, mat = (i >> 5) & 1, r = i & 31;
-      float s = 0.f;
+    if (tid < nt * kRows) {
+      const int j = tid / kRows, r = tid % kRows;
+      float g = 0.f, u = 0.f;
 #pragma unroll
-      for (int ww = 0; ww < kK2Warps; ++ww) s += red[ww][j][mat][r];
-      part[(((int64_t)kq * nslots + slot0 + tg + j) * 2 + mat) * I + rg * 32 + r] = s;
+      for (int ww = 0; ww < kK2Warps; ++ww) {
+        g += red[ww][j][r];
+        u += red[ww][j][kRows + r];
+      }
+      float *hout = shared_expert ? a.sh_h : a.h;
+      hout[(int64_t)(slot0 + tg + j) * I + rg * kRows + r] = silu(g) * u;
     }
     if (shared_expert && rg == 0 && tid < nt) {
       float s = 0.f;
 #pragma unroll
       for (int ww = 0; ww < kK2Warps; ++ww) s += gred[ww][tid];
-      a.shg_part[(int64_t)kq * a.T + tg + tid] = s;
-    }
-  }
-  // the last of the KQ column-quarter CTAs of (expert, row group) finishes
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    int *cnt = a.k2_cnt + aidx * kMaxRG + rg;
-    const int prev = atomicAdd(cnt, 1);
-    s_last = (prev == a.KQ - 1);
-    if (s_last) *cnt = 0;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  float *hout = shared_expert ? a.sh_h : a.h;
-  for (int i = tid; i < n * 32; i += kK2Threads) {
-    const int j = i >> 5, r = i & 31;
-    float g = 0.f, u = 0.f;
-    for (int q = 0; q < a.KQ; ++q) {
-      g += ld_cg(part + (((int64_t)q * nslots + slot0 + j) * 2 + 0) * I + rg * 32 + r);
-      u += ld_cg(part + (((int64_t)q * nslots + slot0 + j) * 2 + 1) * I + rg * 32 + r);
-    }
-    hout[(int64_t)(slot0 + j) * I + rg * 32 + r] = silu(g) * u;
-  }
-  if (shared_expert && rg == 0) {
-    for (int t = tid; t < a.T; t += kK2Threads) {
-      float s = 0.f;
-      for (int q = 0; q < a.KQ; ++q) s += ld_cg(a.shg_part + (int64_t)q * a.T + t);
       // F.linear output and torch.sigmoid both produce the act dtype
       const float logit = Act<TA>::round(s);
-      a.sh_w[t] = Act<TA>::round(1.0f / (1.0f + __expf(-logit)));
+      a.sh_w[tg + tid] = Act<TA>::round(1.0f / (1.0f + __expf(-logit)));
     }
   }
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrExit);
 }
 
-// ===================================================================== K3 ====
+// Tensor-core K2 for 16-bit activations.  Each warp owns a quarter of the
+// hidden dimension and waits only for its own quarter of the 32*H-byte tile
+// (four TMA copies), so math starts while the rest of the tile streams in.
+// Per 16-column chunk a warp issues one ldmatrix.x4 (gate rows 0-15, up rows
+// 0-15), eight e4m3->f16x2 conversions and two m16n8k16 MMAs (N = up to 8
+// tokens); block scales are applied per 8 chunks (128 columns).
+template <typename TA, int kNT>
+__global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t k2_smem[];
+  const int tile_bytes = 32 * a.H;
+  const int quarter = tile_bytes / kK2Warps;
+  const int xstride = a.H + 8;  // f16 per staged token row (+16 bytes: no bank conflicts)
+  uint8_t *wtile = k2_smem;
+  // x rows land here as TA and are converted in place to f16; after the MMAs
+  // the same bytes hold the cross-warp partial sums (keeps 3 CTAs per SM)
+  __half *xs = reinterpret_cast<__half *>(k2_smem + tile_bytes);                 // [kNT][xstride]
+  const TA *xraw = reinterpret_cast<const TA *>(xs);
+  float *ssc = reinterpret_cast<float *>(k2_smem + tile_bytes + max(kNT * xstride * 2, 4096));  // [2][H/128]
+  float(*red)[2][kRows][8] = reinterpret_cast<float(*)[2][kRows][8]>(xs);        // [kK2Warps] (4 KB)
+  __shared__ float xmax[kK2Warps][kNT], s_gl[kK2Warps][kNT];
+  __shared__ int s_shift[kNT];
+  __shared__ __align__(8) uint64_t bar[kK2Warps];
+  __shared__ __align__(8) uint64_t xbar;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrEnter);
+  if (tid == 0) {
+    for (int q = 0; q < kK2Warps; ++q) mbar_init(&bar[q], 1);
+    mbar_init(&xbar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();  // the routing plan and x come from earlier kernels
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrWaited);
+  int b = blockIdx.x;
+  bool shared_expert;
+  int rg, n, slot0, I;
+  const uint8_t *wbase;
+  const float *sbase;
+  if (b < a.routed_ctas) {
+    shared_expert = false;
+    const int aidx = b / a.RG;
+    rg = b % a.RG;
+    const int n_active = ld_cg(a.pl.meta + kMetaNActive);
+    const int4 rec = ld_cg4(a.pl.act_rec + aidx);  // issued together with n_active
+    if (aidx >= n_active) return;
+    n = rec.y;
+    slot0 = rec.z;
+    I = a.I;
+    wbase = a.w13 + (int64_t)rec.x * 2 * a.I * a.H;
+    sbase = a.s13 + (int64_t)rec.x * 2 * (a.I / 128) * (a.H / 128);
+  } else {
+    shared_expert = true;
+    rg = b - a.routed_ctas;
+    n = a.T;
+    slot0 = 0;
+    I = a.Is;
+    wbase = a.sh_w13;
+    sbase = a.sh_s13;
+  }
+  if (tid == 0) {
+    const uint8_t *src = wbase + (int64_t)rg * tile_bytes;
+    for (int q = 0; q < kK2Warps; ++q) {
+      mbar_arrive_expect_tx(&bar[q], quarter);
+      tma_bulk_g2s(wtile + q * quarter, src + q * quarter, quarter, &bar[q]);
+    }
+  }
+  pdl_trigger();
+  const int HB = a.H / 128, KC = a.H / 16;
+  const int ib = (rg * kRows) / 128;
+  for (int i = tid; i < 2 * HB; i += kK2Threads) ssc[i] = __ldg(sbase + ib * 2 * HB + i);
+  const int cpw = KC / kK2Warps;  // chunks per warp
+  const int kc0 = w * cpw;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t wsm = smem_u32(wtile) + kc0 * 512 + lane * 16;
+  const bool gate_logit = shared_expert && rg == 0;
+  bool first = true;
+
+  for (int tg = 0, grp = 0; tg < n; tg += kNT, ++grp) {
+    const int nt = min(kNT, n - tg);
+    if (tg) __syncthreads();  // everyone is done with the previous group's x
+    if (tid == 0) {
+      fence_proxy_async();
+      const uint32_t rowb = (uint32_t)a.H * sizeof(TA);
+      mbar_arrive_expect_tx(&xbar, nt * rowb);
+      for (int j = 0; j < nt; ++j) {
+        const int tok = (shared_expert || a.T == 1) ? tg + j : ld_cg(a.pl.slot_token + slot0 + tg + j);
+        tma_bulk_g2s(xs + (size_t)j * xstride, a.x + (int64_t)tok * a.H, rowb, &xbar);
+      }
+    }
+    if (!tile_ready(&xbar, a.pl.status, grp & 1)) {
+      if (tid == 0)
+        for (int q = 0; q < kK2Warps; ++q) mbar_wait_bounded(&bar[q], 0);
+      return;
+    }
+    // per-token max |x| -> exact power-of-2 shift; optional shared-gate logit (fp32)
+    for (int j = 0; j < nt; ++j) {
+      float m = 0.f, gl = 0.f;
+      const int c_lo = w * (a.H / kK2Warps), c_hi = c_lo + a.H / kK2Warps;
+      for (int c = c_lo + lane; c < c_hi; c += 32) {
+        const float v = Act<TA>::to_f(xraw[(size_t)j * xstride + c]);
+        m = fmaxf(m, fabsf(v));
+        if (gate_logit) gl = fmaf(v, Act<TA>::to_f(__ldg(a.sh_gate_w + c)), gl);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (gate_logit) gl = warp_sum(gl);
+      if (lane == 0) {
+        xmax[w][j] = m;
+        s_gl[w][j] = gl;
+      }
+    }
+    __syncthreads();
+    if (tid < nt) {
+      float m = 0.f, gl = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kK2Warps; ++ww) {
+        m = fmaxf(m, xmax[ww][tid]);
+        gl += s_gl[ww][tid];
+      }
+      s_shift[tid] = f16_shift(m);
+      if (gate_logit) {
+        // F.linear output and torch.sigmoid both produce the act dtype (moe.py:81-83)
+        const float logit = Act<TA>::round(gl);
+        a.sh_w[tg + tid] = Act<TA>::round(1.0f / (1.0f + __expf(-logit)));
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < nt * (a.H / 2); i += kK2Threads) {  // in place: each pair read then written by one thread
+      const int j = i / (a.H / 2), c = (i % (a.H / 2)) * 2;
+      const float sc = ldexpf(1.0f, -s_shift[j]);
+      const __half2 hv = __floats2half2_rn(Act<TA>::to_f(xraw[(size_t)j * xstride + c]) * sc,
+                                           Act<TA>::to_f(xraw[(size_t)j * xstride + c + 1]) * sc);
+      *reinterpret_cast<__half2 *>(xs + (size_t)j * xstride + c) = hv;
+    }
+    __syncthreads();
+    if (first) {  // this warp's quarter of the weight tile
+      first = false;
+      const bool ok = mbar_wait_bounded(&bar[w], 0);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+          atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
+          for (int q = 0; q < kK2Warps; ++q) mbar_wait_bounded(&bar[q], 0);
+        }
+        return;
+      }
+      TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrData);
+    }
+    const __half *xrow = xs + (size_t)min(g, nt - 1) * xstride + 4 * t;  // B column n = g
+    float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int blk = 0; blk < cpw / 8; ++blk) {
+      float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int kc = blk * 8 + i;
+        uint32_t r0, r1, r2, r3, a0, a1, a2, a3;
+        ldsm_x4(wsm + kc * 512, r0, r1, r2, r3);
+        const uint2 bx = *reinterpret_cast<const uint2 *>(xrow + (kc0 + kc) * 16);
+        e4m3x4_to_f16x2x2(r0, a0, a2);
+        e4m3x4_to_f16x2x2(r1, a1, a3);
+        mma_16816(dg, a0, a1, a2, a3, bx.x, bx.y);
+        e4m3x4_to_f16x2x2(r2, a0, a2);
+        e4m3x4_to_f16x2x2(r3, a1, a3);
+        mma_16816(du, a0, a1, a2, a3, bx.x, bx.y);
+      }
+      const int cb = (kc0 + blk * 8) / 8;
+      const float sg = ssc[cb], su = ssc[HB + cb];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        accg[q] = fmaf(dg[q], sg, accg[q]);
+        accu[q] = fmaf(du[q], su, accu[q]);
+      }
+    }
+    // D fragment: (row g, tokens 2t, 2t+1), (row g+8, tokens 2t, 2t+1); the
+    // partial sums reuse the x staging bytes once every warp is past its MMAs
+    __syncthreads();
+    red[w][0][g][2 * t] = accg[0];
+    red[w][0][g][2 * t + 1] = accg[1];
+    red[w][0][g + 8][2 * t] = accg[2];
+    red[w][0][g + 8][2 * t + 1] = accg[3];
+    red[w][1][g][2 * t] = accu[0];
+    red[w][1][g][2 * t + 1] = accu[1];
+    red[w][1][g + 8][2 * t] = accu[2];
+    red[w][1][g + 8][2 * t + 1] = accu[3];
+    __syncthreads();
+    if (tid < nt * kRows) {
+      const int j = tid / kRows, r = tid % kRows;
+      float gs = 0.f, us = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kK2Warps; ++ww) {
+        gs += red[ww][0][r][j];
+        us += red[ww][1][r][j];
+      }
+      const float back = ldexpf(1.0f, s_shift[j]);
+      float *hout = shared_expert ? a.sh_h : a.h;
+      hout[(int64_t)(slot0 + tg + j) * I + rg * kRows + r] = silu(gs * back) * (us * back);
+    }
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrExit);
+}
+
+// =================================================================== K3 ====
 template <typename TA> struct DownArgs {
   const TA *topk_w;
   const uint8_t *w2;
@@ -231,9 +453,10 @@ template <typename TA> struct DownArgs {
   float *ypart;  // [P + T][H]
   int *k3_cnt;
   int T, H, I, Is, E, k, P, RGo;
-  int routed_ctas;  // max(max_active,1) * RGo
+  int routed_ctas;  // max_active * RGo
   int has_shared;
   int combine_in_kernel;
+  int tile_bytes;   // kRows * max(I, Is): shared-memory offset of the h staging area
 };
 
 // out[t, n] for rows [n0, n0 + nrows) and tokens [t0, t1): k-order weighted sum,
@@ -241,118 +464,152 @@ template <typename TA> struct DownArgs {
 template <typename TA>
 __device__ __forceinline__ void combine_rows(const DownArgs<TA> &a, int t0, int t1, int n0, int nrows,
                                              int tid, int nthreads) {
+  constexpr int kMaxK = 16;  // ranks whose loads are issued together
   for (int i = tid; i < (t1 - t0) * nrows; i += nthreads) {
     const int t = t0 + i / nrows, nn = n0 + i % nrows;
+    int slot[kMaxK];
+    float wk[kMaxK], yv[kMaxK];
+#pragma unroll
+    for (int kk = 0; kk < kMaxK; ++kk) {
+      slot[kk] = -1;
+      wk[kk] = 0.f;
+      if (kk < a.k) {
+        slot[kk] = ld_cg(a.pl.pair_slot + (int64_t)t * a.k + kk);
+        wk[kk] = Act<TA>::to_f(Act<TA>::ld_cg(a.topk_w + (int64_t)t * a.k + kk));
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < kMaxK; ++kk)
+      yv[kk] = slot[kk] >= 0 ? ld_cg(a.ypart + (int64_t)slot[kk] * a.H + nn) : 0.f;
     float y = 0.f;
-    for (int kk = 0; kk < a.k; ++kk) {
-      const int slot = a.pl.pair_slot[(int64_t)t * a.k + kk];
-      if (slot >= 0)
-        y = fmaf(Act<TA>::to_f(a.topk_w[(int64_t)t * a.k + kk]), ld_cg(a.ypart + (int64_t)slot * a.H + nn), y);
+#pragma unroll
+    for (int kk = 0; kk < kMaxK; ++kk) y = fmaf(wk[kk], yv[kk], y);
+    for (int kk = kMaxK; kk < a.k; ++kk) {
+      const int s = ld_cg(a.pl.pair_slot + (int64_t)t * a.k + kk);
+      if (s >= 0)
+        y = fmaf(Act<TA>::to_f(Act<TA>::ld_cg(a.topk_w + (int64_t)t * a.k + kk)),
+                 ld_cg(a.ypart + (int64_t)s * a.H + nn), y);
     }
     if (a.has_shared) y = fmaf(ld_cg(a.sh_w + t), ld_cg(a.ypart + (int64_t)(a.P + t) * a.H + nn), y);
-    if (a.residual) y += Act<TA>::to_f(a.residual[(int64_t)t * a.H + nn]);
+    if (a.residual) y += Act<TA>::to_f(Act<TA>::ld_cg(a.residual + (int64_t)t * a.H + nn));
     a.out[(int64_t)t * a.H + nn] = Act<TA>::from_f(y);
+  }
+}
+
+// One expert's 16 down rows against up to kNT tokens' h, K split in 8 slices
+// (4 warps x 2 half-warps).  Lane: row = lane & 15, slice = 2 * warp + lane / 16.
+template <int kNT>
+__device__ __forceinline__ void down_rows_slices(const uint8_t *wtile, const float *hs, const float *srow,
+                                                 int K, int nt, int w, int lane, float (&acc)[kNT]) {
+  const int KC2 = K / 16;
+  const int cps = KC2 / 8;                        // chunks per slice (K % 128 == 0)
+  const int slice = w * 2 + (lane >> 4);
+  const int kc0 = slice * cps;
+  const uint8_t *wl = wtile + kc0 * 256 + (lane & 15) * 16;
+#pragma unroll
+  for (int j = 0; j < kNT; ++j) acc[j] = 0.f;
+#pragma unroll 2
+  for (int i = 0; i < cps; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(wl + i * 256);
+    const float sc = __ldg(srow + (kc0 + i) / 8);
+#pragma unroll
+    for (int j = 0; j < kNT; ++j)
+      if (j < nt) acc[j] = fmaf(dot_chunk(v, hs + j * K + (kc0 + i) * 16), sc, acc[j]);
   }
 }
 
 template <typename TA, int kNT>
 __global__ void __launch_bounds__(kK3Threads) k3_down(DownArgs<TA> a) {
-  extern __shared__ __align__(16) float hs[];  // [kNT][K]
-  __shared__ float red[2][kNT][32];
+  extern __shared__ __align__(128) uint8_t k3_smem[];
+  uint8_t *wtile = k3_smem;                                         // [K/16 chunks][16 rows][16 B]
+  float *hs = reinterpret_cast<float *>(k3_smem + a.tile_bytes);    // [kNT][K]
+  __shared__ float red[8][kNT][kRows];
+  __shared__ __align__(8) uint64_t bar;   // weight tile
+  __shared__ __align__(8) uint64_t hbar;  // h rows of the current token group (one phase per group)
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_init(&hbar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  // The routing plan was written by the router, which completed before any K2
+  // CTA passed its own griddepcontrol.wait, i.e. before this grid could start:
+  // it may be read (through L2) ahead of this kernel's wait on K2.
   int b = blockIdx.x;
-  const int n_active = a.pl.meta[kMetaNActive];
+  const int n_active = ld_cg(a.pl.meta + kMetaNActive);
   bool shared_expert, idle = false;
-  int rgo, n, slot0, K;
-  const uint8_t *wbase;
-  const float *sbase;
-  const float *hsrc;
+  int rgo, n = 0, slot0 = 0, K;
+  const uint8_t *wbase = nullptr;
+  const float *sbase = nullptr;
+  const float *hsrc = nullptr;
   if (b < a.routed_ctas) {
     shared_expert = false;
     const int aidx = b / a.RGo;
     rgo = b % a.RGo;
+    K = a.I;
     if (aidx >= max(n_active, 1)) return;
     if (n_active == 0) {
-      idle = true;  // no routed pair: still count this CTA so the combine runs
-      n = 0; slot0 = 0; K = a.I; wbase = nullptr; sbase = nullptr; hsrc = nullptr;
+      idle = true;  // no routed pair: still counted so that the combine runs
     } else {
-      const int e = a.pl.act_list[aidx];
-      n = a.pl.counts[e];
-      slot0 = a.pl.offsets[e];
-      K = a.I;
-      wbase = a.w2 + (int64_t)e * a.H * a.I;
-      sbase = a.s2 + (int64_t)e * (a.H / 128) * (a.I / 128);
+      const int4 rec = ld_cg4(a.pl.act_rec + aidx);
+      n = rec.y;
+      slot0 = rec.z;
+      wbase = a.w2 + (int64_t)rec.x * a.H * a.I;
+      sbase = a.s2 + (int64_t)rec.x * (a.H / 128) * (a.I / 128);
       hsrc = a.h;
     }
   } else {
     shared_expert = true;
     rgo = b - a.routed_ctas;
     n = a.T;
-    slot0 = 0;
     K = a.Is;
     wbase = a.sh_w2;
     sbase = a.sh_s2;
     hsrc = a.sh_h;
   }
+  const int tile = kRows * K;
+  if (!idle && tid == 0) {
+    mbar_arrive_expect_tx(&bar, tile);
+    tma_bulk_g2s(wtile, wbase + (int64_t)rgo * tile, tile, &bar);
+  }
+  pdl_trigger();
+  pdl_wait();  // K2 (h) has completed
   if (!idle) {
-    const int KC2 = K / 16, KB = K / 128;
-    const int half = KC2 / 2;          // chunks per warp (K % 256 == 0: whole scale blocks)
-    const int kc0 = w * half;
-    const uint8_t *p = wbase + ((int64_t)rgo * KC2 + kc0) * 512 + lane * 16;
-    const float *srow = sbase + (int64_t)((rgo * 32) / 128) * KB;
+    const float *srow = sbase + (int64_t)((rgo * kRows) / 128) * (K / 128);
     const int ypbase = shared_expert ? a.P : 0;
-    for (int tg = 0; tg < n; tg += kNT) {
+    for (int tg = 0, grp = 0; tg < n; tg += kNT, ++grp) {
       const int nt = min(kNT, n - tg);
-      __syncthreads();
-      for (int i = tid; i < nt * K; i += kK3Threads) {
-        const int j = i / K, c = i % K;
-        hs[j * K + c] = ld_cg(hsrc + (int64_t)(slot0 + tg + j) * K + c);
+      if (tg) __syncthreads();  // every thread is done with the previous group's h
+      if (tid == 0) {
+        // h rows of consecutive slots are contiguous: one bulk copy per group
+        fence_proxy_async();
+        const uint32_t bytes = (uint32_t)nt * K * sizeof(float);
+        mbar_arrive_expect_tx(&hbar, bytes);
+        tma_bulk_g2s(hs, hsrc + (int64_t)(slot0 + tg) * K, bytes, &hbar);
       }
-      __syncthreads();
+      if (tg == 0 && !tile_ready(&bar, a.pl.status)) {
+        if (tid == 0) mbar_wait_bounded(&hbar, 0);
+        return;
+      }
+      if (!tile_ready(&hbar, a.pl.status, grp & 1)) return;
       float acc[kNT];
+      down_rows_slices<kNT>(wtile, hs, srow, K, nt, w, lane, acc);
 #pragma unroll
-      for (int j = 0; j < kNT; ++j) acc[j] = 0.f;
-      // 8 chunks (= one 128-column scale block) per step, next step's loads in flight
-      uint4 cur[8], nxt[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) cur[i] = ldg_stream(p + i * 512);
-      for (int blk = 0; blk < half / 8; ++blk) {
-        const bool more = (blk + 1) < half / 8;
-        if (more) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) nxt[i] = ldg_stream(p + ((blk + 1) * 8 + i) * 512);
-        }
-        float bacc[kNT];
-#pragma unroll
-        for (int j = 0; j < kNT; ++j) bacc[j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float wf[16];
-          decode16(cur[i], wf);
-#pragma unroll
-          for (int j = 0; j < kNT; ++j)
-            if (j < nt) bacc[j] += dot16(wf, &hs[j * K + (kc0 + blk * 8 + i) * 16]);
-        }
-        const float sc = srow[(kc0 + blk * 8) / 8];
-#pragma unroll
-        for (int j = 0; j < kNT; ++j) acc[j] = fmaf(bacc[j], sc, acc[j]);
-        if (more) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kNT; ++j) red[w][j][lane] = acc[j];
+      for (int j = 0; j < kNT; ++j) red[w * 2 + (lane >> 4)][j][lane & 15] = acc[j];
       __syncthreads();
-      for (int i = tid; i < nt * 32; i += kK3Threads) {
-        const int j = i >> 5, r = i & 31;
-        a.ypart[(int64_t)(ypbase + slot0 + tg + j) * a.H + rgo * 32 + r] = red[0][j][r] + red[1][j][r];
+      if (tid < nt * kRows) {
+        const int j = tid / kRows, r = tid % kRows;
+        float s = 0.f;
+#pragma unroll
+        for (int sl = 0; sl < 8; ++sl) s += red[sl][j][r];
+        a.ypart[(int64_t)(ypbase + slot0 + tg + j) * a.H + rgo * kRows + r] = s;
       }
     }
   }
   if (!a.combine_in_kernel) return;
-  // the last CTA of this row group (all experts) combines the 32 rows
+  // the last CTA of this row group (all experts) combines the 16 rows
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -364,71 +621,302 @@ __global__ void __launch_bounds__(kK3Threads) k3_down(DownArgs<TA> a) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  combine_rows<TA>(a, 0, a.T, rgo * 32, 32, tid, kK3Threads);
+  combine_rows<TA>(a, 0, a.T, rgo * kRows, kRows, tid, kK3Threads);
+}
+
+// One token: a CTA owns 16 output rows and every routed expert (+ the shared
+// one) at once; no partial outputs leave the CTA.
+template <typename TA>
+__global__ void __launch_bounds__(kK3T1Threads) k3_down_t1(DownArgs<TA> a) {
+  extern __shared__ __align__(128) uint8_t k3_smem[];
+  __shared__ float ysm[kK3T1MaxExperts][kRows];
+  __shared__ int4 s_rec[kK3T1MaxExperts];
+  __shared__ int s_slot[32], s_map[32];   // pair -> slot, slot -> active expert
+  __shared__ float s_w[32];
+  __shared__ __align__(8) uint64_t bar;   // weight tiles
+  __shared__ __align__(8) uint64_t hbar;  // h of every slot
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int rgo = blockIdx.x;
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrEnter);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_init(&hbar, 1);
+    mbar_fence_init();
+  }
+  // plan (the router completed before this grid could start, see k3_down)
+  const int n_active = ld_cg(a.pl.meta + kMetaNActive);
+  const int n_exp = n_active + a.has_shared;  // <= kK3T1MaxExperts (host checks the bound)
+  if (tid < n_active) s_rec[tid] = ld_cg4(a.pl.act_rec + tid);
+  if (tid < a.k) {
+    s_slot[tid] = ld_cg(a.pl.pair_slot + tid);
+    s_w[tid] = Act<TA>::to_f(Act<TA>::ld_cg(a.topk_w + tid));
+  }
+  __syncthreads();
+  const int tile_r = kRows * a.I, tile_s = kRows * a.Is;
+  // [routed tiles][shared tile][h of the k slots][shared h]
+  float *hs = reinterpret_cast<float *>(k3_smem + (size_t)n_active * tile_r + tile_s);
+  if (tid < n_active)
+    for (int c = 0; c < s_rec[tid].y; ++c) s_map[s_rec[tid].z + c] = tid;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar, n_active * tile_r + (a.has_shared ? tile_s : 0));
+    for (int e = 0; e < n_active; ++e)
+      tma_bulk_g2s(k3_smem + (size_t)e * tile_r,
+                   a.w2 + (int64_t)s_rec[e].x * a.H * a.I + (int64_t)rgo * tile_r, tile_r, &bar);
+    if (a.has_shared)
+      tma_bulk_g2s(k3_smem + (size_t)n_active * tile_r, a.sh_w2 + (int64_t)rgo * tile_s, tile_s, &bar);
+  }
+  pdl_trigger();
+  pdl_wait();  // K2 (h) has completed
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrWaited);
+  if (tid == 0) {
+    const uint32_t hb = (uint32_t)a.k * a.I * sizeof(float), hsb = (uint32_t)a.Is * sizeof(float);
+    mbar_arrive_expect_tx(&hbar, hb + (a.has_shared ? hsb : 0));
+    tma_bulk_g2s(hs, a.h, hb, &hbar);  // slots 0..k-1 of the single token
+    if (a.has_shared) tma_bulk_g2s(hs + (size_t)a.k * a.I, a.sh_h, hsb, &hbar);
+  }
+  const bool ok = mbar_wait_bounded(&bar, 0) & mbar_wait_bounded(&hbar, 0);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) {
+      atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(&bar, 0);
+      mbar_wait_bounded(&hbar, 0);
+    }
+    return;
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrData);
+  for (int e = w; e < n_exp; e += kK3T1Warps) {
+    const bool sh = e == n_active;
+    const int K = sh ? a.Is : a.I;
+    const uint8_t *wt = k3_smem + (size_t)e * tile_r;  // the shared tile follows the routed ones
+    const float *he = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
+    const float *srow = (sh ? a.sh_s2 : a.s2 + (int64_t)s_rec[e].x * (a.H / 128) * (a.I / 128)) +
+                        (int64_t)((rgo * kRows) / 128) * (K / 128);
+    // lane: row = lane & 15, half of K = lane / 16
+    const int cph = K / 32;  // chunks per half
+    const int kc0 = (lane >> 4) * cph;
+    const uint8_t *wl = wt + kc0 * 256 + (lane & 15) * 16;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < cph; ++i) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(wl + i * 256);
+      acc = fmaf(dot_chunk(v, he + (kc0 + i) * 16), __ldg(srow + (kc0 + i) / 8), acc);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+    if (lane < kRows) ysm[e][lane] = acc;
+  }
+  __syncthreads();
+  if (tid < kRows) {
+    float y = 0.f;
+    for (int kk = 0; kk < a.k; ++kk)
+      if (s_slot[kk] >= 0) y = fmaf(s_w[kk], ysm[s_map[s_slot[kk]]][tid], y);
+    if (a.has_shared) y = fmaf(ld_cg(a.sh_w), ysm[n_active][tid], y);
+    const int nn = rgo * kRows + tid;
+    if (a.residual) y += Act<TA>::to_f(Act<TA>::ld_cg(a.residual + nn));
+    a.out[nn] = Act<TA>::from_f(y);
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrExit);
+}
+
+// Tensor-core one-token K3 for 16-bit activations: warp e multiplies expert
+// e's 16 x I tile by that expert's h (converted to f16 with an exact
+// power-of-2 shift), one ldmatrix.x2 + four conversions + one m16n8k16 MMA
+// per 16-column chunk (only column 0 of N carries the token).
+template <typename TA>
+__global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t k3_smem[];
+  __shared__ float ysm[kK3T1MaxExperts][kRows];
+  __shared__ int4 s_rec[kK3T1MaxExperts];
+  __shared__ int s_slot[32], s_map[32];   // pair -> slot, slot -> active expert
+  __shared__ float s_w[32];
+  __shared__ __align__(8) uint64_t bar;   // weight tiles
+  __shared__ __align__(8) uint64_t hbar;  // h of every slot
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int rgo = blockIdx.x;
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrEnter);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_init(&hbar, 1);
+    mbar_fence_init();
+  }
+  // plan (the router completed before this grid could start, see k3_down)
+  const int n_active = ld_cg(a.pl.meta + kMetaNActive);
+  const int n_exp = n_active + a.has_shared;  // <= kK3T1MaxExperts (host checks the bound)
+  if (tid < n_active) s_rec[tid] = ld_cg4(a.pl.act_rec + tid);
+  if (tid < a.k) {
+    s_slot[tid] = ld_cg(a.pl.pair_slot + tid);
+    s_w[tid] = Act<TA>::to_f(Act<TA>::ld_cg(a.topk_w + tid));
+  }
+  __syncthreads();
+  const int tile_r = kRows * a.I, tile_s = kRows * a.Is;
+  const int Kmax = max(a.I, a.Is), hstride = Kmax + 8;
+  // [routed tiles][shared tile][h fp32: k slots x I, then Is][h f16: one row per expert]
+  float *hs = reinterpret_cast<float *>(k3_smem + (size_t)n_active * tile_r + tile_s);
+  __half *h16 = reinterpret_cast<__half *>(hs + (size_t)a.k * a.I + a.Is);
+  if (tid < n_active)
+    for (int c = 0; c < s_rec[tid].y; ++c) s_map[s_rec[tid].z + c] = tid;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar, n_active * tile_r + (a.has_shared ? tile_s : 0));
+    for (int e = 0; e < n_active; ++e)
+      tma_bulk_g2s(k3_smem + (size_t)e * tile_r,
+                   a.w2 + (int64_t)s_rec[e].x * a.H * a.I + (int64_t)rgo * tile_r, tile_r, &bar);
+    if (a.has_shared)
+      tma_bulk_g2s(k3_smem + (size_t)n_active * tile_r, a.sh_w2 + (int64_t)rgo * tile_s, tile_s, &bar);
+  }
+  pdl_trigger();
+  pdl_wait();  // K2 (h) has completed
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrWaited);
+  if (tid == 0) {
+    const uint32_t hb = (uint32_t)a.k * a.I * sizeof(float), hsb = (uint32_t)a.Is * sizeof(float);
+    mbar_arrive_expect_tx(&hbar, hb + (a.has_shared ? hsb : 0));
+    tma_bulk_g2s(hs, a.h, hb, &hbar);  // slots 0..k-1 of the single token
+    if (a.has_shared) tma_bulk_g2s(hs + (size_t)a.k * a.I, a.sh_h, hsb, &hbar);
+  }
+  const bool hok = mbar_wait_bounded(&hbar, 0);
+  if (__syncthreads_or(!hok)) {
+    if (tid == 0) {
+      atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(&bar, 0);
+      mbar_wait_bounded(&hbar, 0);
+    }
+    return;
+  }
+  const int g = lane >> 2, t = lane & 3;
+  for (int e = w; e < n_exp; e += kK3T1Warps) {
+    const bool sh = e == n_active;
+    const int K = sh ? a.Is : a.I;
+    const float *hf = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
+    __half *hh = h16 + (size_t)e * hstride;
+    // this expert's h -> f16 with an exact power-of-2 shift (warp-local)
+    float m = 0.f;
+    for (int c = lane; c < K; c += 32) m = fmaxf(m, fabsf(hf[c]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int sh_exp = f16_shift(m);
+    const float sc = ldexpf(1.0f, -sh_exp);
+    for (int c = lane * 2; c < K; c += 64)
+      *reinterpret_cast<__half2 *>(hh + c) = __floats2half2_rn(hf[c] * sc, hf[c + 1] * sc);
+    __syncwarp();
+  }
+  const bool ok = mbar_wait_bounded(&bar, 0);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) {
+      atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(&bar, 0);
+    }
+    return;
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrData);
+  for (int e = w; e < n_exp; e += kK3T1Warps) {
+    const bool sh = e == n_active;
+    const int K = sh ? a.Is : a.I;
+    const float *hf = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
+    float m = 0.f;  // recompute the shift (cheap; keeps the conversion loop register-light)
+    for (int c = lane; c < K; c += 32) m = fmaxf(m, fabsf(hf[c]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float back = ldexpf(1.0f, f16_shift(m));
+    const __half *hrow = h16 + (size_t)e * hstride + 4 * t;
+    const uint32_t wsm = smem_u32(k3_smem + (size_t)e * tile_r) + (lane & 15) * 16;
+    const float *srow = (sh ? a.sh_s2 : a.s2 + (int64_t)s_rec[e].x * (a.H / 128) * (a.I / 128)) +
+                        (int64_t)((rgo * kRows) / 128) * (K / 128);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int blk = 0; blk < K / 128; ++blk) {
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};  // two independent MMA chains
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const int kc = blk * 8 + i;
+        uint32_t r0, r1, r2, r3, a0, a1, a2, a3, c0, c1, c2, c3;
+        ldsm_x2(wsm + kc * 256, r0, r1);
+        ldsm_x2(wsm + (kc + 1) * 256, r2, r3);
+        const uint2 bx0 = *reinterpret_cast<const uint2 *>(hrow + kc * 16);
+        const uint2 bx1 = *reinterpret_cast<const uint2 *>(hrow + (kc + 1) * 16);
+        e4m3x4_to_f16x2x2(r0, a0, a2);
+        e4m3x4_to_f16x2x2(r1, a1, a3);
+        e4m3x4_to_f16x2x2(r2, c0, c2);
+        e4m3x4_to_f16x2x2(r3, c1, c3);
+        mma_16816(d0, a0, a1, a2, a3, bx0.x, bx0.y);
+        mma_16816(d1, c0, c1, c2, c3, bx1.x, bx1.y);
+      }
+      const float s = __ldg(srow + blk);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = fmaf(d0[q] + d1[q], s, acc[q]);
+    }
+    // column 0 of D lives in lanes with t == 0: rows g (acc[0]) and g + 8 (acc[2])
+    if (t == 0) {
+      ysm[e][g] = acc[0] * back;
+      ysm[e][g + 8] = acc[2] * back;
+    }
+  }
+  __syncthreads();
+  if (tid < kRows) {
+    float y = 0.f;
+    for (int kk = 0; kk < a.k; ++kk)
+      if (s_slot[kk] >= 0) y = fmaf(s_w[kk], ysm[s_map[s_slot[kk]]][tid], y);
+    if (a.has_shared) y = fmaf(ld_cg(a.sh_w), ysm[n_active][tid], y);
+    const int nn = rgo * kRows + tid;
+    if (a.residual) y += Act<TA>::to_f(Act<TA>::ld_cg(a.residual + nn));
+    a.out[nn] = Act<TA>::from_f(y);
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrExit);
 }
 
 template <typename TA>
 __global__ void __launch_bounds__(256) k3_combine(DownArgs<TA> a) {
-  // grid: (H / 32, ceil(T / 8)); 8 tokens x 32 rows per CTA
-  const int t0 = blockIdx.y * 8, t1 = min(a.T, t0 + 8);
-  combine_rows<TA>(a, t0, t1, blockIdx.x * 32, 32, threadIdx.x, blockDim.x);
+  // grid: (H / 16, ceil(T / 16)); 16 tokens x 16 rows per CTA
+  pdl_wait();
+  const int t0 = blockIdx.y * 16, t1 = min(a.T, t0 + 16);
+  combine_rows<TA>(a, t0, t1, blockIdx.x * kRows, kRows, threadIdx.x, blockDim.x);
 }
 
 // ================================================================= launch ====
 // Tokens per pass over a weight tile: an expert never has more tokens than the call.
-static int tokens_per_pass(int64_t T) { return T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8; }
-
-template <typename TA> int launch_combine(DownArgs<TA> &a, int64_t T, int H, cudaStream_t s);
-
-template <typename TA, int kNT>
-int launch_k3(DownArgs<TA> &a, int grid, int Kmax, cudaStream_t s) {
-  const size_t smem = (size_t)kNT * Kmax * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k3_down<TA, kNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_check(e, "k3 smem attribute");
-  }
-  k3_down<TA, kNT><<<grid, kK3Threads, smem, s>>>(a);
-  TM_LAUNCH_CHECK("k3_down launch");
-  if (!a.combine_in_kernel) return launch_combine<TA>(a, a.T, a.H, s);
-  return TM_OK;
-}
-
-template <typename TA> int launch_combine(DownArgs<TA> &a, int64_t T, int H, cudaStream_t s) {
-  dim3 g(H / 32, (unsigned)((T + 7) / 8));
-  k3_combine<TA><<<g, 256, 0, s>>>(a);
-  TM_LAUNCH_CHECK("k3_combine launch");
-  return TM_OK;
+static int tokens_per_pass(int64_t T, int cap) {
+  const int t = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+  return t < cap ? t : cap;
 }
 
 struct GateUpLaunch {
   const void *x; int64_t T; int H, I, E, k, Is;
   const uint8_t *w13; const float *s13; const uint8_t *sh_w13; const float *sh_s13; const void *sh_gate_w;
   void *ws; const WsLayout *L; cudaStream_t s;
+  template <typename TA, int kNT> int go(GateUpArgs<TA> &a, int grid) {
+    if constexpr (sizeof(TA) == 2) {
+      // tile + x rows (f16, padded; >= the 4 KB reduction area) + block scales
+      const size_t smem = (size_t)32 * H + std::max<size_t>((size_t)kNT * (H + 8) * 2, 4096) +
+                          2 * (H / 128) * sizeof(float);
+      return launch_pdl(k2_gateup_mma<TA, kNT>, dim3(grid), dim3(kK2Threads), smem, s, "k2_gateup launch", a);
+    } else {
+      const size_t smem = (size_t)32 * H + (size_t)kNT * H * sizeof(float) + 2 * (H / 128) * sizeof(float);
+      return launch_pdl(k2_gateup<TA, kNT>, dim3(grid), dim3(kK2Threads), smem, s, "k2_gateup launch", a);
+    }
+  }
   template <typename TA> int run() {
     GateUpArgs<TA> a;
     a.x = (const TA *)x;
     a.w13 = w13; a.s13 = s13; a.sh_w13 = sh_w13; a.sh_s13 = sh_s13; a.sh_gate_w = (const TA *)sh_gate_w;
     a.pl = plan_view(ws, *L);
-    a.k2_cnt = ws_ptr<int>(ws, L->k2_cnt);
-    a.gu_part = ws_ptr<float>(ws, L->gu_part);
-    a.sh_gu_part = ws_ptr<float>(ws, L->sh_gu_part);
-    a.shg_part = ws_ptr<float>(ws, L->shg_part);
     a.sh_w = ws_ptr<float>(ws, L->sh_w);
     a.h = ws_ptr<float>(ws, L->h);
     a.sh_h = ws_ptr<float>(ws, L->sh_h);
     a.T = (int)T; a.H = H; a.I = I; a.Is = sh_w13 ? Is : 0; a.E = E; a.P = (int)T * k;
-    a.KQ = H / 512; a.RG = I / 32; a.RGs = a.Is / 32;
+    a.RG = I / kRows; a.RGs = a.Is / kRows;
     const int max_active = (int)std::min<int64_t>(E, T * k);
-    a.routed_ctas = max_active * a.RG * a.KQ;
-    const int grid = a.routed_ctas + (sh_w13 ? a.RGs * a.KQ : 0);
-    switch (tokens_per_pass(T)) {
-      case 1: k2_gateup<TA, 1><<<grid, kK2Threads, 0, s>>>(a); break;
-      case 2: k2_gateup<TA, 2><<<grid, kK2Threads, 0, s>>>(a); break;
-      case 4: k2_gateup<TA, 4><<<grid, kK2Threads, 0, s>>>(a); break;
-      default: k2_gateup<TA, 8><<<grid, kK2Threads, 0, s>>>(a); break;
+    a.routed_ctas = max_active * a.RG;
+    const int grid = a.routed_ctas + (sh_w13 ? a.RGs : 0);
+    // tokens per pass: up to the MMA's 8 for small calls, 4 beyond (two CTAs per
+    // SM); the fp32 path keeps its x staging (kNT * H fp32) within 64 KB
+    int cap = sizeof(TA) == 2 ? (T <= 8 ? 8 : 4) : 4;
+    if (H > 4096) cap = std::min(cap, 2);
+    if (H > 8192) cap = 1;
+    switch (tokens_per_pass(T, cap)) {
+      case 1: return go<TA, 1>(a, grid);
+      case 2: return go<TA, 2>(a, grid);
+      case 4: return go<TA, 4>(a, grid);
+      default:
+        if constexpr (sizeof(TA) == 2) return go<TA, 8>(a, grid);
+        else return go<TA, 4>(a, grid);
     }
-    TM_LAUNCH_CHECK("k2_gateup launch");
-    return TM_OK;
   }
 };
 
@@ -436,6 +924,14 @@ struct DownLaunch {
   int64_t T; int H, I, E, k, Is;
   const void *topk_w; const uint8_t *w2; const float *s2; const uint8_t *sh_w2; const float *sh_s2;
   const void *residual; void *out; void *ws; const WsLayout *L; cudaStream_t s;
+  template <typename TA, int kNT> int go(DownArgs<TA> &a, int grid) {
+    const int Kmax = std::max(a.I, a.Is);
+    const size_t smem = (size_t)a.tile_bytes + (size_t)kNT * Kmax * sizeof(float);
+    int rc = launch_pdl(k3_down<TA, kNT>, dim3(grid), dim3(kK3Threads), smem, s, "k3_down launch", a);
+    if (rc || a.combine_in_kernel) return rc;
+    dim3 g(H / kRows, (unsigned)((T + 15) / 16));
+    return launch_pdl(k3_combine<TA>, g, dim3(256), 0, s, "k3_combine launch", a);
+  }
   template <typename TA> int run() {
     DownArgs<TA> a;
     a.topk_w = (const TA *)topk_w; a.w2 = w2; a.s2 = s2; a.sh_w2 = sh_w2; a.sh_s2 = sh_s2;
@@ -447,18 +943,30 @@ struct DownLaunch {
     a.ypart = ws_ptr<float>(ws, L->ypart);
     a.k3_cnt = ws_ptr<int>(ws, L->k3_cnt);
     a.T = (int)T; a.H = H; a.I = I; a.Is = sh_w2 ? Is : 0; a.E = E; a.k = k; a.P = (int)T * k;
-    a.RGo = H / 32;
+    a.RGo = H / kRows;
     a.has_shared = sh_w2 ? 1 : 0;
     const int max_active = (int)std::min<int64_t>(E, T * k);
-    a.routed_ctas = max_active * a.RGo;
     a.combine_in_kernel = T <= kCombineInKernelMaxT ? 1 : 0;
+    a.tile_bytes = kRows * std::max(I, a.Is);
+    if (T == 1 && max_active + a.has_shared <= kK3T1MaxExperts && k <= 32) {
+      size_t smem = (size_t)max_active * kRows * I + (size_t)kRows * a.Is + ((size_t)k * I + a.Is) * sizeof(float);
+      if constexpr (sizeof(TA) == 2) {
+        smem += (size_t)(max_active + a.has_shared) * (std::max(I, a.Is) + 8) * 2;
+        if (smem <= 200 * 1024)
+          return launch_pdl(k3_down_t1_mma<TA>, dim3(a.RGo), dim3(kK3T1Threads), smem, s,
+                            "k3_down_t1 launch", a);
+      } else {
+        if (smem <= 200 * 1024)
+          return launch_pdl(k3_down_t1<TA>, dim3(a.RGo), dim3(kK3T1Threads), smem, s, "k3_down_t1 launch", a);
+      }
+    }
+    a.routed_ctas = max_active * a.RGo;
     const int grid = a.routed_ctas + (sh_w2 ? a.RGo : 0);
-    const int Kmax = std::max(I, a.Is);
-    switch (tokens_per_pass(T)) {
-      case 1: return launch_k3<TA, 1>(a, grid, Kmax, s);
-      case 2: return launch_k3<TA, 2>(a, grid, Kmax, s);
-      case 4: return launch_k3<TA, 4>(a, grid, Kmax, s);
-      default: return launch_k3<TA, 8>(a, grid, Kmax, s);
+    switch (tokens_per_pass(T, 8)) {
+      case 1: return go<TA, 1>(a, grid);
+      case 2: return go<TA, 2>(a, grid);
+      case 4: return go<TA, 4>(a, grid);
+      default: return go<TA, 8>(a, grid);
     }
   }
 };
@@ -474,9 +982,9 @@ extern "C" int tm_moe_decode_gateup(const void *x, int64_t tokens, int hidden, i
                                     int64_t ws_bytes, void *stream) {
   TM_REQUIRE(x && w13 && s13, "null pointer");
   TM_REQUIRE(hidden % 512 == 0, "hidden (%d) must be a multiple of 512", hidden);
-  TM_REQUIRE(inter % 256 == 0 && inter > 0, "inter (%d) must be a positive multiple of 256", inter);
-  TM_REQUIRE(!sh_w13 || (sh_s13 && sh_gate_w && shared_inter > 0 && shared_inter % 256 == 0),
-             "shared expert needs sh_s13, sh_gate_w and shared_inter %% 256 == 0");
+  TM_REQUIRE(inter % 128 == 0 && inter > 0, "inter (%d) must be a positive multiple of 128", inter);
+  TM_REQUIRE(!sh_w13 || (sh_s13 && sh_gate_w && shared_inter > 0 && shared_inter % 128 == 0),
+             "shared expert needs sh_s13, sh_gate_w and shared_inter %% 128 == 0");
   TM_REQUIRE(aligned(x, 16) && aligned(w13, 16) && (!sh_w13 || aligned(sh_w13, 16)),
              "x and weights must be 16-byte aligned");
   WsLayout L;
@@ -494,9 +1002,9 @@ extern "C" int tm_moe_decode_down_combine(int64_t tokens, int hidden, int inter,
                                           void *out, void *ws, int64_t ws_bytes, void *stream) {
   TM_REQUIRE(topk_w && w2 && s2 && out, "null pointer");
   TM_REQUIRE(hidden % 512 == 0, "hidden (%d) must be a multiple of 512", hidden);
-  TM_REQUIRE(inter % 256 == 0 && inter > 0, "inter (%d) must be a positive multiple of 256", inter);
-  TM_REQUIRE(!sh_w2 || (sh_s2 && shared_inter > 0 && shared_inter % 256 == 0),
-             "shared expert needs sh_s2 and shared_inter %% 256 == 0");
+  TM_REQUIRE(inter % 128 == 0 && inter > 0, "inter (%d) must be a positive multiple of 128", inter);
+  TM_REQUIRE(!sh_w2 || (sh_s2 && shared_inter > 0 && shared_inter % 128 == 0),
+             "shared expert needs sh_s2 and shared_inter %% 128 == 0");
   TM_REQUIRE(aligned(w2, 16) && (!sh_w2 || aligned(sh_w2, 16)), "weights must be 16-byte aligned");
   WsLayout L;
   int rc = ws_check(ws, ws_bytes, tokens, n_experts, top_k, hidden, inter, sh_w2 ? shared_inter : 0, &L);

@@ -5,38 +5,57 @@
 // implicit grouping in MoEExecutor.execute_layer (execution/moe.py:132,164-165):
 // experts ascending (torch.unique), tokens ascending within an expert
 // (torch.where over [T, k] in row-major order).
+//
+// Latency matters more than bandwidth here (one decode layer reads 0.5 MB of
+// router weights): each warp holds its expert row in registers before
+// griddepcontrol.wait (weights do not depend on the previous kernel), the
+// token tile arrives by one TMA bulk copy, and no loop carries a chain of
+// dependent global loads.
+#include <cooperative_groups.h>
+
 #include "tm_common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tmoe {
 
-constexpr int kRouterThreads = 256;  // 8 warps
+constexpr int kRouterThreads = 256;     // 8 warps
+constexpr int kRouterWarps = kRouterThreads / 32;
 constexpr int kMaxExpertsPerLane = 32;  // E <= 1024
+constexpr int kRowVecs = 16;            // 16-byte vectors of a router row a lane keeps in registers
+constexpr int kClusterCTAs = 8;         // decode router: one thread-block cluster
+constexpr int kClusterMaxE = kClusterCTAs * kRouterWarps * 2;  // 2 expert rows per warp
+constexpr int kClusterMaxT = 8;
 
 struct PlanPtrs {
   uint32_t *status;
+  uint32_t *trace;  // trace builds only
   int *meta;
   int *counts;    // [E]
   int *offsets;   // [E+1]
   int *act_list;  // [E]
+  int4 *act_rec;  // [E]
   int *slot_token, *slot_pair, *pair_slot;  // [P]
-  int *k2_cnt;    // [(E+1)*rg_max]
-  int *k3_cnt;    // [H/32]
+  int *k2_cnt;    // [(E+1)*kMaxRG]
+  int *k3_cnt;    // [kMaxRGo]
   int k2_cnt_n, k3_cnt_n;
 };
 
 static PlanPtrs plan_ptrs(void *ws, const WsLayout &L) {
   PlanPtrs p;
   p.status = ws_ptr<uint32_t>(ws, L.status);
+  p.trace = kTraceBytes ? ws_ptr<uint32_t>(ws, L.trace) : nullptr;
   p.meta = ws_ptr<int>(ws, L.meta);
   p.counts = ws_ptr<int>(ws, L.counts);
   p.offsets = ws_ptr<int>(ws, L.offsets);
   p.act_list = ws_ptr<int>(ws, L.act_list);
+  p.act_rec = ws_ptr<int4>(ws, L.act_rec);
   p.slot_token = ws_ptr<int>(ws, L.slot_token);
   p.slot_pair = ws_ptr<int>(ws, L.slot_pair);
   p.pair_slot = ws_ptr<int>(ws, L.pair_slot);
   p.k2_cnt = ws_ptr<int>(ws, L.k2_cnt);
   p.k3_cnt = ws_ptr<int>(ws, L.k3_cnt);
-  p.k2_cnt_n = (L.n_experts + 1) * kMaxRG;
+  p.k2_cnt_n = 0;  // K2 keeps no counters
   p.k3_cnt_n = kMaxRGo;
   return p;
 }
@@ -79,18 +98,26 @@ __device__ int block_excl_scan(int *a, int n, int *tmp) {
   return total;
 }
 
-// Build the routing plan from idx [T, k] (int64).  Whole block; `sm` needs
-// (nwarps * E + 2 * E + 64) ints of shared memory.
-__device__ void plan_build(const int64_t *__restrict__ idx, int T, int k, int E, const PlanPtrs &pp,
-                           int *sm) {
+// Top-k index of pair p: from shared memory when this CTA selected them, else
+// (written by other CTAs of the grid, or by the caller) from global memory.
+struct IdxSource {
+  const int64_t *g;
+  const int *s;
+  __device__ __forceinline__ int64_t get(int p) const { return s ? (int64_t)s[p] : __ldcg(g + p); }
+};
+
+// Build the routing plan from the [T, k] top-k indices.  Whole block; `sm`
+// needs (nwarps * E + 3 * E + 64) ints of shared memory.
+__device__ void plan_build(IdxSource idx, int T, int k, int E, const PlanPtrs &pp, int *sm) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, nw = blockDim.x >> 5;
   const int P = T * k;
   int *hist = sm;                    // [nw][E]
-  int *cnt = sm + nw * E;            // [E]
-  int *flag = cnt + E;               // [E]
-  int *tmp = flag + E;               // [33]
+  int *cnt = sm + nw * E;            // [E] counts, then offsets
+  int *flag = cnt + E;               // [E] active flag, then active index
+  int *cnt0 = flag + E;              // [E] counts (kept)
+  int *tmp = cnt0 + E;               // [33]
   for (int i = tid; i < nw * E; i += blockDim.x) hist[i] = 0;
-  // the expert kernels' completion counters are zeroed for the next phases
+  // the expert kernels' completion counters are zeroed for this call
   for (int i = tid; i < pp.k2_cnt_n; i += blockDim.x) pp.k2_cnt[i] = 0;
   for (int i = tid; i < pp.k3_cnt_n; i += blockDim.x) pp.k3_cnt[i] = 0;
   __syncthreads();
@@ -99,7 +126,7 @@ __device__ void plan_build(const int64_t *__restrict__ idx, int T, int k, int E,
   for (int base = lo; base < hi; base += 32) {
     const int p = base + lane;
     if (p < hi) {
-      const int64_t e = idx[p];
+      const int64_t e = idx.get(p);
       if (e >= 0 && e < E) atomicAdd(&hist[w * E + (int)e], 1);
       else bad = true;
     }
@@ -115,18 +142,20 @@ __device__ void plan_build(const int64_t *__restrict__ idx, int T, int k, int E,
       run += c;
     }
     cnt[e] = run;
+    cnt0[e] = run;
     flag[e] = run > 0 ? 1 : 0;
     pp.counts[e] = run;
   }
   __syncthreads();
-  for (int e = tid; e < E; e += blockDim.x) pp.offsets[e] = cnt[e];  // scanned below
-  __syncthreads();
   const int total = block_excl_scan(cnt, E, tmp);
   const int n_active = block_excl_scan(flag, E, tmp);
   for (int e = tid; e < E; e += blockDim.x) {
-    const int c = pp.offsets[e];
+    const int c = cnt0[e];
     pp.offsets[e] = cnt[e];
-    if (c > 0) pp.act_list[flag[e]] = e;
+    if (c > 0) {
+      pp.act_list[flag[e]] = e;
+      pp.act_rec[flag[e]] = make_int4(e, c, cnt[e], 0);
+    }
     for (int j = 0; j < nw; ++j) hist[j * E + e] += cnt[e];
   }
   if (tid == 0) {
@@ -142,7 +171,7 @@ __device__ void plan_build(const int64_t *__restrict__ idx, int T, int k, int E,
     const int p = base + lane;
     int e = -1;
     if (p < hi) {
-      const int64_t v = idx[p];
+      const int64_t v = idx.get(p);
       e = (v >= 0 && v < E) ? (int)v : -1;
     }
     const unsigned peers = __match_any_sync(0xffffffffu, e);
@@ -178,83 +207,94 @@ template <typename TA> struct RouterArgs {
   PlanPtrs pp;
 };
 
-// Dot products of router rows with the staged tokens.  Lane covers 16-byte
-// vectors c*32+lane of the row (V act values each).
-template <typename TA>
-__device__ __forceinline__ void router_rows(const RouterArgs<TA> &a, const float *xs, int t0, int nt,
-                                            int e_begin, int e_end) {
-  constexpr int V = 16 / sizeof(TA);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int nvec = a.H / V;  // 16-byte vectors per row
-  for (int e = e_begin + w; e < e_end; e += kRouterThreads / 32) {
-    const uint4 *row = reinterpret_cast<const uint4 *>(a.w + (int64_t)e * a.H);
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-    for (int v = lane; v < nvec; v += 32) {
-      const uint4 q = __ldg(row + v);
-      const TA *qe = reinterpret_cast<const TA *>(&q);
-      float wf[V];
-#pragma unroll
-      for (int i = 0; i < V; ++i) wf[i] = Act<TA>::to_f(qe[i]);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (j < nt) {
-          const float *xr = xs + (int64_t)j * a.H + v * V;
-#pragma unroll
-          for (int i = 0; i < V; ++i) acc[j] = fmaf(wf[i], xr[i], acc[j]);
-        }
-      }
+// Routing plan of a call with at most 32 (token, rank) pairs: one warp,
+// registers and a few shared words, no block-wide barrier.  Same result as
+// plan_build.  The caller's other warps zero the expert kernels' counters.
+__device__ void plan_small_warp(IdxSource idx, int T, int k, int E, const PlanPtrs &pp) {
+  __shared__ int s_ae[32], s_ac[32];
+  const int lane = threadIdx.x & 31;
+  const int P = T * k;
+  int e = -1;
+  if (lane < P) {
+    const int64_t v = idx.get(lane);
+    e = (v >= 0 && v < E) ? (int)v : -1;
+  }
+  if (__any_sync(0xffffffffu, lane < P && e < 0) && lane == 0) atomicOr(pp.status, TM_STATUS_BAD_EXPERT_ID);
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const bool leader = e >= 0 && lane == __ffs(peers) - 1;
+  const unsigned leaders = __ballot_sync(0xffffffffu, leader);
+  int less = 0, act = 0;  // valid pairs / distinct experts with a smaller expert id
+  for (int q = 0; q < 32; ++q) {
+    const int eq = __shfl_sync(0xffffffffu, e, q);
+    less += (eq >= 0 && eq < e);
+    act += ((leaders >> q) & 1u) && eq < e;
+  }
+  const int n_active = __popc(leaders);
+  if (lane < P) {
+    if (e >= 0) {
+      const int slot = less + __popc(peers & ((1u << lane) - 1u));
+      pp.slot_pair[slot] = lane;
+      pp.slot_token[slot] = lane / k;
+      pp.pair_slot[lane] = slot;
+    } else {
+      pp.pair_slot[lane] = -1;
     }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (j < nt) {
-        const float s = warp_sum(acc[j]);
-        if (lane == 0) {
-          const float r = Act<TA>::round(s);  // F.linear output in act dtype
-          a.logits_ws[(int64_t)(t0 + j) * a.E + e] = r;
-          if (a.logits_out) a.logits_out[(int64_t)(t0 + j) * a.E + e] = Act<TA>::from_f(r);
-        }
-      }
+  }
+  if (leader) {
+    pp.act_list[act] = e;
+    pp.act_rec[act] = make_int4(e, __popc(peers), less, 0);
+    s_ae[act] = e;
+    s_ac[act] = __popc(peers);
+  }
+  __syncwarp();
+  for (int x = lane; x <= E; x += 32) {
+    int below = 0, cnt = 0;
+    for (int a = 0; a < n_active; ++a) {
+      below += s_ae[a] < x ? s_ac[a] : 0;
+      cnt += s_ae[a] == x ? s_ac[a] : 0;
     }
+    pp.offsets[x] = below;
+    if (x < E) pp.counts[x] = cnt;
+  }
+  if (lane == 0) {
+    pp.meta[kMetaNActive] = n_active;
+    pp.meta[kMetaPairs] = P;
+    pp.meta[kMetaTokens] = T;
   }
 }
 
-// softmax(fp32) + top-k (value desc, lower id first on ties) + renormalise, one warp per token.
-template <typename TA>
-__device__ void router_topk_token(const RouterArgs<TA> &a, int t) {
+// softmax(fp32) + top-k (value desc, lower id first on ties) + renormalise, one
+// warp per token, EPL = experts per lane (compile time: compact code).  Lane r
+// keeps the r-th winner; all lanes write in parallel.
+template <typename TA, int EPL>
+__device__ void router_topk_token(const RouterArgs<TA> &a, int t, int *s_idx) {
   const int lane = threadIdx.x & 31;
   const float *lg = a.logits_ws + (int64_t)t * a.E;
-  const int per = (a.E + 31) / 32;
-  float v[kMaxExpertsPerLane];
+  float v[EPL];
   float m = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+  for (int i = 0; i < EPL; ++i) {
     const int e = i * 32 + lane;
-    v[i] = (i < per && e < a.E) ? ld_cg(lg + e) : -INFINITY;
+    v[i] = e < a.E ? ld_cg(lg + e) : -INFINITY;
     m = fmaxf(m, v[i]);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-    const int e = i * 32 + lane;
-    if (i < per && e < a.E) s += __expf(v[i] - m);
-  }
+  for (int i = 0; i < EPL; ++i)
+    if (i * 32 + lane < a.E) s += __expf(v[i] - m);
   s = warp_sum(s);
   unsigned taken = 0;  // bit i: v[i] already selected
-  float psel[32];
-  int esel[32];
-  float psum = 0.f;
+  float my_p = 0.f, psum = 0.f;
+  int my_e = 0;
   for (int r = 0; r < a.k; ++r) {
-    // lane-local best: largest value, then smallest expert id (smallest i)
     float bv = -INFINITY;
     int be = 0x7fffffff;
 #pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    for (int i = 0; i < EPL; ++i) {
       const int e = i * 32 + lane;
-      if (i < per && e < a.E && !(taken & (1u << i))) {
+      if (e < a.E && !(taken & (1u << i))) {
         if (v[i] > bv || (v[i] == bv && e < be)) { bv = v[i]; be = e; }
       }
     }
@@ -266,38 +306,130 @@ __device__ void router_topk_token(const RouterArgs<TA> &a, int t) {
     }
     if ((be & 31) == lane) taken |= 1u << (be >> 5);
     const float p = __expf(bv - m) / s;  // softmax probability of the winner
-    psel[r] = p;
-    esel[r] = be;
     psum += p;
+    if (lane == r) { my_e = be; my_p = p; }
   }
-  if (lane == 0) {
-    for (int r = 0; r < a.k; ++r) {
-      a.idx_out[(int64_t)t * a.k + r] = esel[r];
-      a.w_out[(int64_t)t * a.k + r] = Act<TA>::from_f(psel[r] / psum);
-    }
+  if (lane < a.k) {
+    a.idx_out[(int64_t)t * a.k + lane] = my_e;
+    a.w_out[(int64_t)t * a.k + lane] = Act<TA>::from_f(my_p / psum);
+    if (s_idx) s_idx[t * a.k + lane] = my_e;
   }
 }
 
 template <typename TA>
+__device__ __forceinline__ void topk_dispatch(const RouterArgs<TA> &a, int t, int *s_idx) {
+  if (a.E <= 128) router_topk_token<TA, 4>(a, t, s_idx);
+  else if (a.E <= 256) router_topk_token<TA, 8>(a, t, s_idx);
+  else if (a.E <= 512) router_topk_token<TA, 16>(a, t, s_idx);
+  else router_topk_token<TA, 32>(a, t, s_idx);
+}
+
+// kTB: most tokens per token tile (1, 2, 4, 8 or 16), so the per-token
+// accumulators stay in registers and no unused unrolled work executes.
+template <typename TA, int kTB>
 __global__ void __launch_bounds__(kRouterThreads) k1_router(RouterArgs<TA> a) {
-  extern __shared__ float xs[];  // [TB][H] fp32, reused by the plan phase
+  extern __shared__ __align__(128) uint8_t r_smem[];  // token tile (act dtype), reused by the plan
+  TA *xs = reinterpret_cast<TA *>(r_smem);
+  __shared__ __align__(8) uint64_t bar;
   __shared__ int s_flag;
+  __shared__ int s_idx[8 * 32];  // top-k of a single-tile call (T * k <= 256), for the plan
+  constexpr int V = 16 / sizeof(TA);
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int et = blockIdx.x, tt = blockIdx.y;
   const int t0 = tt * a.TB;
   const int nt = min(a.TB, a.T - t0);
-  // stage the token tile as fp32
-  for (int i = threadIdx.x; i < nt * a.H; i += blockDim.x) {
-    const int j = i / a.H, c = i % a.H;
-    xs[i] = Act<TA>::to_f(a.x[(int64_t)(t0 + j) * a.H + c]);
+  const int e_begin = et * a.EPW * kRouterWarps;
+  const int e_end = min(a.E, e_begin + a.EPW * kRouterWarps);
+  const int nvec = a.H / V;           // 16-byte vectors per row
+  const int vpl = min(nvec / 32, kRowVecs);  // of them per lane held in registers (nvec % 32 == 0)
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrEnter);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  // this warp's first expert row goes to registers before the dependency wait
+  uint4 row[kRowVecs];
+  const int e_first = e_begin + w;
+  if (e_first < e_end) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.w + (int64_t)e_first * a.H);
+#pragma unroll
+    for (int i = 0; i < kRowVecs; ++i)
+      if (i < vpl) row[i] = ldg_stream(src + i * 32 + lane);
   }
   __syncthreads();
-  const int e_begin = et * a.EPW * (kRouterThreads / 32);
-  const int e_end = min(a.E, e_begin + a.EPW * (kRouterThreads / 32));
-  router_rows<TA>(a, xs, t0, nt, e_begin, e_end);
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrWaited);
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)nt * a.H * sizeof(TA);
+    mbar_arrive_expect_tx(&bar, bytes);
+    tma_bulk_g2s(xs, a.x + (int64_t)t0 * a.H, bytes, &bar);
+  }
+  const bool ok = mbar_wait_bounded(&bar, 0);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) {
+      atomicOr(a.pp.status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(&bar, 0);
+    }
+    return;
+  }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
+  for (int e = e_first; e < e_end; e += kRouterWarps) {
+    const bool regs = e == e_first;
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.w + (int64_t)e * a.H);
+    float acc[kTB];
+#pragma unroll
+    for (int j = 0; j < kTB; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowVecs; ++i) {
+      if (i < vpl) {
+        const int v = i * 32 + lane;
+        const uint4 q = regs ? row[i] : __ldg(src + v);
+        const TA *qe = reinterpret_cast<const TA *>(&q);
+        float wf[V];
+#pragma unroll
+        for (int u = 0; u < V; ++u) wf[u] = Act<TA>::to_f(qe[u]);
+#pragma unroll
+        for (int j = 0; j < kTB; ++j) {
+          if (j < nt) {
+            const uint4 xq = *reinterpret_cast<const uint4 *>(xs + (int64_t)j * a.H + v * V);
+            const TA *xe = reinterpret_cast<const TA *>(&xq);
+#pragma unroll
+            for (int u = 0; u < V; ++u) acc[j] = fmaf(wf[u], Act<TA>::to_f(xe[u]), acc[j]);
+          }
+        }
+      }
+    }
+    // rows longer than kRowVecs vectors per lane: the remainder, loaded in place
+    for (int v = kRowVecs * 32 + lane; v < nvec; v += 32) {
+      const uint4 q = __ldg(src + v);
+      const TA *qe = reinterpret_cast<const TA *>(&q);
+#pragma unroll
+      for (int j = 0; j < kTB; ++j) {
+        if (j < nt) {
+          const uint4 xq = *reinterpret_cast<const uint4 *>(xs + (int64_t)j * a.H + v * V);
+          const TA *xe = reinterpret_cast<const TA *>(&xq);
+          for (int u = 0; u < V; ++u) acc[j] = fmaf(Act<TA>::to_f(qe[u]), Act<TA>::to_f(xe[u]), acc[j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kTB; ++j) {
+      if (j < nt) {
+        const float s = warp_sum(acc[j]);
+        if (lane == 0) {
+          const float r = Act<TA>::round(s);  // F.linear output in act dtype
+          a.logits_ws[(int64_t)(t0 + j) * a.E + e] = r;
+          if (a.logits_out) a.logits_out[(int64_t)(t0 + j) * a.E + e] = Act<TA>::from_f(r);
+        }
+      }
+    }
+  }
   // the last expert tile of this token tile finishes the tokens
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrExit);
+  if (tid == 0) {
     const int prev = atomicAdd(&a.tile_cnt[tt], 1);
     s_flag = (prev == a.n_etiles - 1);
     if (s_flag) a.tile_cnt[tt] = 0;
@@ -305,26 +437,284 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router(RouterArgs<TA> a) {
   __syncthreads();
   if (!s_flag) return;
   __threadfence();
-  for (int j = threadIdx.x >> 5; j < nt; j += kRouterThreads / 32) router_topk_token<TA>(a, t0 + j);
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(&a.tile_cnt[kMaxTokenTiles], 1);
-    s_flag = (prev == a.n_ttiles - 1);
-    if (s_flag) a.tile_cnt[kMaxTokenTiles] = 0;
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 4);  // last CTA: top-k starts
+  const bool single_tile = a.n_ttiles == 1 && a.T * a.k <= 8 * 32;
+  for (int j = w; j < nt; j += kRouterWarps) topk_dispatch<TA>(a, t0 + j, single_tile ? s_idx : nullptr);
+  if (!single_tile) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int prev = atomicAdd(&a.tile_cnt[kMaxTokenTiles], 1);
+      s_flag = (prev == a.n_ttiles - 1);
+      if (s_flag) a.tile_cnt[kMaxTokenTiles] = 0;
+    }
+    __syncthreads();
+    if (!s_flag) return;
+    __threadfence();
+  } else {
+    __syncthreads();  // s_idx complete
   }
-  __syncthreads();
-  if (!s_flag) return;
-  __threadfence();
-  plan_build(a.idx_out, a.T, a.k, a.E, a.pp, reinterpret_cast<int *>(xs));
+  const IdxSource src{a.idx_out, single_tile ? s_idx : nullptr};
+  if (a.T * a.k <= 32) {
+    // decode-sized call: warp 0 plans in registers while the others zero the
+    // expert kernels' counters
+    TM_TRACE_EVENT(a.pp.trace, kTrRouter, 5);  // plan starts
+    if (w == 0) {
+      plan_small_warp(src, a.T, a.k, a.E, a.pp);
+      TM_TRACE_EVENT(a.pp.trace, kTrRouter, 6);  // plan done
+    } else {
+      for (int i = tid - 32; i < a.pp.k2_cnt_n; i += kRouterThreads - 32) a.pp.k2_cnt[i] = 0;
+      for (int i = tid - 32; i < a.pp.k3_cnt_n; i += kRouterThreads - 32) a.pp.k3_cnt[i] = 0;
+    }
+    return;
+  }
+  plan_build(src, a.T, a.k, a.E, a.pp, reinterpret_cast<int *>(r_smem));
 }
 
 __global__ void __launch_bounds__(1024) k1_plan_only(const int64_t *idx, int T, int k, int E, PlanPtrs pp) {
   extern __shared__ int sm[];
-  plan_build(idx, T, k, E, pp, sm);
+  pdl_wait();
+  if (T * k <= 32) {
+    if (threadIdx.x < 32) {
+      plan_small_warp(IdxSource{idx, nullptr}, T, k, E, pp);
+    } else {
+      for (int i = threadIdx.x - 32; i < pp.k2_cnt_n; i += blockDim.x - 32) pp.k2_cnt[i] = 0;
+      for (int i = threadIdx.x - 32; i < pp.k3_cnt_n; i += blockDim.x - 32) pp.k3_cnt[i] = 0;
+    }
+    return;
+  }
+  plan_build(IdxSource{idx, nullptr}, T, k, E, pp, sm);
 }
 
-static size_t plan_smem(int nwarps, int E) { return sizeof(int) * ((size_t)nwarps * E + 2 * E + 64); }
+static size_t plan_smem(int nwarps, int E) { return sizeof(int) * ((size_t)nwarps * E + 3 * E + 64); }
+
+// ------------------------------------------------ decode router (cluster) ----
+// 16-bit logits order like their bit patterns once the sign is folded in, so a
+// (logit, expert) pair packs into one u32 whose maximum is the largest logit
+// with the lowest expert id: one redux.sync per top-k round.
+template <typename TA> struct LogitKey;
+template <> struct LogitKey<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t bits(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+  static __device__ __forceinline__ float value(uint32_t b) { return __bfloat162float(__ushort_as_bfloat16((unsigned short)b)); }
+};
+template <> struct LogitKey<__half> {
+  static __device__ __forceinline__ uint32_t bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
+  static __device__ __forceinline__ float value(uint32_t b) { return __half2float(__ushort_as_half((unsigned short)b)); }
+};
+__device__ __forceinline__ uint32_t order16(uint32_t b) {
+  if (b == 0x8000u) b = 0;  // -0 == +0
+  return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+}
+__device__ __forceinline__ uint32_t unorder16(uint32_t k) { return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu); }
+
+// Top-k of one token from logits in shared memory (one warp); with
+// `plan` (a single-token call) the same warp also writes the routing plan.
+template <typename TA, int EPL>
+__device__ void topk_redux_token(const RouterArgs<TA> &a, const float *lg, int t, int *s_idx, bool plan) {
+  const int lane = threadIdx.x & 31;
+  float v[EPL];
+  uint32_t key[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < a.E ? lg[e] : -INFINITY;
+    key[i] = e < a.E ? (order16(LogitKey<TA>::bits(v[i])) << 16) | (0xFFFFu - e) : 0u;
+  }
+  unsigned taken = 0;
+  float m = 0.f, my_v = 0.f;
+  int my_e = 0;
+  for (int r = 0; r < a.k; ++r) {
+    uint32_t loc = 0;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i)
+      if (!(taken & (1u << i))) loc = max(loc, key[i]);
+    const uint32_t win = __reduce_max_sync(0xffffffffu, loc);
+    const int e = 0xFFFF - (int)(win & 0xFFFFu);
+    if ((e & 31) == lane) taken |= 1u << (e >> 5);
+    const float val = LogitKey<TA>::value(unorder16(win >> 16));
+    if (r == 0) m = val;
+    if (lane == r) { my_e = e; my_v = val; }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i)
+    if (i * 32 + lane < a.E) s += __expf(v[i] - m);
+  s = warp_sum(s);
+  const float p = lane < a.k ? __expf(my_v - m) / s : 0.f;  // softmax probability of rank `lane`
+  const float psum = warp_sum(p);
+  if (lane < a.k) {
+    a.idx_out[(int64_t)t * a.k + lane] = my_e;
+    a.w_out[(int64_t)t * a.k + lane] = Act<TA>::from_f(p / psum);
+    if (s_idx) s_idx[t * a.k + lane] = my_e;
+  }
+  if (!plan) return;
+  // single token: the k distinct experts each get one slot, in ascending id order
+  int asc = 0;
+  for (int q = 0; q < a.k; ++q) asc += __shfl_sync(0xffffffffu, my_e, q) < my_e;
+  const PlanPtrs &pp = a.pp;
+  if (lane < a.k) {
+    pp.slot_pair[asc] = lane;
+    pp.slot_token[asc] = 0;
+    pp.pair_slot[lane] = asc;
+    pp.act_list[asc] = my_e;
+    pp.act_rec[asc] = make_int4(my_e, 1, asc, 0);
+  }
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int x = i * 32 + lane;
+    int below = 0;
+    for (int q = 0; q < a.k; ++q) below += __shfl_sync(0xffffffffu, my_e, q) < x;
+    if (x < a.E) {
+      pp.counts[x] = (taken >> i) & 1u;
+      pp.offsets[x] = below;
+    }
+  }
+  if (lane == 0) {
+    pp.offsets[a.E] = a.k;
+    pp.meta[kMetaNActive] = a.k;
+    pp.meta[kMetaPairs] = a.k;
+    pp.meta[kMetaTokens] = 1;
+  }
+}
+
+// Decode router: one cluster of kClusterCTAs CTAs, two expert rows per warp
+// (held in registers before the dependency wait).  Every CTA writes its
+// logits straight into CTA 0's shared memory; after the cluster barrier CTA 0
+// selects the top-k and writes the plan.  No global atomics or fences.
+template <typename TA, int kTB>
+__global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t r_smem[];  // token tile, then (CTA 0) the plan's scratch
+  TA *xs = reinterpret_cast<TA *>(r_smem);
+  __shared__ float s_logit[kClusterMaxT][kClusterMaxE];
+  __shared__ int s_idx[kClusterMaxT * 32];
+  __shared__ __align__(8) uint64_t bar;
+  constexpr int V = 8;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int nt = a.T;
+  const int nvec = a.H / V, vpl = nvec / 32;  // <= 8 (host checks)
+  const int e0 = crank * (kRouterWarps * 2) + w * 2;
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrEnter);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  uint4 row[2][8];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (e0 + r < a.E) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(a.w + (int64_t)(e0 + r) * a.H);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < vpl) row[r][i] = ldg_stream(src + i * 32 + lane);
+    }
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrWaited);
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)nt * a.H * sizeof(TA);
+    mbar_arrive_expect_tx(&bar, bytes);
+    tma_bulk_g2s(xs, a.x, bytes, &bar);
+  }
+  const bool ok = !__syncthreads_or(!mbar_wait_bounded(&bar, 0));
+  if (!ok && tid == 0) {
+    atomicOr(a.pp.status, TM_STATUS_TIMEOUT);
+    mbar_wait_bounded(&bar, 0);
+  }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
+  float *logit0 = cluster.map_shared_rank(&s_logit[0][0], 0);
+  if (ok) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int e = e0 + r;
+      if (e >= a.E) continue;
+      float acc[kTB];
+#pragma unroll
+      for (int j = 0; j < kTB; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < vpl) {
+          const int vv = i * 32 + lane;
+          const TA *qe = reinterpret_cast<const TA *>(&row[r][i]);
+          float wf[V];
+#pragma unroll
+          for (int u = 0; u < V; ++u) wf[u] = Act<TA>::to_f(qe[u]);
+#pragma unroll
+          for (int j = 0; j < kTB; ++j) {
+            if (j < nt) {
+              const uint4 xq = *reinterpret_cast<const uint4 *>(xs + (int64_t)j * a.H + vv * V);
+              const TA *xe = reinterpret_cast<const TA *>(&xq);
+#pragma unroll
+              for (int u = 0; u < V; ++u) acc[j] = fmaf(wf[u], Act<TA>::to_f(xe[u]), acc[j]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kTB; ++j) {
+        if (j < nt) {
+          const float s = warp_sum(acc[j]);
+          if (lane == 0) {
+            const float rr = Act<TA>::round(s);  // F.linear output in act dtype
+            logit0[j * kClusterMaxE + e] = rr;
+            if (a.logits_out) a.logits_out[(int64_t)j * a.E + e] = Act<TA>::from_f(rr);
+          }
+        }
+      }
+    }
+  }
+  cluster.sync();  // every CTA's logits are in CTA 0
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrExit);
+  if (crank != 0 || !ok) return;
+  if (nt == 1) {
+    if (w == 0) {
+      topk_redux_token<TA, kClusterMaxE / 32>(a, s_logit[0], 0, nullptr, true);
+      TM_TRACE_EVENT(a.pp.trace, kTrRouter, 6);
+    } else {
+      for (int i = tid - 32; i < a.pp.k3_cnt_n; i += kRouterThreads - 32) a.pp.k3_cnt[i] = 0;
+    }
+    return;
+  }
+  if (w < nt) topk_redux_token<TA, kClusterMaxE / 32>(a, s_logit[w], w, s_idx, false);
+  __syncthreads();
+  const IdxSource src{a.idx_out, s_idx};
+  if (nt * a.k <= 32) {
+    if (w == 0) {
+      plan_small_warp(src, nt, a.k, a.E, a.pp);
+    } else {
+      for (int i = tid - 32; i < a.pp.k3_cnt_n; i += kRouterThreads - 32) a.pp.k3_cnt[i] = 0;
+    }
+    return;
+  }
+  plan_build(src, nt, a.k, a.E, a.pp, reinterpret_cast<int *>(r_smem));
+}
+
+template <typename Kern, typename... Args>
+static int launch_cluster_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, int cluster_x, cudaStream_t s,
+                              const char *what, Args... args) {
+  int rc = ensure_smem(reinterpret_cast<const void *>(kernel), smem);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, args...), what);
+}
+
 
 struct RouterLaunch {
   const void *x, *w;
@@ -344,25 +734,42 @@ struct RouterLaunch {
     a.logits_ws = ws_ptr<float>(ws, L->logits);
     a.tile_cnt = ws_ptr<int>(ws, L->router_cnt);
     a.T = T; a.H = H; a.E = E; a.k = k;
+    if constexpr (sizeof(TA) == 2) {
+      // decode-sized call: one thread-block cluster, no global synchronisation
+      if (T <= kClusterMaxT && E <= kClusterMaxE && H / 8 <= 32 * 8 && (H / 8) % 32 == 0 && k <= 32) {
+        a.pp = plan_ptrs(ws, *L);
+        a.TB = T;
+        a.n_ttiles = 1;
+        a.n_etiles = kClusterCTAs;
+        const size_t smem = std::max((size_t)T * H * sizeof(TA), plan_smem(kRouterWarps, E));
+        const dim3 grid(kClusterCTAs), block(kRouterThreads);
+        switch (T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8) {
+          case 1: return launch_cluster_pdl(k1_router_cluster<TA, 1>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
+          case 2: return launch_cluster_pdl(k1_router_cluster<TA, 2>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
+          case 4: return launch_cluster_pdl(k1_router_cluster<TA, 4>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
+          default: return launch_cluster_pdl(k1_router_cluster<TA, 8>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
+        }
+      }
+    }
     if (T <= 8) { a.TB = T; a.EPW = 1; }
     else { a.TB = 16; a.EPW = 4; }
-    // keep the fp32 token tile within 160 KB of shared memory
-    while (a.TB > 1 && (size_t)a.TB * H * 4 > 160 * 1024) a.TB /= 2;
+    // keep the token tile within 96 KB of shared memory
+    while (a.TB > 1 && (size_t)a.TB * H * sizeof(TA) > 96 * 1024) a.TB /= 2;
     a.n_ttiles = (T + a.TB - 1) / a.TB;
-    const int ew = a.EPW * (kRouterThreads / 32);
+    const int ew = a.EPW * kRouterWarps;
     a.n_etiles = (E + ew - 1) / ew;
     if (a.n_ttiles > kMaxTokenTiles)
       return fail(TM_ERR_UNSUPPORTED, "too many tokens for one router call (%d)", T);
     a.pp = plan_ptrs(ws, *L);
-    size_t smem = std::max((size_t)a.TB * H * 4, plan_smem(kRouterThreads / 32, E));
-    if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(k1_router<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return cuda_check(e, "router smem attribute");
+    const size_t smem = std::max((size_t)a.TB * H * sizeof(TA), plan_smem(kRouterWarps, E));
+    const dim3 grid(a.n_etiles, a.n_ttiles), block(kRouterThreads);
+    switch (a.TB <= 1 ? 1 : a.TB <= 2 ? 2 : a.TB <= 4 ? 4 : a.TB <= 8 ? 8 : 16) {
+      case 1: return launch_pdl(k1_router<TA, 1>, grid, block, smem, s, "k1_router launch", a);
+      case 2: return launch_pdl(k1_router<TA, 2>, grid, block, smem, s, "k1_router launch", a);
+      case 4: return launch_pdl(k1_router<TA, 4>, grid, block, smem, s, "k1_router launch", a);
+      case 8: return launch_pdl(k1_router<TA, 8>, grid, block, smem, s, "k1_router launch", a);
+      default: return launch_pdl(k1_router<TA, 16>, grid, block, smem, s, "k1_router launch", a);
     }
-    dim3 grid(a.n_etiles, a.n_ttiles);
-    k1_router<TA><<<grid, kRouterThreads, smem, s>>>(a);
-    TM_LAUNCH_CHECK("k1_router launch");
-    return TM_OK;
   }
 };
 
@@ -398,9 +805,6 @@ extern "C" int tm_route_plan(const int64_t *topk_idx, int64_t tokens, int top_k,
   PlanPtrs pp = plan_ptrs(ws, L);
   const int threads = 1024;
   const size_t smem = plan_smem(threads / 32, n_experts);
-  cudaError_t e = cudaFuncSetAttribute(k1_plan_only, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return cuda_check(e, "plan smem attribute");
-  k1_plan_only<<<1, threads, smem, as_stream(stream)>>>(topk_idx, (int)tokens, top_k, n_experts, pp);
-  TM_LAUNCH_CHECK("k1_plan_only launch");
-  return TM_OK;
+  return launch_pdl(k1_plan_only, dim3(1), dim3(threads), smem, as_stream(stream), "k1_plan_only launch",
+                    topk_idx, (int)tokens, top_k, n_experts, pp);
 }
