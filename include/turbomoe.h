@@ -68,9 +68,11 @@ int tm_dequant_fp8_block(const uint8_t *w, const float *scale_inv, int64_t rows,
  *
  * Per expert (H = hidden, I = intermediate):
  *   w13: gate and up interleaved in 16-byte column chunks,
- *        [I/32][H/16][2 (gate, up)][32 rows][16 bytes]          = 2*I*H bytes
+ *        [I/16][H/16][2 (gate, up)][16 rows][16 bytes]          = 2*I*H bytes
+ *        (a 16-row group over all of H is one contiguous 32*H-byte tile; each
+ *        16x16 chunk is one m16k16 tensor-core A tile)
  *   s13: [I/128][2][H/128] fp32                                  = 2*(I/128)*(H/128)
- *   w2 : down, [H/32][I/16][32 rows][16 bytes]                   = H*I bytes
+ *   w2 : down, [H/16][I/16][16 rows][16 bytes]                   = H*I bytes
  *   s2 : [H/128][I/128] fp32
  * Experts are stacked: expert e starts at e * tm_packed_*(...). */
 int64_t tm_packed_w13_bytes(int hidden, int inter);
@@ -146,8 +148,8 @@ int tm_route_plan(const int64_t *topk_idx, int64_t tokens, int top_k, int n_expe
  * Needs the plan of tm_router_topk / tm_route_plan in `ws`.  Writes
  * h = silu(x G^T) * (x U^T) (fp32) into the workspace.  sh_gate_w: [hidden]
  * act, the shared expert's sigmoid-gate row (mlp.shared_expert_gate.weight);
- * required when sh_w13 != NULL.  hidden % 512 == 0, inter % 256 == 0,
- * shared_inter % 256 == 0. */
+ * required when sh_w13 != NULL.  hidden % 512 == 0, inter % 128 == 0,
+ * shared_inter % 128 == 0. */
 int tm_moe_decode_gateup(const void *x, int64_t tokens, int hidden, int inter,
                          int n_experts, int top_k, int act_dtype, const uint8_t *w13,
                          const float *s13, const uint8_t *sh_w13, const float *sh_s13,

@@ -66,7 +66,6 @@ WsLayout ws_layout(int64_t tokens, int n_experts, int top_k, int hidden, int int
   WsLayout L;
   memset(&L, 0, sizeof(L));
   const int64_t T = tokens, E = n_experts, P = tokens * top_k;
-  const int64_t KQ = hidden / 512 > 0 ? hidden / 512 : 1;
   const int64_t Is = shared_inter;
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
@@ -89,9 +88,6 @@ WsLayout ws_layout(int64_t tokens, int n_experts, int top_k, int hidden, int int
   L.slot_token = take(P * 4);
   L.slot_pair = take(P * 4);
   L.pair_slot = take(P * 4);
-  L.gu_part = take(KQ * P * 2 * inter * 4);
-  L.sh_gu_part = take(KQ * T * 2 * Is * 4);
-  L.shg_part = take(KQ * T * 4);
   L.sh_w = take(T * 4);
   L.h = take(P * inter * 4);
   L.sh_h = take(T * Is * 4);

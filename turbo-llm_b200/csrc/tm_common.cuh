@@ -338,10 +338,7 @@ struct WsLayout {
   int64_t slot_token;  // int32 [P]
   int64_t slot_pair;   // int32 [P]
   int64_t pair_slot;   // int32 [P]
-  int64_t gu_part;     // fp32 [KQ][P][2][I]
-  int64_t sh_gu_part;  // fp32 [KQ][T][2][Is]
-  int64_t shg_part;    // fp32 [KQ][T] shared-gate logit partials
-  int64_t sh_w;        // fp32 [T] sigmoid(shared gate)
+  int64_t sh_w;       // fp32 [T] sigmoid(shared gate)
   int64_t h;           // fp32 [P][I]
   int64_t sh_h;        // fp32 [T][Is]
   int64_t ypart;       // fp32 [P + T][H]
