@@ -169,6 +169,36 @@ int tm_moe_decode_down_combine(int64_t tokens, int hidden, int inter, int n_expe
                                const float *sh_s2, int shared_inter, const void *residual,
                                void *out, void *ws, int64_t ws_bytes, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* One whole decode layer without a caller workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory for a
+ * workspace (a C/FFI host without a device allocator, or a serving process
+ * whose memory pool already owns the free HBM; cudaMalloc would also
+ * synchronise the device).  Runs tm_router_topk, tm_moe_decode_gateup and
+ * tm_moe_decode_down_combine (same arguments and results as those) on a
+ * library-owned static device array of TM_NOALLOC_SCRATCH_BYTES per GPU, held
+ * by every GPU that loads the library until exit, and allocates nothing.
+ *   - Calls whose tm_workspace_bytes(tokens, n_experts, top_k, hidden, inter,
+ *     shared_inter) exceeds TM_NOALLOC_SCRATCH_BYTES are rejected with
+ *     TM_ERR_WORKSPACE (8 MiB covers 64 tokens of Qwen3-30B-A3B and Qwen3.5
+ *     MoE layers).
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - Every call shares the array; each call clears its header first.  Calls
+ *     that overlap on the GPU (other streams or threads on the same device)
+ *     race on it: order them on one stream.
+ *   - status: optional device uint32, receives the TM_STATUS_* bits of this
+ *     call (NULL to skip).  sh_w13 and sh_w2 are both set or both NULL. */
+#define TM_NOALLOC_SCRATCH_BYTES (8ll << 20)
+int tm_moe_decode_layer_noalloc(const void *x, int64_t tokens, int hidden, int inter,
+                                int n_experts, int top_k, int act_dtype, const void *router_w,
+                                const uint8_t *w13, const float *s13, const uint8_t *w2,
+                                const float *s2, const uint8_t *sh_w13, const float *sh_s13,
+                                const uint8_t *sh_w2, const float *sh_s2, int shared_inter,
+                                const void *sh_gate_w, const void *residual, int64_t *topk_idx,
+                                void *topk_w, void *out, uint32_t *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
