@@ -170,6 +170,26 @@ int tm_moe_decode_down_combine(int64_t tokens, int hidden, int inter, int n_expe
                                void *out, void *ws, int64_t ws_bytes, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* K4: prefill (many tokens) as grouped GEMMs on the tcgen05 tensor cores.
+ * Replaces the multi-token branch of MoEExecutor.execute_layer
+ * (execution/moe.py:157-180): per active expert, h = silu(x G^T) * (x U^T),
+ * y = h D^T, out[t] = residual[t] + sum_k topk_w[t,k] * y_{idx[t,k]}[t].
+ * Weights are dequantised on chip to act dtype exactly as
+ * ExpertLoader.dequantize_weight does (loader/expert_loader.py:150-160) and
+ * multiplied with the activations on the tensor cores, fp32 accumulation;
+ * h and y are rounded to act dtype (as the reference's F.linear outputs are).
+ * Needs the routing plan of tm_router_topk / tm_route_plan in `ws`; uses the
+ * workspace's h and partial-output regions.  act_dtype bf16 or fp16;
+ * hidden % 256 == 0, inter % 128 == 0, no shared expert (a shared expert runs
+ * through the decode entry points).  |weight_scale_inv| must stay below 255
+ * (the on-chip dequantisation scales by 2^120 (bf16) / 2^8 (fp16)). */
+int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden, int inter, int n_experts,
+                           int top_k, int act_dtype, const void *topk_w, const uint8_t *w13,
+                           const float *s13, const uint8_t *w2, const float *s2,
+                           const void *residual, void *out, void *ws, int64_t ws_bytes,
+                           void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* One whole decode layer without a caller workspace.  No counterpart in the
  * reference: it exists for callers that cannot allocate device memory for a
  * workspace (a C/FFI host without a device allocator, or a serving process

@@ -267,6 +267,28 @@ def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out:
                                            _stream(out)), "tm_moe_decode_down_combine")
 
 
+# Calls with at least this many tokens (and no shared expert, 16-bit
+# activations) run on the tensor-core grouped GEMMs (tm_moe_prefill_grouped).
+PREFILL_MIN_TOKENS = 256
+
+
+def prefill_eligible(T: int, dtype, packed: PackedExperts, shared) -> bool:
+    return (T >= PREFILL_MIN_TOKENS and shared is None and dtype in (torch.bfloat16, torch.float16)
+            and packed.hidden % 256 == 0)
+
+
+def moe_prefill(x: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Workspace, out: torch.Tensor,
+                residual: torch.Tensor | None = None):
+    """K4: grouped-GEMM expert FFN + combine for the plan already in ``ws``."""
+    T, H = x.shape
+    k = w.shape[1]
+    buf = ws.buf
+    check(lib().tm_moe_prefill_grouped(x.data_ptr(), T, H, packed.inter, packed.n_experts, k, _code(x.dtype),
+                                       w.data_ptr(), packed.w13.data_ptr(), packed.s13.data_ptr(),
+                                       packed.w2.data_ptr(), packed.s2.data_ptr(), _ptr(residual), out.data_ptr(),
+                                       buf.data_ptr(), buf.numel(), _stream(x)), "tm_moe_prefill_grouped")
+
+
 def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Workspace,
                 shared: PackedExperts | None = None, shared_gate_w: torch.Tensor | None = None,
                 residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -285,6 +307,9 @@ def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: Pac
     w = w.contiguous()
     if out is None:
         out = torch.empty_like(x)
+    if prefill_eligible(T, x.dtype, packed, shared):
+        moe_prefill(x, w, packed, ws, out, residual.contiguous() if residual is not None else None)
+        return out
     moe_gateup(x, k, packed, ws, shared, shared_gate_w)
     moe_down_combine(w, packed, ws, out, shared, residual.contiguous() if residual is not None else None)
     return out
