@@ -1,9 +1,11 @@
 """GPU parity of the tensor-core prefill path (tm_moe_prefill_grouped).
 
-The kernels multiply the reference's own dequantised weights (bit-exact
-bf16/fp16, checked by the pack/dequant tests) with the untouched activations
-and accumulate in fp32, rounding h and y to the act dtype as the reference's
-F.linear outputs are.  `emulate` restates exactly that on the CPU, so the
+The kernels multiply dequantised weights with the activations on the tensor
+cores and accumulate in fp32, rounding h and y to the act dtype as the
+reference's F.linear outputs are.  The weights are the reference's own
+dequantisation in the act dtype, except for the gate/up GEMM of bf16 calls,
+which runs on f16 operands (`gateup_weight`; finer rounding than the
+reference's bf16).  `emulate` restates exactly that on the CPU, so the
 kernels must agree with it up to fp32 accumulation order: max-abs <= 1e-2,
 cosine >= 0.99999 and most elements bitwise equal.  Against the reference's
 own golden output (2048-token prefill of a Qwen3-30B-A3B layer) the
@@ -22,6 +24,18 @@ pytestmark = pytest.mark.gpu
 MAXABS, COS = 1e-2, 0.99999
 
 
+def gateup_weight(q, s, dt):
+    """The gate/up GEMM's weights: for fp16 activations the reference's fp16
+    dequantisation; for bf16 activations the GEMM runs on f16 operands with
+    weights round_f16(w * round_f16(scale * 2^8)) / 2^8 (activations enter
+    exactly, shifted by a power of 2)."""
+    if dt != torch.bfloat16:
+        return O.dequantize_weight(q, s, dt).float()
+    sf = (s.float() * 256).to(torch.float16)
+    sf = sf.repeat_interleave(128, 0).repeat_interleave(128, 1)
+    return (q.float().to(torch.float16) * sf).float() / 256
+
+
 def emulate(lw, x, idx, w, residual=None):
     """CPU restatement of the kernels' arithmetic (see module docstring)."""
     dt = x.dtype
@@ -31,8 +45,8 @@ def emulate(lw, x, idx, w, residual=None):
     ypair = torch.zeros(T, k, H)
     for e in torch.unique(idx[(idx >= 0) & (idx < lw.gate.shape[0])]).tolist():
         t, r = torch.where(idx == e)
-        wg = O.dequantize_weight(lw.gate[e], lw.gate_s[e], dt).float()
-        wu = O.dequantize_weight(lw.up[e], lw.up_s[e], dt).float()
+        wg = gateup_weight(lw.gate[e], lw.gate_s[e], dt)
+        wu = gateup_weight(lw.up[e], lw.up_s[e], dt)
         wd = O.dequantize_weight(lw.down[e], lw.down_s[e], dt).float()
         xe = xf[t]
         h = (F.silu(xe @ wg.T) * (xe @ wu.T)).to(dt).float()

@@ -17,99 +17,121 @@
 // dimension ("swap AB"), so an expert's variable token count becomes N rounded
 // up to 16 instead of padding a 128-row M tile.
 //
-// Weights stay FP8 in HBM and are dequantised on chip: a TMA bulk copy brings
-// the raw e4m3 rows of one 64-column K slice into shared memory, eight
-// converter warps turn them into bf16 (fp16) exactly as the reference's
-// dequantize_weight does in that dtype (loader/expert_loader.py:150-160):
-// round(cast(w) * cast(scale)).  The e4m3 byte is placed into the 16-bit
-// pattern (value * 2^-120 for bf16, * 2^-8 for fp16; exact, subnormals
-// included) and one bf16x2/f16x2 multiply by cast(scale) * 2^120 (2^8)
-// applies the scale with a single rounding.  The tensor cores then see the
-// reference's dequantised weights and the untouched activations and
-// accumulate in fp32, as the reference's F.linear does.
+// Where the bytes go.  A tcgen05.mma with both operands in shared memory is
+// limited by shared-memory bandwidth (128 B/cycle/SM) whenever N < 256: it
+// reads (128 + N) x 32 bytes per K=16 step.  So operand A, the dequantised
+// weights, never touches shared memory: eight converter warps load the raw
+// e4m3 rows of each 64-column K slice from global memory (L2-prefetched by a
+// producer warp), dequantise them in registers and write them to tensor memory
+// with tcgen05.st; the MMA reads A from TMEM and only the token rows (B) from
+// shared memory.
 //
-// Warp roles (16 warps): 0 TMA producer, 1 TMEM owner + MMA issuer,
-// 2-3 token-row gather (cp.async), 4-11 converters, 12-15 epilogue.
-// Operand layouts are the UMMA K-major SWIZZLE_NONE canonical layout: 8 rows x
-// 16 bytes core matrices, [k chunk][row / 8][8][16 B].  Accumulators are
-// double-buffered in TMEM (2 x 256 columns) so a tile's epilogue overlaps the
-// next tile's MMAs.  Every wait is bounded; on a timeout the CTA flags the
-// status word, drains its copies and MMAs, frees TMEM and exits.
+// Dequantisation.  f16 operands (gate/up always; down for fp16 activations):
+// the hardware e4m3x2 -> f16x2 conversion (exact) and one f16x2 multiply by
+// f16(scale * 2^kw).  For fp16 activations kw = 0 and this is the reference's
+// fp16 dequantize_weight (loader/expert_loader.py:150-160) bit for bit; for
+// bf16 activations the gate/up GEMM runs on f16 (activations shifted by an
+// exact per-token power of 2, weights by 2^8; both undone in the epilogue).
+// bf16 down projection: bf16 weights exactly as the reference's bf16
+// dequantisation, round(cast(w) * cast(scale)): the e4m3 byte is placed into a
+// bf16 pattern (value * 2^-120, exact) and one bf16x2 multiply by
+// bf16(scale) * 2^120 applies the scale with a single rounding.  The tensor
+// cores accumulate in fp32, as the reference's F.linear does.
+//
+// Warp roles (16 warps): 0 L2 prefetch of the weights, 1 TMEM owner + MMA
+// issuer, 2-3 token-row gather (cp.async into the K-major 128-byte-swizzle
+// layout, several stages in flight), 4-11 converters (warp w: operand
+// (w - 4) / 4, TMEM lane quadrant w % 4), 12-15 epilogue.  TMEM: columns
+// [0, 128) hold the A ring (2 stages x 2 operands x 32 columns), [128, 512)
+// the accumulators: tiles of <= 96 tokens alternate between two 192-column
+// slots (the epilogue of one overlaps the MMAs of the next), larger tiles
+// (<= 192 tokens) use both.  Every wait is bounded; on a timeout the CTA
+// flags the status word, drains its copies and MMAs, frees TMEM and exits.
 #include "tm_common.cuh"
 
 namespace tmoe {
 
 constexpr int kPfKT = 64;                        // K elements per pipeline stage
-constexpr int kPfNMax = 128;                     // tokens per tile (MMA N)
-constexpr int kPfRawStages = 4;
-constexpr int kPfOpStages = 3;
-constexpr int kPfRawBytes = 256 * kPfKT;         // 256 weight rows x 64 e4m3
-constexpr int kPfABytes = 128 * kPfKT * 2;       // one 128-row 16-bit operand
-constexpr int kPfBBytes = kPfNMax * kPfKT * 2;   // token rows of one stage
-constexpr int kPfSmem = kPfRawStages * kPfRawBytes + kPfOpStages * (2 * kPfABytes + kPfBBytes) + 1024;
+constexpr int kPfNMax = 192;                     // tokens per tile (MMA N; <= 2 x kPfNSmall)
+constexpr int kPfNSmall = 96;                    // tiles up to this size double-buffer their accumulators
+constexpr int kPfAStages = 2;                    // dequantised weight slices in TMEM (converters -> MMA)
+constexpr int kPfBStages = 5;                    // token-row slices in shared memory (gather -> MMA)
+constexpr int kPfGatherLag = 3;                  // gather stages in flight (< kPfBStages)
+constexpr int kPfL2Ahead = 6;                    // weight slices prefetched into L2 ahead of the converters
+constexpr int kPfBBytes = kPfNMax * kPfKT * 2;   // token rows of one stage (24 KB)
+constexpr int kPfSmem = kPfBStages * kPfBBytes + 1024;
 constexpr int kPfThreads = 512;
-constexpr int kPfWTma = 0, kPfWMma = 1, kPfWGather = 2, kPfNGather = 2, kPfWConv = 4, kPfNConv = 8,
+constexpr int kPfWPre = 0, kPfWMma = 1, kPfWGather = 2, kPfNGather = 2, kPfWConv = 4, kPfNConv = 8,
               kPfWEpi = 12;
 constexpr int kPfTmemCols = 512;
+constexpr int kPfAccBase = kPfAStages * 64;      // first accumulator column
+constexpr int kPfSlotCols = 192;                 // one accumulator slot (gate + up of <= 96 tokens)
 constexpr int kPfMaxExperts = 1024;
-constexpr int kPfALbo = (128 / 8) * 128;         // K-direction core-matrix stride of A
+constexpr int kPfMaxKBlocks = 128;               // K <= 16384
+constexpr int kPfMaxLocalTiles = 32;             // tile descriptors cached in shared memory
 
 enum { kPfGateUp = 0, kPfDown = 1 };
 
 template <typename TA> struct PfConv;
 template <> struct PfConv<__nv_bfloat16> {
   static constexpr uint32_t kFmt = 1;  // instruction-descriptor operand format BF16
-  static constexpr int kShift = 4;     // e4m3 magnitude bits -> bf16 bits 4..10 (value * 2^-120)
-  static __device__ __forceinline__ uint32_t scale(float s) {
+  static __device__ __forceinline__ uint32_t scale(float s) {  // bf16(s) * 2^112, exact
     const float sb = __bfloat162float(__float2bfloat16_rn(s));
-    const uint32_t q = __bfloat16_as_ushort(__float2bfloat16_rn(sb * 0x1p120f));
+    const uint32_t q = __bfloat16_as_ushort(__float2bfloat16_rn(sb * 0x1p112f));
     return q | (q << 16);
-  }
-  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
   }
 };
 template <> struct PfConv<__half> {
   static constexpr uint32_t kFmt = 0;  // F16
-  static constexpr int kShift = 1;     // -> f16 bits 7..13 (value * 2^-8)
-  static __device__ __forceinline__ uint32_t scale(float s) {
-    const float sh = __half2float(__float2half_rn(s));
-    const uint32_t q = __half_as_ushort(__float2half_rn(sh * 256.f));
-    return q | (q << 16);
-  }
-  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-  }
 };
 
-// Four e4m3 bytes -> two 16-bit pairs (bytes 0,1 -> w0; 2,3 -> w1), dequantised.
-template <typename TA>
-__device__ __forceinline__ void pf_convert4(uint32_t v, uint32_t S, uint32_t &w0, uint32_t &w1) {
-  const uint32_t vm = v & 0x7F7F7F7Fu;
-  const uint32_t a0 = __byte_perm(vm, 0, 0x1404) >> PfConv<TA>::kShift;
-  const uint32_t a1 = __byte_perm(vm, 0, 0x3424) >> PfConv<TA>::kShift;
-  const uint32_t s0 = __byte_perm(v, 0, 0x1404), s1 = __byte_perm(v, 0, 0x3424);
+// f16 weights: round_f16(w * f16(scale * 2^kw)).
+__device__ __forceinline__ uint32_t pf_scale_f16(float s, int kw) {
+  const uint32_t q = __half_as_ushort(__float2half_rn(ldexpf(s, kw)));
+  return q | (q << 16);
+}
+__device__ __forceinline__ void pf_convert4_f16(uint32_t v, uint32_t S, uint32_t &w0, uint32_t &w1) {
+  uint32_t h0, h1;
+  asm("{\n\t.reg .b16 p, q;\n\tmov.b32 {p, q}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, p;\n\tcvt.rn.f16x2.e4m3x2 %1, q;\n\t}"
+      : "=r"(h0), "=r"(h1)
+      : "r"(v));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w0) : "r"(h0), "r"(S));
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w1) : "r"(h1), "r"(S));
+}
+// bf16 weights (reference-exact): bytes 0,1 -> w0; 2,3 -> w1.  The exact f16
+// image of each e4m3 value has its 7 low mantissa bits zero, so shifting the
+// f16 magnitude right by 3 yields a bf16 pattern of value * 2^-112 (exponent
+// rebiased by the bf16 - f16 bias difference, never subnormal); the sign is
+// merged back and one bf16x2 multiply by bf16(scale) * 2^112 applies the
+// scale with a single rounding.  (Only an e4m3 NaN byte, absent from finite
+// checkpoints, would disturb its pair neighbour.)
+__device__ __forceinline__ void pf_convert4_bf16(uint32_t v, uint32_t S, uint32_t &w0, uint32_t &w1) {
+  uint32_t h0, h1;
+  asm("{\n\t.reg .b16 p, q;\n\tmov.b32 {p, q}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, p;\n\tcvt.rn.f16x2.e4m3x2 %1, q;\n\t}"
+      : "=r"(h0), "=r"(h1)
+      : "r"(v));
   uint32_t r0, r1;
-  asm("lop3.b32 %0, %1, %2, %3, 0xD8;" : "=r"(r0) : "r"(a0), "r"(s0), "r"(0x80008000u));  // sign from s, rest a
-  asm("lop3.b32 %0, %1, %2, %3, 0xD8;" : "=r"(r1) : "r"(a1), "r"(s1), "r"(0x80008000u));
-  w0 = PfConv<TA>::mul(r0, S);
-  w1 = PfConv<TA>::mul(r1, S);
+  asm("lop3.b32 %0, %1, %2, %3, 0xD8;" : "=r"(r0) : "r"((h0 & 0x7FFF7FFFu) >> 3), "r"(h0), "r"(0x80008000u));
+  asm("lop3.b32 %0, %1, %2, %3, 0xD8;" : "=r"(r1) : "r"((h1 & 0x7FFF7FFFu) >> 3), "r"(h1), "r"(0x80008000u));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(w0) : "r"(r0), "r"(S));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(w1) : "r"(r1), "r"(S));
 }
 
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | (uint64_t)((lbo >> 4) & 0x3FFF) << 16 |
-         (uint64_t)((sbo >> 4) & 0x3FFF) << 32 | (uint64_t)1 << 46;  // SWIZZLE_NONE, sm100 version
+// UMMA shared-memory descriptor, K-major 128-byte swizzle: 8-row groups 1024 B
+// apart (SBO), LBO unused (16 B), sm100 version bit 46.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (uint64_t)1 << 16 | (uint64_t)(1024 >> 4) << 32 | (uint64_t)1 << 46 |
+         (uint64_t)2 << 61;
 }
 
 template <typename TA> struct PfArgs {
-  const TA *act;       // gate/up: x [T][H]; down: h [P][I]
+  const TA *act;       // gate/up: x [T][H] (bf16 calls: its f16 copy); down: h [P][I]
   const uint8_t *w;    // packed w13 or w2 (all experts)
   const float *s;      // s13 or s2
   TA *out;             // gate/up: h [P][I]; down: y [P][H]
+  const float *slot_scale;  // gate/up with bf16 activations: per-slot 2^(shift - 8), else NULL
   const int *meta;
   const int4 *act_rec; // {expert, count, first slot, 0} per active expert
   const int *slot_token;
@@ -176,9 +198,10 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile("{.reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;}" ::"r"(d),
-               "l"(a), "l"(b), "r"(idesc), "r"(acc));
+// D[tmem] (+)= A[tmem] . B[smem]^T
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile("{.reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;}" ::"r"(d),
+               "r"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
@@ -191,35 +214,71 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+// 32 lanes x 32 consecutive 32-bit columns from this warp's 32 registers per lane.
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Accumulator placement of a tile (identical in the MMA issuer and the
+// epilogue): small tiles alternate between slots 0 and 1, large tiles use both.
+struct PfAcc {
+  uint32_t off;  // first column of gate (or first row half); second operand at off + npad
+  int slot;      // 0/1 for small tiles, -1 for large ones (both slots)
+};
+__device__ __forceinline__ PfAcc pf_acc(int npad, int &small_count) {
+  PfAcc r;
+  if (npad <= kPfNSmall) {
+    r.slot = small_count & 1;
+    ++small_count;
+    r.off = kPfAccBase + r.slot * kPfSlotCols;
+  } else {
+    r.slot = -1;
+    r.off = kPfAccBase;
+  }
+  return r;
+}
+
 template <typename TA, int kMode>
 __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
-  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *raw = sm;                                            // [kPfRawStages][kPfRawBytes]
-  uint8_t *opA = raw + kPfRawStages * kPfRawBytes;              // [kPfOpStages][2][kPfABytes]
-  uint8_t *opB = opA + kPfOpStages * 2 * kPfABytes;             // [kPfOpStages][kPfBBytes]
-  __shared__ __align__(8) uint64_t raw_full[kPfRawStages], raw_empty[kPfRawStages];
-  __shared__ __align__(8) uint64_t op_full[kPfOpStages], op_empty[kPfOpStages];
+  uint8_t *opB = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t a_full[kPfAStages], a_empty[kPfAStages];
+  __shared__ __align__(8) uint64_t b_full[kPfBStages], b_empty[kPfBStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
   __shared__ int prefix[kPfMaxExperts + 1];
+  __shared__ int4 tl_a[kPfMaxLocalTiles];  // {e, slot0, nvalid, npad}
+  __shared__ int tl_mt[kPfMaxLocalTiles];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
+  __shared__ volatile int conv_done;       // K slices the converters have finished (prefetch throttle)
   __shared__ int s_na, s_tiles;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool gate_up = kMode == kPfGateUp;
+  // f16 operands for every GEMM except the bf16 down projection
+  constexpr bool kF16 = kMode == kPfGateUp || PfConv<TA>::kFmt == 0;
+  constexpr uint32_t kFmt = kF16 ? 0u : 1u;
+  const int kw = (kMode == kPfGateUp && PfConv<TA>::kFmt == 1) ? 8 : 0;  // weight pre-scale 2^kw
   const int K = gate_up ? a.H : a.I;                   // reduction length
   const int MT = gate_up ? a.I / 128 : a.H / 256;      // weight-row blocks per expert
   const int out_ld = gate_up ? a.I : a.H;
   const int nk = K / kPfKT;
+  const int KB = K / 128;
 
   // ---- tile table: prefix[a] = first tile of active expert a ----
   if (warp == 0) {
@@ -246,20 +305,29 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
       s_na = na;
       s_tiles = run;
       abort_flag = 0;
+      conv_done = 0;
     }
   }
   __syncthreads();
   const int na = s_na, tiles = s_tiles;
   if ((int)blockIdx.x >= tiles) return;  // CTA-uniform
+  const int n_local = (tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
-  if (tid == 0) {
-    for (int s = 0; s < kPfRawStages; ++s) {
-      mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kPfNConv * 32);
+  if (warp == 0) {
+    for (int j = lane; j < min(n_local, kPfMaxLocalTiles); j += 32) {
+      const PfTile t = pf_tile(blockIdx.x + j * gridDim.x, prefix, na, a.act_rec, MT);
+      tl_a[j] = make_int4(t.e, t.slot0, t.nvalid, t.npad);
+      tl_mt[j] = t.mt;
     }
-    for (int s = 0; s < kPfOpStages; ++s) {
-      mbar_init(&op_full[s], (kPfNConv + kPfNGather) * 32);
-      mbar_init(&op_empty[s], 1);
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kPfAStages; ++s) {
+      mbar_init(&a_full[s], kPfNConv * 32);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < kPfBStages; ++s) {
+      mbar_init(&b_full[s], kPfNGather * 32);
+      mbar_init(&b_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -278,69 +346,89 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
-  if (warp == kPfWTma) {
-    // ---------------------------------------------------- TMA producer ----
+  auto tile_at = [&](int j) -> PfTile {
+    if (j < kPfMaxLocalTiles) {
+      const int4 v = tl_a[j];
+      PfTile t;
+      t.e = v.x; t.slot0 = v.y; t.nvalid = v.z; t.npad = v.w; t.mt = tl_mt[j];
+      return t;
+    }
+    return pf_tile(blockIdx.x + j * gridDim.x, prefix, na, a.act_rec, MT);
+  };
+  // Raw slice (tile t, stage kt) of weight rows: gate/up = 8 row groups x 2 KB
+  // (4 chunks x gate,up x 16 rows x 16 B), down = 16 row groups x 1 KB.
+  const int ngroups = gate_up ? 8 : 16;
+  const uint32_t gbytes = gate_up ? 2048 : 1024;
+  const size_t gstride = gate_up ? (size_t)32 * a.H : (size_t)16 * a.I;
+  auto slice_src = [&](const PfTile &t, int kt) -> const uint8_t * {
+    return gate_up ? a.w + (size_t)t.e * 2 * a.I * a.H + (size_t)(t.mt * 8) * 32 * a.H + (size_t)kt * 4 * 512
+                   : a.w + (size_t)t.e * a.H * a.I + (size_t)(t.mt * 16) * 16 * a.I + (size_t)kt * 4 * 256;
+  };
+
+  if (warp == kPfWPre) {
+    // ------------------------------------------ L2 prefetch of the weights ----
     if (lane == 0) {
-      uint32_t i = 0;
-      int last_parity[kPfRawStages];
-      for (int s = 0; s < kPfRawStages; ++s) last_parity[s] = -1;
-      for (int u = blockIdx.x; u < tiles && !abort_flag; u += gridDim.x) {
-        const PfTile t = pf_tile(u, prefix, na, a.act_rec, MT);
-        for (int kt = 0; kt < nk; ++kt, ++i) {
-          const int rs = i % kPfRawStages;
-          if (!pf_wait(&raw_empty[rs], ((i / kPfRawStages) & 1) ^ 1, &abort_flag, a.status)) break;
-          mbar_arrive_expect_tx(&raw_full[rs], kPfRawBytes);
-          last_parity[rs] = (i / kPfRawStages) & 1;
-          uint8_t *dst = raw + rs * kPfRawBytes;
-          if (gate_up) {
-            // 8 row groups x (4 chunks x gate,up x 16 rows x 16 B) = 8 x 2 KB
-            const uint8_t *src = a.w + (size_t)t.e * 2 * a.I * a.H + (size_t)(t.mt * 8) * 32 * a.H + (size_t)kt * 4 * 512;
-            for (int g = 0; g < 8; ++g) tma_bulk_g2s(dst + g * 2048, src + (size_t)g * 32 * a.H, 2048, &raw_full[rs]);
-          } else {
-            // 16 row groups x (4 chunks x 16 rows x 16 B) = 16 x 1 KB
-            const uint8_t *src = a.w + (size_t)t.e * a.H * a.I + (size_t)(t.mt * 16) * 16 * a.I + (size_t)kt * 4 * 256;
-            for (int g = 0; g < 16; ++g) tma_bulk_g2s(dst + g * 1024, src + (size_t)g * 16 * a.I, 1024, &raw_full[rs]);
+      int i = 0;
+      uint64_t t0;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+      for (int j = 0; j < n_local && !abort_flag; ++j) {
+        const PfTile t = tile_at(j);
+        for (int kt = 0; kt < nk && !abort_flag; ++kt, ++i) {
+          // stay at most kPfL2Ahead slices ahead of the converters
+          for (uint32_t it = 0; conv_done + kPfL2Ahead <= i && !abort_flag; ++it) {
+            if ((it & 255) == 255) {
+              uint64_t tn;
+              asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tn));
+              if (tn - t0 > 1000000000ull) break;  // keep prefetching; the converters have their own bounds
+            }
+            __nanosleep(64);
           }
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+          const uint8_t *src = slice_src(t, kt);
+          for (int g = 0; g < ngroups; ++g)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src + g * gstride), "r"(gbytes) : "memory");
         }
       }
-      // drain: every armed copy must land before the CTA may exit
-      volatile int no_abort = 0;
-      for (int s = 0; s < kPfRawStages; ++s)
-        if (last_parity[s] >= 0) pf_wait(&raw_full[s], (uint32_t)last_parity[s], &no_abort, a.status);
     }
   } else if (warp == kPfWMma) {
     // ------------------------------------------------------ MMA issuer ----
     if (lane == 0) {
-      uint32_t i = 0, l = 0;
+      uint32_t i = 0;
+      uint32_t use_e[2] = {0, 0};  // acc_empty phases waited per slot
+      int small_count = 0;
       bool issued = false;
-      for (int u = blockIdx.x; u < tiles && !abort_flag; u += gridDim.x, ++l) {
-        const PfTile t = pf_tile(u, prefix, na, a.act_rec, MT);
-        const int b = l & 1;
-        if (!pf_wait(&acc_empty[b], ((l >> 1) & 1) ^ 1, &abort_flag, a.status)) break;
-        tc_fence_after();
-        const uint32_t idesc = (1u << 4) | (PfConv<TA>::kFmt << 7) | (PfConv<TA>::kFmt << 10) |
-                               ((uint32_t)(t.npad >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-        const uint32_t lboB = (uint32_t)(t.npad / 8) * 128;
+      for (int j = 0; j < n_local && !abort_flag; ++j) {
+        const PfTile t = tile_at(j);
+        const PfAcc acc = pf_acc(t.npad, small_count);
         bool ok = true;
+        for (int s = 0; s < 2 && ok; ++s)
+          if (acc.slot < 0 || acc.slot == s) {
+            ok = pf_wait(&acc_empty[s], (use_e[s] & 1) ^ 1, &abort_flag, a.status);
+            ++use_e[s];
+          }
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t idesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((uint32_t)(t.npad >> 3) << 17) |
+                               ((uint32_t)(128 >> 4) << 24);
         for (int kt = 0; kt < nk; ++kt, ++i) {
-          const int os = i % kPfOpStages;
-          if (!pf_wait(&op_full[os], (i / kPfOpStages) & 1, &abort_flag, a.status)) { ok = false; break; }
+          const int as = i % kPfAStages, bs = i % kPfBStages;
+          if (!pf_wait(&a_full[as], (i / kPfAStages) & 1, &abort_flag, a.status) ||
+              !pf_wait(&b_full[bs], (i / kPfBStages) & 1, &abort_flag, a.status)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t aBase = smem_u32(opA + os * 2 * kPfABytes), bBase = smem_u32(opB + os * kPfBBytes);
+          const uint32_t bBase = smem_u32(opB + bs * kPfBBytes);
 #pragma unroll
           for (int s = 0; s < kPfKT / 16; ++s) {
-            const uint64_t bd = umma_desc(bBase + 2 * s * lboB, lboB, 128);
+            const uint64_t bd = umma_desc_sw128(bBase + 32 * s);
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint64_t ad = umma_desc(aBase + j * kPfABytes + 2 * s * kPfALbo, kPfALbo, 128);
-              tc_mma(tmem + b * 256 + j * 128, ad, bd, idesc, (kt | s) != 0);
-            }
+            for (int h = 0; h < 2; ++h)
+              tc_mma_ts(tmem + acc.off + h * t.npad, tmem + as * 64 + h * 32 + s * 8, bd, idesc, (kt | s) != 0);
           }
           issued = true;
-          tc_commit(&op_empty[os]);
+          tc_commit(&a_empty[as]);
+          tc_commit(&b_empty[bs]);
         }
         if (!ok) break;
-        tc_commit(&acc_full[b]);
+        tc_commit(&acc_full[acc.slot < 0 ? 0 : acc.slot]);
       }
       if (issued) {  // all MMAs of this CTA complete before TMEM may be freed
         tc_commit(&drain_bar);
@@ -351,128 +439,174 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   } else if (warp < kPfWConv) {
     // --------------------------------------------- token-row gather ----
     const int gt = tid - kPfWGather * 32;  // 0..63
+    const int kc = gt & 7;                 // 16-byte chunk of the row's 128-byte K slice
+    const int rsub = gt >> 3;              // row within each 8-row group
+    // swizzled destination of (row 8q + rsub, chunk kc)
+    const uint32_t dst_off = (uint32_t)rsub * 128 + (uint32_t)((kc ^ rsub) * 16);
     uint32_t i = 0;
-    int prev_os = -1;
-    for (int u = blockIdx.x; u < tiles && !abort_flag; u += gridDim.x) {
-      const PfTile t = pf_tile(u, prefix, na, a.act_rec, MT);
-      const int kc = gt & 7;
-      // rows this thread copies: n = gt/8 + 8q, q < npad/8
-      const TA *rows[kPfNMax / 8];
+    bool ok = true;
+    for (int j = 0; j < n_local && ok && !abort_flag; ++j) {
+      const PfTile t = tile_at(j);
+      int rowv[kPfNMax / 8];  // source row of each of this thread's rows
 #pragma unroll
       for (int q = 0; q < kPfNMax / 8; ++q) {
-        const int n = (gt >> 3) + 8 * q;
-        const int slot = t.slot0 + min(n, t.nvalid - 1);
-        const int r = gate_up ? __ldcg(a.slot_token + slot) : slot;
-        rows[q] = a.act + (size_t)r * K + kc * 8;
+        const int slot = t.slot0 + min(8 * q + rsub, t.nvalid - 1);
+        rowv[q] = gate_up ? __ldcg(a.slot_token + slot) : slot;
       }
-      bool ok = true;
       for (int kt = 0; kt < nk; ++kt, ++i) {
-        const int os = i % kPfOpStages;
-        if (!pf_wait(&op_empty[os], ((i / kPfOpStages) & 1) ^ 1, &abort_flag, a.status)) { ok = false; break; }
-        uint8_t *dstB = opB + os * kPfBBytes;
+        const int bs = i % kPfBStages;
+        if (!pf_wait(&b_empty[bs], ((i / kPfBStages) & 1) ^ 1, &abort_flag, a.status)) { ok = false; break; }
+        const uint32_t dstB = smem_u32(opB + bs * kPfBBytes) + dst_off;
+        const TA *base = a.act + (size_t)kt * kPfKT + kc * 8;
 #pragma unroll
-        for (int q = 0; q < kPfNMax / 8; ++q) {
-          const int n = (gt >> 3) + 8 * q;
-          if (n < t.npad)
-            cp_async16(dstB + (kc * (t.npad / 8) + n / 8) * 128 + (n % 8) * 16, rows[q] + kt * kPfKT);
-        }
+        for (int q = 0; q < kPfNMax / 8; ++q)
+          if (8 * q < t.npad) cp_async16(dstB + q * 1024, base + (size_t)rowv[q] * K);
         cp_async_commit();
-        if (prev_os >= 0) {
-          cp_async_wait<1>();
+        if (i >= (uint32_t)kPfGatherLag) {
+          cp_async_wait<kPfGatherLag>();
           fence_proxy_async();
-          mbar_arrive(&op_full[prev_os]);
+          mbar_arrive(&b_full[(i - kPfGatherLag) % kPfBStages]);
         }
-        prev_os = os;
       }
-      if (!ok) break;
     }
     cp_async_wait<0>();
-    if (prev_os >= 0 && !abort_flag) {
+    if (ok && !abort_flag) {
       fence_proxy_async();
-      mbar_arrive(&op_full[prev_os]);
+      for (uint32_t r = (i > (uint32_t)kPfGatherLag ? i - kPfGatherLag : 0); r < i; ++r)
+        mbar_arrive(&b_full[r % kPfBStages]);
     }
   } else if (warp < kPfWEpi) {
     // ------------------------------------------------------ converters ----
-    const int ct = tid - kPfWConv * 32;  // 0..255
-    uint32_t i = 0;
-    for (int u = blockIdx.x; u < tiles && !abort_flag; u += gridDim.x) {
-      const PfTile t = pf_tile(u, prefix, na, a.act_rec, MT);
-      bool ok = true;
-      for (int kt = 0; kt < nk; ++kt, ++i) {
-        const int rs = i % kPfRawStages, os = i % kPfOpStages;
-        uint32_t S0, S1;
-        if (gate_up) {
-          const float *sp = a.s + ((size_t)(t.e * (a.I / 128) + t.mt) * 2) * (a.H / 128) + (kt * kPfKT) / 128;
-          S0 = PfConv<TA>::scale(__ldg(sp));
-          S1 = PfConv<TA>::scale(__ldg(sp + a.H / 128));
-        } else {
-          const float *sp = a.s + ((size_t)t.e * (a.H / 128) + t.mt * 2) * (a.I / 128) + (kt * kPfKT) / 128;
-          S0 = PfConv<TA>::scale(__ldg(sp));
-          S1 = PfConv<TA>::scale(__ldg(sp + a.I / 128));
-        }
-        if (!pf_wait(&raw_full[rs], (i / kPfRawStages) & 1, &abort_flag, a.status)) { ok = false; break; }
-        if (!pf_wait(&op_empty[os], ((i / kPfOpStages) & 1) ^ 1, &abort_flag, a.status)) { ok = false; break; }
-        const uint8_t *src = raw + rs * kPfRawBytes;
-        uint8_t *dstA = opA + os * 2 * kPfABytes;
+    // Thread = one weight row m (TMEM lane) of operand h: its 64-byte K slice
+    // (4 chunks of 16 B) per stage, loaded a stage ahead into registers.
+    const int h = (warp - kPfWConv) >> 2;
+    const int q = warp & 3;
+    const int m = q * 32 + lane;
+    const uint32_t tlane = tmem + ((uint32_t)(q * 32) << 16);
+    // byte offset of (row m of operand h, chunk c) inside a slice: chunk stride
+    const size_t row_off = gate_up ? (size_t)(m >> 4) * 32 * a.H + h * 256 + (m & 15) * 16
+                                   : (size_t)(h * 8 + (m >> 4)) * 16 * a.I + (m & 15) * 16;
+    const int cstride = gate_up ? 512 : 256;
+    auto scale_ptr = [&](const PfTile &t) -> const float * {
+      return gate_up ? a.s + ((size_t)(t.e * (a.I / 128) + t.mt) * 2 + h) * KB
+                     : a.s + ((size_t)t.e * (a.H / 128) + t.mt * 2 + h) * (a.I / 128);
+    };
+    uint4 cur[4], nxt[4];
+    float cur_s = 0.f, nxt_s = 0.f;
+    PfTile t = tile_at(0);
+    {
+      const uint8_t *src = slice_src(t, 0) + row_off;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int p = ct + 256 * q;  // 16-byte piece of the raw stage
-          int r, c, j, m;
-          if (gate_up) {                // [g 8][c 4][j 2][r 16]
-            r = p & 15; j = (p >> 4) & 1; c = (p >> 5) & 3; m = (p >> 7) * 16 + r;
-          } else {                      // [g 16][c 4][r 16]
-            r = p & 15; c = (p >> 4) & 3; const int g = p >> 6; j = g >> 3; m = (g & 7) * 16 + r;
-          }
-          const uint4 v = *reinterpret_cast<const uint4 *>(src + p * 16);
-          const uint32_t S = j ? S1 : S0;
-          uint4 lo, hi;
-          pf_convert4<TA>(v.x, S, lo.x, lo.y);
-          pf_convert4<TA>(v.y, S, lo.z, lo.w);
-          pf_convert4<TA>(v.z, S, hi.x, hi.y);
-          pf_convert4<TA>(v.w, S, hi.z, hi.w);
-          uint8_t *d = dstA + j * kPfABytes + (m / 8) * 128 + (m % 8) * 16;
-          *reinterpret_cast<uint4 *>(d + (2 * c) * kPfALbo) = lo;
-          *reinterpret_cast<uint4 *>(d + (2 * c + 1) * kPfALbo) = hi;
+      for (int c = 0; c < 4; ++c) cur[c] = ldg_stream(src + c * cstride);
+      cur_s = __ldg(scale_ptr(t));
+    }
+    uint32_t i = 0;
+    bool ok = true;
+    for (int j = 0; j < n_local && ok && !abort_flag; ++j) {
+      for (int kt = 0; kt < nk; ++kt, ++i) {
+        // issue the next slice's loads before converting this one
+        const bool last_k = kt + 1 == nk;
+        const bool have_next = !last_k || j + 1 < n_local;
+        if (have_next) {
+          const PfTile tn = last_k ? tile_at(j + 1) : t;
+          const int ktn = last_k ? 0 : kt + 1;
+          const uint8_t *src = slice_src(tn, ktn) + row_off;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) nxt[c] = ldg_stream(src + c * cstride);
+          nxt_s = __ldg(scale_ptr(tn) + (ktn * kPfKT) / 128);
         }
-        mbar_arrive(&raw_empty[rs]);
-        fence_proxy_async();
-        mbar_arrive(&op_full[os]);
+        const int as = i % kPfAStages;
+        // warp-uniform outcome: the tcgen05.st below is .sync.aligned
+        if (!__all_sync(0xffffffffu, pf_wait(&a_empty[as], ((i / kPfAStages) & 1) ^ 1, &abort_flag, a.status))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t w[32];
+        if constexpr (kF16) {
+          const uint32_t S = pf_scale_f16(cur_s, kw);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            pf_convert4_f16(cur[c].x, S, w[8 * c + 0], w[8 * c + 1]);
+            pf_convert4_f16(cur[c].y, S, w[8 * c + 2], w[8 * c + 3]);
+            pf_convert4_f16(cur[c].z, S, w[8 * c + 4], w[8 * c + 5]);
+            pf_convert4_f16(cur[c].w, S, w[8 * c + 6], w[8 * c + 7]);
+          }
+        } else {
+          const uint32_t S = PfConv<TA>::scale(cur_s);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            pf_convert4_bf16(cur[c].x, S, w[8 * c + 0], w[8 * c + 1]);
+            pf_convert4_bf16(cur[c].y, S, w[8 * c + 2], w[8 * c + 3]);
+            pf_convert4_bf16(cur[c].z, S, w[8 * c + 4], w[8 * c + 5]);
+            pf_convert4_bf16(cur[c].w, S, w[8 * c + 6], w[8 * c + 7]);
+          }
+        }
+        tc_st32(tlane + as * 64 + h * 32, w);
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&a_full[as]);
+        if (tid == kPfWConv * 32) conv_done = (int)i + 1;
+        if (have_next) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) cur[c] = nxt[c];
+          cur_s = nxt_s;
+          if (last_k) t = tile_at(j + 1);
+        }
       }
-      if (!ok) break;
     }
   } else {
     // -------------------------------------------------------- epilogue ----
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int m = q * 32 + lane;
-    uint32_t l = 0;
-    for (int u = blockIdx.x; u < tiles && !abort_flag; u += gridDim.x, ++l) {
-      const PfTile t = pf_tile(u, prefix, na, a.act_rec, MT);
-      const int b = l & 1;
-      if (!pf_wait(&acc_full[b], (l >> 1) & 1, &abort_flag, a.status)) break;
+    uint32_t use_f[2] = {0, 0};
+    int small_count = 0;
+    for (int j = 0; j < n_local && !abort_flag; ++j) {
+      const PfTile t = tile_at(j);
+      const PfAcc acc = pf_acc(t.npad, small_count);
+      const int fs = acc.slot < 0 ? 0 : acc.slot;
+      // warp-uniform outcome: the tcgen05.ld below is .sync.aligned
+      if (!__all_sync(0xffffffffu, pf_wait(&acc_full[fs], use_f[fs] & 1, &abort_flag, a.status))) break;
+      ++use_f[fs];
       tc_fence_after();
-      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + b * 256;
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + acc.off;
+      // column scales (undo the token's f16 shift and the weights' 2^kw; exact
+      // powers of 2): lane jj of the warp holds the scale of column c0 + jj,
+      // loaded one 16-column chunk ahead
+      auto col_scale = [&](int c0) -> float {
+        return (a.slot_scale && lane < 16 && c0 + lane < t.nvalid) ? __ldcg(a.slot_scale + t.slot0 + c0 + lane) : 1.f;
+      };
+      float cs_next = gate_up ? col_scale(0) : 1.f;
       for (int c0 = 0; c0 < t.nvalid; c0 += 16) {
+        const float cs_cur = cs_next;
+        if (gate_up && c0 + 16 < t.nvalid) cs_next = col_scale(c0 + 16);
         float v0[16], v1[16];
         tc_ld16(tb + c0, v0);
-        tc_ld16(tb + 128 + c0, v1);
+        tc_ld16(tb + t.npad + c0, v1);
         tc_wait_ld();
         if (gate_up) {
           TA *o = a.out + (size_t)(t.slot0 + c0) * out_ld + t.mt * 128 + m;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (c0 + j < t.nvalid) o[(size_t)j * out_ld] = Act<TA>::from_f(silu(v0[j]) * v1[j]);
+          for (int jj = 0; jj < 16; ++jj) {
+            const float cs = __shfl_sync(0xffffffffu, cs_cur, jj);
+            if (c0 + jj < t.nvalid) {
+              const float g = v0[jj] * cs, u = v1[jj] * cs;
+              o[(size_t)jj * out_ld] = Act<TA>::from_f(__fdividef(g, 1.0f + __expf(-g)) * u);
+            }
+          }
         } else {
           TA *o = a.out + (size_t)(t.slot0 + c0) * out_ld + t.mt * 256 + m;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (c0 + j < t.nvalid) {
-              o[(size_t)j * out_ld] = Act<TA>::from_f(v0[j]);
-              o[(size_t)j * out_ld + 128] = Act<TA>::from_f(v1[j]);
+          for (int jj = 0; jj < 16; ++jj)
+            if (c0 + jj < t.nvalid) {
+              o[(size_t)jj * out_ld] = Act<TA>::from_f(v0[jj]);
+              o[(size_t)jj * out_ld + 128] = Act<TA>::from_f(v1[jj]);
             }
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[b]);
+      for (int s = 0; s < 2; ++s)
+        if (acc.slot < 0 || acc.slot == s) mbar_arrive(&acc_empty[s]);
     }
   }
 
@@ -515,6 +649,45 @@ __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, cons
   }
 }
 
+// bf16 activations only: x[t] -> f16 x16[t] = x[t] * 2^-s_t with s_t from the
+// row's max |x| (exact for bf16 values: 8 significant bits into f16's 11, the
+// row maximum scaled into [2^13, 2^14)), and for each of the token's k slots
+// slot_scale = 2^(s_t - 8), which undoes the shift and the weights' 2^8 in the
+// gate/up epilogue.  One CTA per token.
+__global__ void __launch_bounds__(256) k4_prep_x(const __nv_bfloat16 *x, const int *pair_slot, int H, int k,
+                                                 __half *x16, float *slot_scale) {
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  const __nv_bfloat16 *xr = x + (size_t)t * H;
+  float m = 0.f;
+  for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(xr + o));
+    const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(__bfloat162float(p[j])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+  const int sh = f16_shift(m);
+  for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(xr + o));
+    const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(&v);
+    uint4 r;
+    __half *q = reinterpret_cast<__half *>(&r);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = __float2half_rn(ldexpf(__bfloat162float(p[j]), -sh));
+    *reinterpret_cast<uint4 *>(x16 + (size_t)t * H + o) = r;
+  }
+  if ((int)threadIdx.x < k) {
+    const int s = __ldcg(pair_slot + (size_t)t * k + threadIdx.x);
+    if (s >= 0) slot_scale[s] = ldexpf(1.f, sh - 8);
+  }
+}
+
 static int num_sms() {
   static int n = 0;
   if (!n) {
@@ -542,12 +715,22 @@ struct PrefillLaunch {
       TA *h = ws_ptr<TA>(ws, L->h);        // [P][I] act dtype (region sized for fp32)
       TA *y = ws_ptr<TA>(ws, L->ypart);    // [P][H] act dtype
       const int grid = num_sms();
-      g.act = (const TA *)x; g.w = w13; g.s = s13; g.out = h;
+      g.act = (const TA *)x; g.w = w13; g.s = s13; g.out = h; g.slot_scale = nullptr;
+      if constexpr (PfConv<TA>::kFmt == 1) {
+        // bf16: the gate/up GEMM runs on f16 operands (x16 after y in the partial-output region)
+        __half *x16 = reinterpret_cast<__half *>(reinterpret_cast<char *>(y) + (size_t)T * k * H * sizeof(TA));
+        float *slot_scale = ws_ptr<float>(ws, L->logits);  // [P] (the region holds T * E >= P floats)
+        k4_prep_x<<<(unsigned)T, 256, 0, s>>>((const __nv_bfloat16 *)x, ws_ptr<int>(ws, L->pair_slot), H, k, x16,
+                                               slot_scale);
+        TM_LAUNCH_CHECK("k4_prep_x launch");
+        g.act = (const TA *)x16;
+        g.slot_scale = slot_scale;
+      }
       int rc = ensure_smem(reinterpret_cast<const void *>(k4_gemm<TA, kPfGateUp>), kPfSmem);
       if (rc) return rc;
       k4_gemm<TA, kPfGateUp><<<grid, kPfThreads, kPfSmem, s>>>(g);
       TM_LAUNCH_CHECK("k4_gemm gate/up launch");
-      g.act = h; g.w = w2; g.s = s2; g.out = y;
+      g.act = h; g.w = w2; g.s = s2; g.out = y; g.slot_scale = nullptr;
       rc = ensure_smem(reinterpret_cast<const void *>(k4_gemm<TA, kPfDown>), kPfSmem);
       if (rc) return rc;
       k4_gemm<TA, kPfDown><<<grid, kPfThreads, kPfSmem, s>>>(g);
@@ -569,8 +752,10 @@ extern "C" int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden,
                                       const float *s13, const uint8_t *w2, const float *s2, const void *residual,
                                       void *out, void *ws, int64_t ws_bytes, void *stream) {
   TM_REQUIRE(x && topk_w && w13 && s13 && w2 && s2 && out, "null pointer");
-  TM_REQUIRE(hidden % 256 == 0 && hidden > 0, "hidden (%d) must be a positive multiple of 256", hidden);
-  TM_REQUIRE(inter % 128 == 0 && inter > 0, "inter (%d) must be a positive multiple of 128", inter);
+  TM_REQUIRE(hidden % 256 == 0 && hidden > 0 && hidden <= 128 * kPfMaxKBlocks,
+             "hidden (%d) must be a positive multiple of 256, at most %d", hidden, 128 * kPfMaxKBlocks);
+  TM_REQUIRE(inter % 128 == 0 && inter > 0 && inter <= 128 * kPfMaxKBlocks,
+             "inter (%d) must be a positive multiple of 128, at most %d", inter, 128 * kPfMaxKBlocks);
   TM_REQUIRE(n_experts <= kPfMaxExperts, "n_experts %d > %d", n_experts, kPfMaxExperts);
   TM_REQUIRE(aligned(x, 16) && aligned(w13, 16) && aligned(w2, 16) && aligned(out, 16) &&
                  (!residual || aligned(residual, 16)),
