@@ -33,15 +33,14 @@
 // bf16 activations the gate/up GEMM runs on f16 (activations shifted by an
 // exact per-token power of 2, weights by 2^8; both undone in the epilogue).
 // bf16 down projection: bf16 weights exactly as the reference's bf16
-// dequantisation, round(cast(w) * cast(scale)): the e4m3 byte is placed into a
-// bf16 pattern (value * 2^-120, exact) and one bf16x2 multiply by
-// bf16(scale) * 2^120 applies the scale with a single rounding.  The tensor
+// dequantisation, round(cast(w) * cast(scale)) (pf_convert4_bf16).  The tensor
 // cores accumulate in fp32, as the reference's F.linear does.
 //
-// Warp roles (16 warps): 0 L2 prefetch of the weights, 1 TMEM owner + MMA
+// Warp roles (20 warps): 0 L2 prefetch of the weights, 1 TMEM owner + MMA
 // issuer, 2-3 token-row gather (cp.async into the K-major 128-byte-swizzle
 // layout, several stages in flight), 4-11 converters (warp w: operand
-// (w - 4) / 4, TMEM lane quadrant w % 4), 12-15 epilogue.  TMEM: columns
+// (w - 4) / 4, TMEM lane quadrant w % 4), 12-19 epilogue (two warps per lane
+// quadrant, alternate 16-column chunks).  TMEM: columns
 // [0, 128) hold the A ring (2 stages x 2 operands x 32 columns), [128, 512)
 // the accumulators: tiles of <= 96 tokens alternate between two 192-column
 // slots (the epilogue of one overlaps the MMAs of the next), larger tiles
@@ -60,9 +59,9 @@ constexpr int kPfGatherLag = 3;                  // gather stages in flight (< k
 constexpr int kPfL2Ahead = 6;                    // weight slices prefetched into L2 ahead of the converters
 constexpr int kPfBBytes = kPfNMax * kPfKT * 2;   // token rows of one stage (24 KB)
 constexpr int kPfSmem = kPfBStages * kPfBBytes + 1024;
-constexpr int kPfThreads = 512;
 constexpr int kPfWPre = 0, kPfWMma = 1, kPfWGather = 2, kPfNGather = 2, kPfWConv = 4, kPfNConv = 8,
-              kPfWEpi = 12;
+              kPfWEpi = 12, kPfNEpi = 8;
+constexpr int kPfThreads = (kPfWEpi + kPfNEpi) * 32;
 constexpr int kPfTmemCols = 512;
 constexpr int kPfAccBase = kPfAStages * 64;      // first accumulator column
 constexpr int kPfSlotCols = 192;                 // one accumulator slot (gate + up of <= 96 tokens)
@@ -214,15 +213,12 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// 32 lanes x 32 consecutive 32-bit columns from this warp's 32 registers per lane.
-__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+// 32 lanes x 16 consecutive 32-bit columns from this warp's 16 registers per lane.
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
-      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
-      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -331,7 +327,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], kPfNEpi * 32);
     }
     mbar_init(&drain_bar, 1);
     mbar_fence_init();
@@ -478,12 +474,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   } else if (warp < kPfWEpi) {
     // ------------------------------------------------------ converters ----
     // Thread = one weight row m (TMEM lane) of operand h: its 64-byte K slice
-    // (4 chunks of 16 B) per stage, loaded a stage ahead into registers.
+    // (4 chunks of 16 B) per stage.  Software pipeline over the CTA's slices:
+    // the loads of slice i + 2 are in flight while slice i is converted.
     const int h = (warp - kPfWConv) >> 2;
     const int q = warp & 3;
     const int m = q * 32 + lane;
     const uint32_t tlane = tmem + ((uint32_t)(q * 32) << 16);
-    // byte offset of (row m of operand h, chunk c) inside a slice: chunk stride
+    // byte offset of (row m of operand h, chunk 0) inside a slice; chunk stride
     const size_t row_off = gate_up ? (size_t)(m >> 4) * 32 * a.H + h * 256 + (m & 15) * 16
                                    : (size_t)(h * 8 + (m >> 4)) * 16 * a.I + (m & 15) * 16;
     const int cstride = gate_up ? 512 : 256;
@@ -491,73 +488,69 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
       return gate_up ? a.s + ((size_t)(t.e * (a.I / 128) + t.mt) * 2 + h) * KB
                      : a.s + ((size_t)t.e * (a.H / 128) + t.mt * 2 + h) * (a.I / 128);
     };
-    uint4 cur[4], nxt[4];
-    float cur_s = 0.f, nxt_s = 0.f;
-    PfTile t = tile_at(0);
-    {
-      const uint8_t *src = slice_src(t, 0) + row_off;
+    int pj = 0, pkt = 0;  // next slice to load
+    PfTile pt = tile_at(0);
+    auto load_slice = [&](uint4 (&dst)[4], float &sc) {
+      const uint8_t *src = slice_src(pt, pkt) + row_off;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) cur[c] = ldg_stream(src + c * cstride);
-      cur_s = __ldg(scale_ptr(t));
-    }
-    uint32_t i = 0;
-    bool ok = true;
-    for (int j = 0; j < n_local && ok && !abort_flag; ++j) {
-      for (int kt = 0; kt < nk; ++kt, ++i) {
-        // issue the next slice's loads before converting this one
-        const bool last_k = kt + 1 == nk;
-        const bool have_next = !last_k || j + 1 < n_local;
-        if (have_next) {
-          const PfTile tn = last_k ? tile_at(j + 1) : t;
-          const int ktn = last_k ? 0 : kt + 1;
-          const uint8_t *src = slice_src(tn, ktn) + row_off;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) nxt[c] = ldg_stream(src + c * cstride);
-          nxt_s = __ldg(scale_ptr(tn) + (ktn * kPfKT) / 128);
-        }
-        const int as = i % kPfAStages;
-        // warp-uniform outcome: the tcgen05.st below is .sync.aligned
-        if (!__all_sync(0xffffffffu, pf_wait(&a_empty[as], ((i / kPfAStages) & 1) ^ 1, &abort_flag, a.status))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t w[32];
-        if constexpr (kF16) {
-          const uint32_t S = pf_scale_f16(cur_s, kw);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            pf_convert4_f16(cur[c].x, S, w[8 * c + 0], w[8 * c + 1]);
-            pf_convert4_f16(cur[c].y, S, w[8 * c + 2], w[8 * c + 3]);
-            pf_convert4_f16(cur[c].z, S, w[8 * c + 4], w[8 * c + 5]);
-            pf_convert4_f16(cur[c].w, S, w[8 * c + 6], w[8 * c + 7]);
-          }
-        } else {
-          const uint32_t S = PfConv<TA>::scale(cur_s);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            pf_convert4_bf16(cur[c].x, S, w[8 * c + 0], w[8 * c + 1]);
-            pf_convert4_bf16(cur[c].y, S, w[8 * c + 2], w[8 * c + 3]);
-            pf_convert4_bf16(cur[c].z, S, w[8 * c + 4], w[8 * c + 5]);
-            pf_convert4_bf16(cur[c].w, S, w[8 * c + 6], w[8 * c + 7]);
-          }
-        }
-        tc_st32(tlane + as * 64 + h * 32, w);
-        tc_wait_st();
-        tc_fence_before();
-        mbar_arrive(&a_full[as]);
-        if (tid == kPfWConv * 32) conv_done = (int)i + 1;
-        if (have_next) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) cur[c] = nxt[c];
-          cur_s = nxt_s;
-          if (last_k) t = tile_at(j + 1);
-        }
+      for (int c = 0; c < 4; ++c) dst[c] = ldg_stream(src + c * cstride);
+      sc = __ldg(scale_ptr(pt) + (pkt * kPfKT) / 128);
+      if (++pkt == nk) {
+        pkt = 0;
+        if (++pj < n_local) pt = tile_at(pj);
       }
+    };
+    const uint32_t total = (uint32_t)n_local * (uint32_t)nk;
+    uint4 b0[4], b1[4], b2[4];
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    load_slice(b0, s0);
+    if (total > 1) load_slice(b1, s1);
+    for (uint32_t i = 0; i < total && !abort_flag; ++i) {
+      if (i + 2 < total) load_slice(b2, s2);
+      const int as = i % kPfAStages;
+      // warp-uniform outcome: the tcgen05.st below is .sync.aligned
+      if (!__all_sync(0xffffffffu, pf_wait(&a_empty[as], ((i / kPfAStages) & 1) ^ 1, &abort_flag, a.status))) break;
+      tc_fence_after();
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {  // chunks 2*half, 2*half + 1 -> 16 TMEM columns
+        uint32_t w[16];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const uint4 v = b0[2 * half + cc];
+          if constexpr (kF16) {
+            const uint32_t S = pf_scale_f16(s0, kw);
+            pf_convert4_f16(v.x, S, w[8 * cc + 0], w[8 * cc + 1]);
+            pf_convert4_f16(v.y, S, w[8 * cc + 2], w[8 * cc + 3]);
+            pf_convert4_f16(v.z, S, w[8 * cc + 4], w[8 * cc + 5]);
+            pf_convert4_f16(v.w, S, w[8 * cc + 6], w[8 * cc + 7]);
+          } else {
+            const uint32_t S = PfConv<TA>::scale(s0);
+            pf_convert4_bf16(v.x, S, w[8 * cc + 0], w[8 * cc + 1]);
+            pf_convert4_bf16(v.y, S, w[8 * cc + 2], w[8 * cc + 3]);
+            pf_convert4_bf16(v.z, S, w[8 * cc + 4], w[8 * cc + 5]);
+            pf_convert4_bf16(v.w, S, w[8 * cc + 6], w[8 * cc + 7]);
+          }
+        }
+        tc_st16(tlane + as * 64 + h * 32 + half * 16, w);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(&a_full[as]);
+      if (tid == kPfWConv * 32) conv_done = (int)i + 1;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        b0[c] = b1[c];
+        b1[c] = b2[c];
+      }
+      s0 = s1;
+      s1 = s2;
     }
   } else {
     // -------------------------------------------------------- epilogue ----
+    // two warps per TMEM lane quadrant; warp half `hf` takes the 16-column
+    // chunks 2c + hf of every tile
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int hf = (warp - kPfWEpi) >> 2;
     const int m = q * 32 + lane;
     uint32_t use_f[2] = {0, 0};
     int small_count = 0;
@@ -572,14 +565,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
       const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + acc.off;
       // column scales (undo the token's f16 shift and the weights' 2^kw; exact
       // powers of 2): lane jj of the warp holds the scale of column c0 + jj,
-      // loaded one 16-column chunk ahead
+      // loaded one chunk ahead
       auto col_scale = [&](int c0) -> float {
         return (a.slot_scale && lane < 16 && c0 + lane < t.nvalid) ? __ldcg(a.slot_scale + t.slot0 + c0 + lane) : 1.f;
       };
-      float cs_next = gate_up ? col_scale(0) : 1.f;
-      for (int c0 = 0; c0 < t.nvalid; c0 += 16) {
+      float cs_next = gate_up ? col_scale(16 * hf) : 1.f;
+      for (int c0 = 16 * hf; c0 < t.nvalid; c0 += 32) {
         const float cs_cur = cs_next;
-        if (gate_up && c0 + 16 < t.nvalid) cs_next = col_scale(c0 + 16);
+        if (gate_up && c0 + 32 < t.nvalid) cs_next = col_scale(c0 + 32);
         float v0[16], v1[16];
         tc_ld16(tb + c0, v0);
         tc_ld16(tb + t.npad + c0, v1);
