@@ -284,6 +284,34 @@ def run_ours(args, rank, world, local):
         torch.cuda.synchronize()
         return a_.elapsed_time(b_) / reps
 
+    # ---- prefill (tcgen05 grouped GEMMs): one 2048-token call of layer 0 ----
+    prefill = None
+    if args.prefill_tokens > 0:
+        Tp = args.prefill_tokens
+        pl0 = pls[0]
+        wsp = ops.Workspace(dev, 128, 8, shape.hidden, shape.inter, 0)
+        xp = synth.make_hidden(Tp, shape.hidden, SEED + 11, device=dev)
+        idx_p, w_p = ops.router_topk(xp, router.routers[0], 8, wsp)
+        outp = torch.empty_like(xp)
+        for _ in range(3):
+            ops.moe_prefill(xp, w_p, pl0.experts, wsp, outp)
+        torch.cuda.synchronize()
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        for _ in range(10):
+            ops.moe_prefill(xp, w_p, pl0.experts, wsp, outp)
+        b_.record()
+        torch.cuda.synchronize()
+        us = a_.elapsed_time(b_) / 10 * 1000
+        flops = 2.0 * Tp * 8 * 3 * shape.hidden * shape.inter
+        wbytes = 128 * EXPERT_BYTES
+        prefill = {"workload": f"one MoE layer call with {Tp} tokens (router excluded): tcgen05 grouped GEMMs",
+                   "us_per_layer": round(us, 1), "tokens_per_s_per_layer": round(Tp / (us * 1e-6), 1),
+                   "tflops": round(flops / (us * 1e-6) / 1e12, 1), "algorithmic_flops": flops,
+                   "weight_bytes": wbytes, "hbm_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+                   "status": ws.status() | wsp.status()}
+        assert torch.isfinite(outp.float()).all(), "non-finite prefill output"
+
     reps = max(5, args.steps)
     t_b = graph_time(False, False, reps)
     t_a = graph_time(True, False, reps)
@@ -322,7 +350,71 @@ def run_ours(args, rank, world, local):
         "clocks": clk.summary(),
         "upload_s": round(upload_s, 1),
     }
+    if prefill is not None:
+        res["prefill"] = prefill
     return res
+
+
+# ------------------------------------------------- expert-parallel decode ----
+def run_ep(args, rank, world, local):
+    """Expert-parallel batched decode: `--ep-tokens` sequences (one token each)
+    split over the ranks, the 128 experts of every layer sharded over them;
+    one step = the tokens through `--layers` MoE layers (dispatch / experts /
+    combine per layer).  Timed with CUDA events, max over ranks."""
+    from turbomoe import ops, synth
+    from turbomoe.ep import ExpertParallelMoE, cuda_functions
+    import torch.distributed as dist
+    if world == 1 and not dist.is_initialized():
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % (29500 + os.getpid() % 1000),
+                                rank=0, world_size=1)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shape = synth.QWEN3_30B_A3B
+    E, k, H, I = shape.experts, shape.top_k, shape.hidden, shape.inter
+    E_loc = E // world
+    T = args.ep_tokens // world
+    layers = []
+    for l in range(args.layers):
+        lw = synth.make_layer(shape, SEED, l, device=dev)
+        sl = slice(rank * E_loc, (rank + 1) * E_loc)
+        local_experts = ops.pack_experts(lw.gate[sl], lw.gate_s[sl], lw.up[sl], lw.up_s[sl], lw.down[sl],
+                                         lw.down_s[sl])
+        router_w = lw.router.to(torch.bfloat16).contiguous()
+        del lw
+        layers.append(ExpertParallelMoE(E, k, *cuda_functions(router_w, local_experts, k, E, H, I)))
+    torch.cuda.empty_cache()
+    x0 = synth.make_hidden(T, H, SEED + 100 + rank, rms_normalise=True, device=dev)
+
+    def step(x):
+        for ep in layers:
+            x = ep.forward(x, residual=x)
+        return x
+
+    for _ in range(args.warmup):
+        step(x0)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            y = step(x0)
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    assert torch.isfinite(y.float()).all(), "non-finite output"
+    sc, rc = layers[-1].last_counts
+    return {"metric": "expert-parallel batched decode tok/s, Qwen3-30B-A3B-FP8 MoE layers",
+            "value": round(T * world * args.steps / (ms / 1000.0), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e4m3 weights, bf16 act, fp32 math", "data": "synthetic (seeded weights, uniform routing)",
+            "config": {"workload": f"{args.ep_tokens} sequences x 1 token through {args.layers} MoE layers, "
+                                   f"experts sharded {E_loc} per GPU, all-to-all dispatch/combine (NCCL)",
+                       "tokens_per_rank": T, "experts_per_rank": E_loc, "parallelism": f"ep{world}"},
+            "rows_sent_last_layer_rank0": sc, "rows_recv_last_layer_rank0": rc,
+            "clocks": clk.summary()}
 
 
 # ------------------------------------------------------- CPU reference ----
@@ -389,6 +481,11 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="MoE layers per step (48 = the model)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=2048,
+                    help="also time one prefill layer call of this many tokens (0 = skip)")
+    ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
+                    help="decode: batch-1 decode (replicas for N>1); ep: expert-parallel batched decode")
+    ap.add_argument("--ep-tokens", type=int, default=256, help="ep workload: sequences over all ranks")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -400,6 +497,14 @@ def main():
             print(json.dumps(res), flush=True)
         return
     rank, world, local = dist_setup(args.gpus)
+    if args.workload == "ep":
+        res = run_ep(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        return
     res = run_ours(args, rank, world, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tps, dt, desc, threads = cpu_reference(steps=3, warmup=1, LAYERS=args.layers)

@@ -189,6 +189,17 @@ int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden, int inter,
                            const void *residual, void *out, void *ws, int64_t ws_bytes,
                            void *stream);
 
+/* Weighted combine of per-slot expert outputs in top-k order:
+ * out[t] = residual[t] + sum_r topk_w[t,r] * y[pair_slot[t*top_k + r]]
+ * (fp32 sums, slots < 0 skipped).  Replaces the weighted scatter-add of
+ * execution/moe.py:173-176 where the expert outputs were computed elsewhere
+ * (the expert-parallel path: rows come back from the ranks owning the
+ * experts).  y: [P][hidden] act; pair_slot: int32 [tokens*top_k]; bf16/fp16;
+ * hidden % 8 == 0. */
+int tm_combine_slots(const void *y, const void *topk_w, const int32_t *pair_slot, int64_t tokens,
+                     int hidden, int top_k, int act_dtype, const void *residual, void *out,
+                     void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* One whole decode layer without a caller workspace.  No counterpart in the
  * reference: it exists for callers that cannot allocate device memory for a

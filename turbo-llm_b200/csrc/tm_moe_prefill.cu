@@ -740,6 +740,34 @@ struct PrefillLaunch {
 
 using namespace tmoe;
 
+namespace tmoe {
+struct CombineLaunch {
+  const void *y; const void *w; const int *pair_slot; const void *residual; void *out; int64_t T; int H, k;
+  cudaStream_t s;
+  template <typename TA> int run() {
+    if constexpr (sizeof(TA) != 2) {
+      return fail(TM_ERR_UNSUPPORTED, "tm_combine_slots: act dtype must be bf16 or fp16");
+    } else {
+      k4_combine<TA><<<(unsigned)T, 256, 0, s>>>((const TA *)y, (const TA *)w, pair_slot, (const TA *)residual,
+                                                   (TA *)out, H, k);
+      TM_LAUNCH_CHECK("k4_combine launch");
+      return TM_OK;
+    }
+  }
+};
+}  // namespace tmoe
+
+extern "C" int tm_combine_slots(const void *y, const void *topk_w, const int32_t *pair_slot, int64_t tokens,
+                                int hidden, int top_k, int act_dtype, const void *residual, void *out,
+                                void *stream) {
+  TM_REQUIRE(y && topk_w && pair_slot && out, "null pointer");
+  TM_REQUIRE(tokens >= 1 && top_k >= 1 && hidden > 0 && hidden % 8 == 0, "bad shape");
+  TM_REQUIRE(aligned(y, 16) && aligned(out, 16) && (!residual || aligned(residual, 16)),
+             "y, residual and out must be 16-byte aligned");
+  CombineLaunch f{y, topk_w, pair_slot, residual, out, tokens, hidden, top_k, as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
 extern "C" int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden, int inter, int n_experts,
                                       int top_k, int act_dtype, const void *topk_w, const uint8_t *w13,
                                       const float *s13, const uint8_t *w2, const float *s2, const void *residual,

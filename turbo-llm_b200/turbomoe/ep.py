@@ -1,0 +1,123 @@
+"""Expert parallelism for batched decode: experts sharded over the ranks of a
+process group, tokens dispatched to the expert owners and the results combined
+back (all-to-all over NCCL / NVLink).
+
+Rank g of a group of G holds the experts [g * E/G, (g + 1) * E/G) of every MoE
+layer and its own tokens (data-parallel attention).  One layer call:
+
+  1. route the local tokens (fused router: top-k + routing plan).  The plan's
+     slot order is experts ascending, so the rows bound for each owner rank
+     are contiguous in it;
+  2. gather the routed token rows in slot order; exchange per-rank row counts
+     (an all-to-all of G ints, read on the host to size the exchange);
+  3. dispatch: all-to-all of the rows and of their expert ids local to the
+     owner;
+  4. the owner runs its experts on the received rows (one expert per row,
+     weight 1: the decode kernels, or the tcgen05 grouped GEMMs from 256 rows);
+  5. combine: all-to-all of the expert outputs back to the token owners, then
+     the routing-weighted sum in top-k order (tm_combine_slots).
+
+Per token the arithmetic is that of MoEExecutor.execute_layer
+(execution/moe.py:99-208): the same experts, weights and SwiGLU; only the
+summation order of the k expert outputs differs (top-k order, fp32).  The
+reference engine itself runs batch 1 on one device and has no expert
+parallelism.
+
+The exchange logic is independent of where the compute runs: `route_fn`,
+`expert_fn` and `combine_fn` are supplied by the caller.  `cuda_functions`
+builds the product ones from this library's kernels.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class Routing:
+    """Top-k routing of the local tokens and its plan (slots = routed pairs in
+    expert-ascending, then token-ascending order)."""
+    idx: torch.Tensor          # [T, k] int64 expert ids
+    w: torch.Tensor            # [T, k] routing weights (act dtype)
+    slot_token: torch.Tensor   # [P] int64 token of each slot
+    slot_expert: torch.Tensor  # [P] int64 expert of each slot
+    pair_slot: torch.Tensor    # [T * k] slot of (token t, rank r) at t * k + r
+    counts: torch.Tensor       # [E] int64 slots per expert
+
+
+class ExpertParallelMoE:
+    """One expert-parallel MoE layer call per `forward` (all ranks of `group`
+    must call it, in the same order, with their own tokens)."""
+
+    def __init__(self, n_experts: int, top_k: int, route_fn: Callable[[torch.Tensor], Routing],
+                 expert_fn: Callable[[torch.Tensor, torch.Tensor], torch.Tensor],
+                 combine_fn: Callable[[torch.Tensor, Routing, torch.Tensor | None], torch.Tensor],
+                 group=None):
+        self.group = group
+        self.G = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if n_experts % self.G:
+            raise ValueError(f"{n_experts} experts do not shard over {self.G} ranks")
+        self.E, self.k = n_experts, top_k
+        self.E_loc = n_experts // self.G
+        self.route_fn, self.expert_fn, self.combine_fn = route_fn, expert_fn, combine_fn
+        self.last_counts = None  # (send, recv) rows per rank of the last call, for reporting
+
+    def local_experts(self) -> range:
+        return range(self.rank * self.E_loc, (self.rank + 1) * self.E_loc)
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        T, H = x.shape
+        r = self.route_fn(x)
+        # 2. rows in slot order (grouped by owner rank) and the row counts
+        send_rows = x.index_select(0, r.slot_token)
+        send_eid = (r.slot_expert % self.E_loc).to(torch.int32)
+        send_counts = r.counts.view(self.G, self.E_loc).sum(1).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        self.last_counts = (sc, rc)
+        # 3. dispatch
+        R = sum(rc)
+        recv_rows = x.new_empty(R, H)
+        recv_eid = send_eid.new_empty(R)
+        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=self.group)
+        dist.all_to_all_single(recv_eid, send_eid, rc, sc, group=self.group)
+        # 4. local experts
+        y_recv = self.expert_fn(recv_rows, recv_eid) if R else x.new_empty(0, H)
+        # 5. combine
+        y_slots = x.new_empty(send_rows.shape[0], H)
+        dist.all_to_all_single(y_slots, y_recv.contiguous(), sc, rc, group=self.group)
+        return self.combine_fn(y_slots, r, residual)
+
+
+def cuda_functions(router_w: torch.Tensor, local_experts, top_k: int, n_experts: int, hidden: int, inter: int):
+    """(route_fn, expert_fn, combine_fn) on this library's kernels for one
+    layer: `router_w` [E, H] (act dtype), `local_experts` the PackedExperts of
+    this rank's shard."""
+    from . import ops
+    dev = router_w.device
+    ws_route = ops.Workspace(dev, n_experts, top_k, hidden, inter, 0)
+    ws_expert = ops.Workspace(dev, local_experts.n_experts, 1, hidden, inter, 0)
+
+    def route_fn(x):
+        T = x.shape[0]
+        idx, w = ops.router_topk(x, router_w, top_k, ws_route)
+        pv = ops.plan_views(ws_route, T, top_k)
+        slot_pair = pv["slot_pair"].long()
+        return Routing(idx=idx, w=w, slot_token=pv["slot_token"].long(), slot_expert=idx.view(-1)[slot_pair],
+                       pair_slot=pv["pair_slot"].clone(), counts=pv["counts"].long())
+
+    def expert_fn(rows, eid):
+        R = rows.shape[0]
+        ones = torch.ones(R, 1, dtype=rows.dtype, device=rows.device)
+        return ops.moe_experts(rows, eid.long().view(R, 1), ones, local_experts, ws_expert)
+
+    def combine_fn(y_slots, r, residual):
+        out = torch.empty(r.w.shape[0], y_slots.shape[1], dtype=y_slots.dtype, device=y_slots.device)
+        return ops.combine_slots(y_slots, r.w, r.pair_slot, out, residual)
+
+    return route_fn, expert_fn, combine_fn

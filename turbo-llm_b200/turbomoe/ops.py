@@ -225,6 +225,36 @@ def read_plan(ws: Workspace, tokens: int, top_k: int):
             "pair_slot": i32(off[6], P)}
 
 
+def plan_views(ws: Workspace, tokens: int, top_k: int):
+    """Device int32 views (no copy) of the routing plan in ``ws``: dict of
+    counts [E], offsets [E+1], slot_token [P], slot_pair [P], pair_slot [P]."""
+    import ctypes
+    off = (ctypes.c_int64 * 8)()
+    check(lib().tm_plan_offsets(tokens, ws.E, top_k, off), "tm_plan_offsets")
+    b = ws.buf
+    P = tokens * top_k
+
+    def i32(o, n):
+        return b[o:o + 4 * n].view(torch.int32)
+
+    return {"counts": i32(off[1], ws.E), "offsets": i32(off[2], ws.E + 1), "slot_token": i32(off[4], P),
+            "slot_pair": i32(off[5], P), "pair_slot": i32(off[6], P)}
+
+
+def combine_slots(y: torch.Tensor, w: torch.Tensor, pair_slot: torch.Tensor, out: torch.Tensor,
+                  residual: torch.Tensor | None = None):
+    """out[t] = residual[t] + sum_r w[t,r] * y[pair_slot[t*k+r]] (tm_combine_slots)."""
+    _need_cuda(y, w, pair_slot, out)
+    T, k = w.shape
+    ps = pair_slot.to(torch.int32).contiguous()
+    w = w.to(out.dtype).contiguous()
+    y = y.contiguous()
+    check(lib().tm_combine_slots(y.data_ptr(), w.data_ptr(), ps.data_ptr(), T, out.shape[1], k, _code(out.dtype),
+                                 _ptr(residual.contiguous() if residual is not None else None), out.data_ptr(),
+                                 _stream(out)), "tm_combine_slots")
+    return out
+
+
 def route_plan(idx: torch.Tensor, n_experts: int, ws: Workspace):
     _need_cuda(idx)
     src = idx
