@@ -299,7 +299,10 @@ def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out:
 
 # Calls with at least this many tokens (and no shared expert, 16-bit
 # activations) run on the tensor-core grouped GEMMs (tm_moe_prefill_grouped).
-PREFILL_MIN_TOKENS = 256
+# Measured on B200, Qwen3-30B-A3B layer (128 experts, top-8): the decode
+# kernels win at 4 tokens (55 vs 92 us), tie at 8, and the grouped GEMMs win
+# from 16 tokens (167 vs 181 us) to 2048 (298 us vs 9.7 ms).
+PREFILL_MIN_TOKENS = 16
 
 
 def prefill_eligible(T: int, dtype, packed: PackedExperts, shared) -> bool:
