@@ -266,3 +266,64 @@ def test_cuda_graph_replay_matches_eager():
         g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
+
+
+# Router tile shapes: one 16-token tile (9, 16 tokens), a ragged second tile
+# (17, 40), experts that do not fill the last warp (60) and 1..16 n-tiles per
+# warp (60, 128, 512, 1024 experts).  Logits against an fp64 dot product of the
+# same act-dtype inputs, rounded once: within one act-dtype ulp.
+TILE_CASES = [(60, 4, 1024, torch.float16), (128, 8, 2048, torch.bfloat16), (512, 10, 1024, torch.bfloat16),
+              (1024, 8, 512, torch.float16)]
+
+
+@pytest.mark.parametrize("E,k,H,dt", TILE_CASES)
+@pytest.mark.parametrize("T", [9, 16, 17, 40])
+def test_router_tile_shapes(E, k, H, dt, T):
+    from turbomoe import ops, synth
+    g = torch.Generator().manual_seed(E * 100 + T)
+    x = torch.randn(T, H, generator=g).to(dt)
+    rw = (torch.randn(E, H, generator=g) * 0.05).to(dt)
+    ws = ops.Workspace("cuda", E, k, H, 128, 0)
+    idx, w, logits = ops.router_topk(x.cuda(), rw.cuda(), k, ws, want_logits=True)
+    idx, w, logits = idx.cpu(), w.cpu(), logits.cpu()
+    exact = x.double() @ rw.double().T
+    ulp = torch.finfo(dt).eps * exact.abs().clamp_min(1e-3) * 1.01
+    assert bool(((logits.double() - exact).abs() <= ulp).all())
+    ref_idx, ref_p = O.topk_from_logits_stable(logits, k)
+    assert torch.equal(idx, ref_idx)
+    assert (w.float() - O.renormalise(ref_p, dt).float()).abs().max().item() <= 2 * torch.finfo(dt).eps
+    plan = ops.read_plan(ws, T, k)
+    grp = O.routing_groups(idx, E)
+    assert torch.equal(plan["counts"].long(), grp["counts"])
+    assert torch.equal(plan["offsets"].long(), grp["offsets"])
+    assert plan["experts"].tolist() == grp["experts"]
+    assert torch.equal(plan["slot_token"].long(), grp["tokens"])
+    assert torch.equal((plan["slot_pair"] % k).long(), grp["kpos"])
+    assert ws.status() == 0
+
+
+def test_route_plan_many_pairs_flags_bad_ids():
+    """The multi-CTA plan (more than 2048 pairs): a bad id gets pair_slot -1,
+    is left out of the counts, and sets the status bit; the others keep the
+    reference's grouping."""
+    from turbomoe import ops, synth
+    shape = synth.MoEShape(512, 256, 64, 4, 0)
+    ws = workspace_for(shape)
+    g = torch.Generator().manual_seed(3)
+    T = 700
+    idx = torch.stack([torch.randperm(64, generator=g)[:4] for _ in range(T)])
+    bad = idx.clone()
+    bad[308, 2] = 64                       # pair 1234
+    ops.route_plan(bad.cuda(), 64, ws)
+    plan = ops.read_plan(ws, T, 4)
+    assert ws.status() == 1
+    assert int(plan["pair_slot"][1234]) == -1
+    counts = torch.bincount(idx.flatten(), minlength=64)
+    counts[idx[308, 2]] -= 1
+    assert torch.equal(plan["counts"].long(), counts)
+    ops.route_plan(idx.cuda(), 64, ws)
+    plan = ops.read_plan(ws, T, 4)
+    grp = O.routing_groups(idx, 64)
+    assert torch.equal(plan["slot_token"].long(), grp["tokens"])
+    assert torch.equal((plan["slot_pair"] % 4).long(), grp["kpos"])
+    assert ws.status() == 0

@@ -88,6 +88,7 @@ WsLayout ws_layout(int64_t tokens, int n_experts, int top_k, int hidden, int int
   L.slot_token = take(P * 4);
   L.slot_pair = take(P * 4);
   L.pair_slot = take(P * 4);
+  L.unit_hist = take((T + 15) / 16 * E * 4);
   L.sh_w = take(T * 4);
   L.h = take(P * inter * 4);
   L.sh_h = take(T * Is * 4);

@@ -338,6 +338,7 @@ struct WsLayout {
   int64_t slot_token;  // int32 [P]
   int64_t slot_pair;   // int32 [P]
   int64_t pair_slot;   // int32 [P]
+  int64_t unit_hist;   // int32 [ceil(T/16)][E]: routed pairs per expert of each 16-token unit
   int64_t sh_w;       // fp32 [T] sigmoid(shared gate)
   int64_t h;           // fp32 [P][I]
   int64_t sh_h;        // fp32 [T][Is]

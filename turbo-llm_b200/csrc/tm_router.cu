@@ -38,6 +38,7 @@ struct PlanPtrs {
   int *slot_token, *slot_pair, *pair_slot;  // [P]
   int *k2_cnt;    // [(E+1)*kMaxRG]
   int *k3_cnt;    // [kMaxRGo]
+  int *unit_hist; // [ceil(T/16)][E]
   int k2_cnt_n, k3_cnt_n;
 };
 
@@ -55,6 +56,7 @@ static PlanPtrs plan_ptrs(void *ws, const WsLayout &L) {
   p.pair_slot = ws_ptr<int>(ws, L.pair_slot);
   p.k2_cnt = ws_ptr<int>(ws, L.k2_cnt);
   p.k3_cnt = ws_ptr<int>(ws, L.k3_cnt);
+  p.unit_hist = ws_ptr<int>(ws, L.unit_hist);
   p.k2_cnt_n = 0;  // K2 keeps no counters
   p.k3_cnt_n = kMaxRGo;
   return p;
@@ -693,6 +695,319 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<T
   plan_build(src, nt, a.k, a.E, a.pp, reinterpret_cast<int *>(r_smem));
 }
 
+// ------------------------------------- multi-token router (tensor cores) ----
+// Every 16-bit call the decode router does not take: one thread-block cluster
+// of kClusterCTAs CTAs per tile of kTcTile tokens.  CTA r of a cluster takes
+// the r-th eighth of the hidden dimension (in 32-element chunks) for every
+// expert; warp w covers experts [w*8*NT, (w+1)*8*NT) on mma.sync m16n8k16
+// (16-bit operands, fp32 accumulators).  The order of the reduction dimension
+// inside one MMA is free as long as A and B use the same one, so every lane
+// loads 16 contiguous bytes of its token rows and of its expert row and feeds
+// them to two MMAs (no shared-memory staging).  The eight partial sums of a
+// token go to the CTA that owns it (token j of a tile: CTA j % 8), which adds
+// them in CTA order, rounds to the act dtype (F.linear's output) and selects
+// the top-k.  A one-tile call also builds the routing plan in CTA 0; larger
+// calls leave it to k1_plan_scatter.
+constexpr int kTcTile = 16;
+
+template <typename TA> struct MmaAct;
+template <> struct MmaAct<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    mma_16816(d, a0, a1, a2, a3, b0, b1);
+  }
+};
+template <> struct MmaAct<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+};
+
+template <typename TA>
+__device__ __forceinline__ void topk_redux_dispatch(const RouterArgs<TA> &a, const float *lg, int t) {
+  if (a.E <= 128) topk_redux_token<TA, 4>(a, lg, t, nullptr, false);
+  else if (a.E <= 256) topk_redux_token<TA, 8>(a, lg, t, nullptr, false);
+  else if (a.E <= 512) topk_redux_token<TA, 16>(a, lg, t, nullptr, false);
+  else topk_redux_token<TA, 32>(a, lg, t, nullptr, false);
+}
+
+// Dynamic shared memory: partial logits [kClusterCTAs][2][Ec] (Ec = 64 * NT
+// experts), later the plan's scratch in CTA 0 of a one-tile call.
+template <typename TA, int NT>
+__global__ void __launch_bounds__(kRouterThreads) k1_router_tc(RouterArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(16) float tc_part[];
+  constexpr int EW = 8 * NT;                 // experts per warp
+  constexpr int Ec = kRouterWarps * EW;      // experts per CTA (>= E)
+  constexpr int G = NT <= 2 ? 4 : (NT <= 4 ? 2 : 1);  // chunks in flight per lane
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int t0 = blockIdx.y * kTcTile;
+  const int nt = min(kTcTile, a.T - t0);
+  const int nchunk = a.H / 32;
+  const int c_lo = crank * nchunk / kClusterCTAs, c_hi = (crank + 1) * nchunk / kClusterCTAs;
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrEnter);
+  // this CTA's slice of the router weights does not depend on the previous kernel
+  {
+    const int row_bytes = (c_hi - c_lo) * 64;  // 32 elements x 2 bytes per chunk
+    const int lines = (row_bytes + 127) / 128;
+    for (int i = tid; i < a.E * lines; i += kRouterThreads) {
+      const int e = i / lines, l = i - e * lines;
+      const char *p = reinterpret_cast<const char *>(a.w + (int64_t)e * a.H + c_lo * 32) + l * 128;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    }
+  }
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrWaited);
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  const bool rg = g < nt, rg8 = g + 8 < nt;
+  const uint4 *xg = reinterpret_cast<const uint4 *>(a.x + (int64_t)(t0 + (rg ? g : 0)) * a.H) + c;
+  const uint4 *xg8 = reinterpret_cast<const uint4 *>(a.x + (int64_t)(t0 + (rg8 ? g + 8 : 0)) * a.H) + c;
+  const uint4 *wr[NT];
+  bool we[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int e = w * EW + 8 * j + g;
+    we[j] = e < a.E;
+    wr[j] = reinterpret_cast<const uint4 *>(a.w + (int64_t)(we[j] ? e : 0) * a.H) + c;
+  }
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int ch = c_lo; ch < c_hi; ch += G) {
+    uint4 xa[G], xb[G], wv[G][NT];
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      const bool in = ch + u < c_hi;
+      const int v = (ch + u) * 4;  // 16-byte vectors before this chunk
+      xa[u] = (in && rg) ? __ldcg(xg + v) : z;
+      xb[u] = (in && rg8) ? __ldcg(xg8 + v) : z;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) wv[u][j] = (in && we[j]) ? __ldg(wr[j] + v) : z;
+    }
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        MmaAct<TA>::run(acc[j], xa[u].x, xb[u].x, xa[u].y, xb[u].y, wv[u][j].x, wv[u][j].y);
+        MmaAct<TA>::run(acc[j], xa[u].z, xb[u].z, xa[u].w, xb[u].w, wv[u][j].z, wv[u][j].w);
+      }
+    }
+  }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
+  // rows g and g + 8 of the tile both belong to CTA g
+  float *dst = cluster.map_shared_rank(tc_part, g);
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int e = w * EW + 8 * j + 2 * c;
+    *reinterpret_cast<float2 *>(dst + (crank * 2 + 0) * Ec + e) = make_float2(acc[j][0], acc[j][1]);
+    *reinterpret_cast<float2 *>(dst + (crank * 2 + 1) * Ec + e) = make_float2(acc[j][2], acc[j][3]);
+  }
+  cluster.sync();  // every partial of this CTA's two tokens has arrived
+  for (int i = tid; i < 2 * a.E; i += kRouterThreads) {
+    const int lr = i >= a.E ? 1 : 0, e = i - lr * a.E;
+    float s = 0.f;
+#pragma unroll
+    for (int src = 0; src < kClusterCTAs; ++src) s += tc_part[(src * 2 + lr) * Ec + e];
+    const float r = Act<TA>::round(s);  // F.linear output in act dtype
+    tc_part[lr * Ec + e] = r;           // over source 0's partial, read above by this thread only
+    const int t = crank + 8 * lr;
+    if (a.logits_out && t < nt) a.logits_out[(int64_t)(t0 + t) * a.E + e] = Act<TA>::from_f(r);
+  }
+  __syncthreads();
+  if (w < 2 && crank + 8 * w < nt) topk_redux_dispatch<TA>(a, tc_part + w * Ec, t0 + crank + 8 * w);
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrExit);
+  // CTA 0 reads the tile's indices the cluster wrote
+  __threadfence();
+  cluster.sync();
+  if (crank != 0) return;
+  if (a.n_ttiles != 1) {
+    // the tile's routed pairs per expert, for k1_plan_scatter
+    int *h = reinterpret_cast<int *>(tc_part);
+    for (int e = tid; e < a.E; e += kRouterThreads) h[e] = 0;
+    __syncthreads();
+    for (int p = tid; p < nt * a.k; p += kRouterThreads)
+      atomicAdd(&h[(int)__ldcg(a.idx_out + (int64_t)t0 * a.k + p)], 1);  // top-k ids are < E
+    __syncthreads();
+    for (int e = tid; e < a.E; e += kRouterThreads) a.pp.unit_hist[(int64_t)blockIdx.y * a.E + e] = h[e];
+    return;
+  }
+  // one tile: CTA 0 builds the plan
+  const IdxSource src{a.idx_out, nullptr};
+  if (nt * a.k <= 32) {
+    if (w == 0) {
+      plan_small_warp(src, nt, a.k, a.E, a.pp);
+    } else {
+      for (int i = tid - 32; i < a.pp.k2_cnt_n; i += kRouterThreads - 32) a.pp.k2_cnt[i] = 0;
+      for (int i = tid - 32; i < a.pp.k3_cnt_n; i += kRouterThreads - 32) a.pp.k3_cnt[i] = 0;
+    }
+    return;
+  }
+  plan_build(src, nt, a.k, a.E, a.pp, reinterpret_cast<int *>(tc_part));
+}
+
+template <int NT> static size_t router_tc_smem(int E) {
+  return std::max((size_t)kClusterCTAs * 2 * kRouterWarps * 8 * NT * sizeof(float), plan_smem(kRouterWarps, E));
+}
+
+// Routing plan of a call with many (token, rank) pairs, on many CTAs, from
+// the per-expert counts of every 16-token unit (unit_hist).  CTA b takes units
+// [b * U, (b + 1) * U): it adds up the counts of all units (totals) and of
+// the units before its own, derives the expert offsets, and places its pairs:
+// slot = offset[e] + earlier pairs of e, i.e. experts ascending and pair index
+// ascending within an expert (the order of plan_build).  CTA 0 also writes the
+// per-expert tables and zeroes the expert kernels' counters.
+constexpr int kUnitTokens = 16;
+static_assert(kUnitTokens == kTcTile, "k1_router_tc writes one unit_hist row per token tile");
+constexpr int kScatterThreads = 512;
+constexpr int kScatterWarps = kScatterThreads / 32;
+
+static size_t plan_scatter_smem(int E) { return sizeof(int) * ((size_t)(4 + kScatterWarps) * E + 64); }
+
+__global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t *idx, int T, int k, int E,
+                                                                   int U, PlanPtrs pp) {
+  extern __shared__ int sc_sm[];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int P = T * k;
+  const int n_units = (T + kUnitTokens - 1) / kUnitTokens;
+  const int u_lo = blockIdx.x * U;
+  const int lo = u_lo * kUnitTokens * k, hi = min(P, (u_lo + U) * kUnitTokens * k);
+  int *before = sc_sm;              // [E] valid pairs of e in units before u_lo
+  int *cnt = before + E;            // [E] valid pairs of e, then offsets
+  int *flag = cnt + E;              // [E] active flag, then active index
+  int *cnt0 = flag + E;             // [E] counts (kept)
+  int *hist = cnt0 + E;             // [kScatterWarps][E]
+  int *tmp = hist + kScatterWarps * E;  // [33]
+  for (int i = tid; i < 2 * E; i += kScatterThreads) sc_sm[i] = 0;
+  for (int i = tid; i < kScatterWarps * E; i += kScatterThreads) hist[i] = 0;
+  pdl_trigger();
+  pdl_wait();  // indices and unit counts come from the previous kernel
+  TM_TRACE_EVENT(pp.trace, kTrPlan, kTrWaited);
+  if (blockIdx.x == 0) {
+    for (int i = tid; i < pp.k2_cnt_n; i += kScatterThreads) pp.k2_cnt[i] = 0;
+    for (int i = tid; i < pp.k3_cnt_n; i += kScatterThreads) pp.k3_cnt[i] = 0;
+  }
+  __syncthreads();
+  // column sums of unit_hist: q threads per expert, each a strided set of units
+  const int q = max(1, kScatterThreads / E);
+  for (int col = tid; col < q * E; col += kScatterThreads) {
+    const int e = col % E, part = col / E;
+    int sb = 0, st = 0;
+#pragma unroll 8
+    for (int u = part; u < n_units; u += q) {
+      const int v = __ldcg(pp.unit_hist + (int64_t)u * E + e);
+      st += v;
+      sb += u < u_lo ? v : 0;
+    }
+    atomicAdd(&before[e], sb);
+    atomicAdd(&cnt[e], st);
+  }
+  __syncthreads();
+  for (int x = tid; x < E; x += kScatterThreads) {
+    cnt0[x] = cnt[x];
+    flag[x] = cnt[x] > 0 ? 1 : 0;
+  }
+  __syncthreads();
+  const int total = block_excl_scan(cnt, E, tmp);
+  const int n_active = block_excl_scan(flag, E, tmp);
+  if (blockIdx.x == 0) {
+    for (int x = tid; x < E; x += kScatterThreads) {
+      const int c0 = cnt0[x];
+      pp.counts[x] = c0;
+      pp.offsets[x] = cnt[x];
+      if (c0 > 0) {
+        pp.act_list[flag[x]] = x;
+        pp.act_rec[flag[x]] = make_int4(x, c0, cnt[x], 0);
+      }
+    }
+    if (tid == 0) {
+      pp.offsets[E] = total;
+      pp.meta[kMetaNActive] = n_active;
+      pp.meta[kMetaPairs] = P;
+      pp.meta[kMetaTokens] = T;
+    }
+  }
+  // this CTA's pairs: per-warp histograms, then a stable scatter (as plan_build)
+  const int n = max(0, hi - lo);
+  const int wlo = lo + (int)((int64_t)w * n / kScatterWarps), whi = lo + (int)((int64_t)(w + 1) * n / kScatterWarps);
+  for (int b = wlo; b < whi; b += 32) {
+    const int p = b + lane;
+    if (p < whi) {
+      const int64_t v = __ldcg(idx + p);
+      if (v >= 0 && v < E) atomicAdd(&hist[w * E + (int)v], 1);
+    }
+  }
+  __syncthreads();
+  for (int x = tid; x < E; x += kScatterThreads) {
+    int run = cnt[x] + before[x];
+    for (int j = 0; j < kScatterWarps; ++j) {
+      const int c0 = hist[j * E + x];
+      hist[j * E + x] = run;
+      run += c0;
+    }
+  }
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int b = wlo; b < whi; b += 32) {
+    const int p = b + lane;
+    int e = -1;
+    if (p < whi) {
+      const int64_t v = __ldcg(idx + p);
+      e = (v >= 0 && v < E) ? (int)v : -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & lt_mask);
+    if (p < whi) {
+      if (e >= 0) {
+        const int slot = hist[w * E + e] + rank;
+        pp.slot_pair[slot] = p;
+        pp.slot_token[slot] = p / k;
+        pp.pair_slot[p] = slot;
+      } else {
+        pp.pair_slot[p] = -1;
+      }
+    }
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) hist[w * E + e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// unit_hist from top-k indices given by the caller: one CTA per 16-token unit.
+__global__ void __launch_bounds__(256) k1_plan_hist(const int64_t *idx, int T, int k, int E, PlanPtrs pp) {
+  extern __shared__ int ph_sm[];
+  const int tid = threadIdx.x;
+  const int t0 = blockIdx.x * kUnitTokens, nt = min(kUnitTokens, T - t0);
+  for (int e = tid; e < E; e += blockDim.x) ph_sm[e] = 0;
+  pdl_trigger();
+  pdl_wait();
+  __syncthreads();
+  bool bad = false;
+  for (int p = tid; p < nt * k; p += blockDim.x) {
+    const int64_t v = __ldcg(idx + (int64_t)t0 * k + p);
+    if (v >= 0 && v < E) atomicAdd(&ph_sm[(int)v], 1);
+    else bad = true;
+  }
+  if (__any_sync(0xffffffffu, bad) && (tid & 31) == 0) atomicOr(pp.status, TM_STATUS_BAD_EXPERT_ID);
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) pp.unit_hist[(int64_t)blockIdx.x * E + e] = ph_sm[e];
+}
+
+// CTAs and units per CTA of k1_plan_scatter for T tokens.
+static void plan_scatter_grid(int64_t T, int *ctas, int *units) {
+  const int64_t n_units = (T + kUnitTokens - 1) / kUnitTokens;
+  const int64_t n = std::min<int64_t>(n_units, 148);
+  *units = (int)((n_units + n - 1) / n);
+  *ctas = (int)((n_units + *units - 1) / *units);
+}
 template <typename Kern, typename... Args>
 static int launch_cluster_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, int cluster_x, cudaStream_t s,
                               const char *what, Args... args) {
@@ -750,25 +1065,50 @@ struct RouterLaunch {
           default: return launch_cluster_pdl(k1_router_cluster<TA, 8>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
         }
       }
+      // every other 16-bit call: tensor-core logits, one cluster per 16 tokens
+      a.pp = plan_ptrs(ws, *L);
+      a.TB = kTcTile;
+      a.n_ttiles = (T + kTcTile - 1) / kTcTile;
+      a.n_etiles = kClusterCTAs;
+      if (a.n_ttiles > 65535) return fail(TM_ERR_UNSUPPORTED, "too many tokens for one router call (%d)", T);
+      const dim3 grid(kClusterCTAs, a.n_ttiles), block(kRouterThreads);
+      const int nt64 = (E + 63) / 64;
+      int rc;
+      switch (nt64 <= 1 ? 1 : nt64 <= 2 ? 2 : nt64 <= 4 ? 4 : nt64 <= 8 ? 8 : 16) {
+        case 1: rc = launch_cluster_pdl(k1_router_tc<TA, 1>, grid, block, router_tc_smem<1>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
+        case 2: rc = launch_cluster_pdl(k1_router_tc<TA, 2>, grid, block, router_tc_smem<2>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
+        case 4: rc = launch_cluster_pdl(k1_router_tc<TA, 4>, grid, block, router_tc_smem<4>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
+        case 8: rc = launch_cluster_pdl(k1_router_tc<TA, 8>, grid, block, router_tc_smem<8>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
+        default: rc = launch_cluster_pdl(k1_router_tc<TA, 16>, grid, block, router_tc_smem<16>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
+      }
+      if (rc || a.n_ttiles == 1) return rc;
+      int ctas, units;
+      plan_scatter_grid(T, &ctas, &units);
+      return launch_pdl(k1_plan_scatter, dim3(ctas), dim3(kScatterThreads), plan_scatter_smem(E), s,
+                        "k1_plan_scatter launch", (const int64_t *)idx, T, k, E, units, a.pp);
+    } else {
+      return run_fp32(a);
     }
+  }
+  int run_fp32(RouterArgs<float> &a) {
     if (T <= 8) { a.TB = T; a.EPW = 1; }
     else { a.TB = 16; a.EPW = 4; }
     // keep the token tile within 96 KB of shared memory
-    while (a.TB > 1 && (size_t)a.TB * H * sizeof(TA) > 96 * 1024) a.TB /= 2;
+    while (a.TB > 1 && (size_t)a.TB * H * sizeof(float) > 96 * 1024) a.TB /= 2;
     a.n_ttiles = (T + a.TB - 1) / a.TB;
     const int ew = a.EPW * kRouterWarps;
     a.n_etiles = (E + ew - 1) / ew;
     if (a.n_ttiles > kMaxTokenTiles)
       return fail(TM_ERR_UNSUPPORTED, "too many tokens for one router call (%d)", T);
     a.pp = plan_ptrs(ws, *L);
-    const size_t smem = std::max((size_t)a.TB * H * sizeof(TA), plan_smem(kRouterWarps, E));
+    const size_t smem = std::max((size_t)a.TB * H * sizeof(float), plan_smem(kRouterWarps, E));
     const dim3 grid(a.n_etiles, a.n_ttiles), block(kRouterThreads);
     switch (a.TB <= 1 ? 1 : a.TB <= 2 ? 2 : a.TB <= 4 ? 4 : a.TB <= 8 ? 8 : 16) {
-      case 1: return launch_pdl(k1_router<TA, 1>, grid, block, smem, s, "k1_router launch", a);
-      case 2: return launch_pdl(k1_router<TA, 2>, grid, block, smem, s, "k1_router launch", a);
-      case 4: return launch_pdl(k1_router<TA, 4>, grid, block, smem, s, "k1_router launch", a);
-      case 8: return launch_pdl(k1_router<TA, 8>, grid, block, smem, s, "k1_router launch", a);
-      default: return launch_pdl(k1_router<TA, 16>, grid, block, smem, s, "k1_router launch", a);
+      case 1: return launch_pdl(k1_router<float, 1>, grid, block, smem, s, "k1_router launch", a);
+      case 2: return launch_pdl(k1_router<float, 2>, grid, block, smem, s, "k1_router launch", a);
+      case 4: return launch_pdl(k1_router<float, 4>, grid, block, smem, s, "k1_router launch", a);
+      case 8: return launch_pdl(k1_router<float, 8>, grid, block, smem, s, "k1_router launch", a);
+      default: return launch_pdl(k1_router<float, 16>, grid, block, smem, s, "k1_router launch", a);
     }
   }
 };
@@ -784,7 +1124,7 @@ extern "C" int tm_router_topk(const void *x, int64_t tokens, int hidden, int act
   TM_REQUIRE(x && router_w && topk_idx && topk_w, "null pointer");
   TM_REQUIRE(hidden > 0 && hidden % 128 == 0, "hidden (%d) must be a positive multiple of 128", hidden);
   TM_REQUIRE(n_experts <= 32 * kMaxExpertsPerLane, "n_experts %d > %d", n_experts, 32 * kMaxExpertsPerLane);
-  TM_REQUIRE(top_k <= 32, "top_k %d > 32", top_k);
+  TM_REQUIRE(top_k >= 1 && top_k <= 32 && top_k <= n_experts, "top_k %d must be in [1, min(32, n_experts %d)]", top_k, n_experts);
   TM_REQUIRE(aligned(x, 16) && aligned(router_w, 16), "x and router_w must be 16-byte aligned");
   WsLayout L;
   // the router only needs the header + logits + plan regions; expert sizes do not matter
@@ -803,6 +1143,16 @@ extern "C" int tm_route_plan(const int64_t *topk_idx, int64_t tokens, int top_k,
   int rc = ws_check(ws, ws_bytes, tokens, n_experts, top_k, 128, 0, 0, &L);
   if (rc) return rc;
   PlanPtrs pp = plan_ptrs(ws, L);
+  if (tokens * top_k > 2048) {  // many pairs: counts per 16-token unit, then one CTA per range of units
+    const int n_units = (int)((tokens + kUnitTokens - 1) / kUnitTokens);
+    int rc = launch_pdl(k1_plan_hist, dim3(n_units), dim3(256), sizeof(int) * (size_t)n_experts, as_stream(stream),
+                        "k1_plan_hist launch", topk_idx, (int)tokens, top_k, n_experts, pp);
+    if (rc) return rc;
+    int ctas, units;
+    plan_scatter_grid(tokens, &ctas, &units);
+    return launch_pdl(k1_plan_scatter, dim3(ctas), dim3(kScatterThreads), plan_scatter_smem(n_experts),
+                      as_stream(stream), "k1_plan_scatter launch", topk_idx, (int)tokens, top_k, n_experts, units, pp);
+  }
   const int threads = 1024;
   const size_t smem = plan_smem(threads / 32, n_experts);
   return launch_pdl(k1_plan_only, dim3(1), dim3(threads), smem, as_stream(stream), "k1_plan_only launch",
