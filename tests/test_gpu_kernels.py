@@ -268,8 +268,8 @@ def test_cuda_graph_replay_matches_eager():
     assert torch.equal(out, eager)
 
 
-# Router tile shapes: one 16-token tile (9, 16 tokens), a ragged second tile
-# (17, 40), experts that do not fill the last warp (60) and 1..16 n-tiles per
+# Router tile shapes: one 16-token tile (3, 9, 16 tokens), a ragged second
+# tile (17, 40), 64-token tiles with a ragged last one (600), experts that do not fill the last warp (60) and 1..16 n-tiles per
 # warp (60, 128, 512, 1024 experts).  Logits against an fp64 dot product of the
 # same act-dtype inputs, rounded once: within one act-dtype ulp.
 TILE_CASES = [(60, 4, 1024, torch.float16), (128, 8, 2048, torch.bfloat16), (512, 10, 1024, torch.bfloat16),
@@ -277,7 +277,7 @@ TILE_CASES = [(60, 4, 1024, torch.float16), (128, 8, 2048, torch.bfloat16), (512
 
 
 @pytest.mark.parametrize("E,k,H,dt", TILE_CASES)
-@pytest.mark.parametrize("T", [9, 16, 17, 40])
+@pytest.mark.parametrize("T", [3, 9, 16, 17, 40, 600])
 def test_router_tile_shapes(E, k, H, dt, T):
     from turbomoe import ops, synth
     g = torch.Generator().manual_seed(E * 100 + T)

@@ -26,6 +26,7 @@ constexpr int kRowVecs = 16;            // 16-byte vectors of a router row a lan
 constexpr int kClusterCTAs = 8;         // decode router: one thread-block cluster
 constexpr int kClusterMaxE = kClusterCTAs * kRouterWarps * 2;  // 2 expert rows per warp
 constexpr int kClusterMaxT = 8;
+constexpr int kClusterMaxTFast = 2;  // beyond this the tensor-core router is faster (measured on B200)
 
 struct PlanPtrs {
   uint32_t *status;
@@ -509,7 +510,8 @@ __device__ __forceinline__ uint32_t order16(uint32_t b) {
 }
 __device__ __forceinline__ uint32_t unorder16(uint32_t k) { return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu); }
 
-// Top-k of one token from logits in shared memory (one warp); with
+// Top-k of one token from logits in shared memory (one warp); the ids also go
+// to s_idx[0..k) when given (local or another CTA's shared memory).  With
 // `plan` (a single-token call) the same warp also writes the routing plan.
 template <typename TA, int EPL>
 __device__ void topk_redux_token(const RouterArgs<TA> &a, const float *lg, int t, int *s_idx, bool plan) {
@@ -547,7 +549,7 @@ __device__ void topk_redux_token(const RouterArgs<TA> &a, const float *lg, int t
   if (lane < a.k) {
     a.idx_out[(int64_t)t * a.k + lane] = my_e;
     a.w_out[(int64_t)t * a.k + lane] = Act<TA>::from_f(p / psum);
-    if (s_idx) s_idx[t * a.k + lane] = my_e;
+    if (s_idx) s_idx[lane] = my_e;
   }
   if (!plan) return;
   // single token: the k distinct experts each get one slot, in ascending id order
@@ -681,7 +683,7 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<T
     }
     return;
   }
-  if (w < nt) topk_redux_token<TA, kClusterMaxE / 32>(a, s_logit[w], w, s_idx, false);
+  if (w < nt) topk_redux_token<TA, kClusterMaxE / 32>(a, s_logit[w], w, s_idx + w * a.k, false);
   __syncthreads();
   const IdxSource src{a.idx_out, s_idx};
   if (nt * a.k <= 32) {
@@ -729,28 +731,37 @@ template <> struct MmaAct<__nv_bfloat16> {
 };
 
 template <typename TA>
-__device__ __forceinline__ void topk_redux_dispatch(const RouterArgs<TA> &a, const float *lg, int t) {
-  if (a.E <= 128) topk_redux_token<TA, 4>(a, lg, t, nullptr, false);
-  else if (a.E <= 256) topk_redux_token<TA, 8>(a, lg, t, nullptr, false);
-  else if (a.E <= 512) topk_redux_token<TA, 16>(a, lg, t, nullptr, false);
-  else topk_redux_token<TA, 32>(a, lg, t, nullptr, false);
+__device__ __forceinline__ void topk_redux_dispatch(const RouterArgs<TA> &a, const float *lg, int t, int *s_idx) {
+  if (a.E <= 128) topk_redux_token<TA, 4>(a, lg, t, s_idx, false);
+  else if (a.E <= 256) topk_redux_token<TA, 8>(a, lg, t, s_idx, false);
+  else if (a.E <= 512) topk_redux_token<TA, 16>(a, lg, t, s_idx, false);
+  else topk_redux_token<TA, 32>(a, lg, t, s_idx, false);
 }
 
-// Dynamic shared memory: partial logits [kClusterCTAs][2][Ec] (Ec = 64 * NT
-// experts), later the plan's scratch in CTA 0 of a one-tile call.
-template <typename TA, int NT>
-__global__ void __launch_bounds__(kRouterThreads) k1_router_tc(RouterArgs<TA> a) {
+constexpr int kTcMaxMT = 4;  // m16 tiles per cluster (64 tokens)
+
+// MT m16 tiles (16 * MT tokens) per cluster; token j of a tile belongs to CTA
+// j % 8 as its row j / 8.  64-token tiles are held to 128 registers (two CTAs
+// per SM: measured faster than one CTA with more chunks in flight).  Dynamic shared memory: partial logits
+// [kClusterCTAs][2 * MT][Ec] (Ec = 64 * NT experts), later the plan's scratch
+// in CTA 0 of a one-tile call.
+template <typename TA, int NT, int MT>
+__global__ void __launch_bounds__(kRouterThreads, MT == 4 ? 2 : 1) k1_router_tc(RouterArgs<TA> a) {
   static_assert(sizeof(TA) == 2, "16-bit activations");
+  static_assert(2 * MT <= kRouterWarps, "one warp per owned token");
   extern __shared__ __align__(16) float tc_part[];
+  __shared__ int s_tidx[kTcTile * kTcMaxMT * 32];  // CTA 0: the tile's top-k ids
   constexpr int EW = 8 * NT;                 // experts per warp
   constexpr int Ec = kRouterWarps * EW;      // experts per CTA (>= E)
-  constexpr int G = NT <= 2 ? 4 : (NT <= 4 ? 2 : 1);  // chunks in flight per lane
+  constexpr int R = 2 * MT;                  // rows (tokens) owned per CTA
+  constexpr int LPC = 2 * MT + NT;           // 16-byte loads per lane per chunk
+  constexpr int G = LPC <= 4 ? 2 : 1;        // chunks in flight per lane
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
-  const int t0 = blockIdx.y * kTcTile;
-  const int nt = min(kTcTile, a.T - t0);
+  const int t0 = blockIdx.y * (kTcTile * MT);
+  const int nt = min(kTcTile * MT, a.T - t0);
   const int nchunk = a.H / 32;
   const int c_lo = crank * nchunk / kClusterCTAs, c_hi = (crank + 1) * nchunk / kClusterCTAs;
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrEnter);
@@ -767,12 +778,21 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_tc(RouterArgs<TA> a)
   pdl_trigger();
   pdl_wait();  // x comes from the previous kernel
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrWaited);
-  float acc[NT][4];
+  float acc[MT][NT][4];
 #pragma unroll
-  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const bool rg = g < nt, rg8 = g + 8 < nt;
-  const uint4 *xg = reinterpret_cast<const uint4 *>(a.x + (int64_t)(t0 + (rg ? g : 0)) * a.H) + c;
-  const uint4 *xg8 = reinterpret_cast<const uint4 *>(a.x + (int64_t)(t0 + (rg8 ? g + 8 : 0)) * a.H) + c;
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[m][j][0] = acc[m][j][1] = acc[m][j][2] = acc[m][j][3] = 0.f;
+  const uint4 *xr[MT][2];
+  bool xin[MT][2];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = 16 * m + 8 * h + g;
+      xin[m][h] = r < nt;
+      xr[m][h] = reinterpret_cast<const uint4 *>(a.x + (int64_t)(t0 + (xin[m][h] ? r : 0)) * a.H) + c;
+    }
   const uint4 *wr[NT];
   bool we[NT];
 #pragma unroll
@@ -783,65 +803,77 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_tc(RouterArgs<TA> a)
   }
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
   for (int ch = c_lo; ch < c_hi; ch += G) {
-    uint4 xa[G], xb[G], wv[G][NT];
+    uint4 xv[G][MT][2], wv[G][NT];
 #pragma unroll
     for (int u = 0; u < G; ++u) {
       const bool in = ch + u < c_hi;
       const int v = (ch + u) * 4;  // 16-byte vectors before this chunk
-      xa[u] = (in && rg) ? __ldcg(xg + v) : z;
-      xb[u] = (in && rg8) ? __ldcg(xg8 + v) : z;
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) xv[u][m][h] = (in && xin[m][h]) ? __ldcg(xr[m][h] + v) : z;
 #pragma unroll
       for (int j = 0; j < NT; ++j) wv[u][j] = (in && we[j]) ? __ldg(wr[j] + v) : z;
     }
 #pragma unroll
-    for (int u = 0; u < G; ++u) {
+    for (int u = 0; u < G; ++u)
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        MmaAct<TA>::run(acc[j], xa[u].x, xb[u].x, xa[u].y, xb[u].y, wv[u][j].x, wv[u][j].y);
-        MmaAct<TA>::run(acc[j], xa[u].z, xb[u].z, xa[u].w, xb[u].w, wv[u][j].z, wv[u][j].w);
-      }
-    }
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const uint4 &p = xv[u][m][0], &q = xv[u][m][1], &b = wv[u][j];
+          MmaAct<TA>::run(acc[m][j], p.x, q.x, p.y, q.y, b.x, b.y);
+          MmaAct<TA>::run(acc[m][j], p.z, q.z, p.w, q.w, b.z, b.w);
+        }
   }
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
-  // rows g and g + 8 of the tile both belong to CTA g
+  // rows 16m + g and 16m + g + 8 belong to CTA g as its rows 2m and 2m + 1
   float *dst = cluster.map_shared_rank(tc_part, g);
 #pragma unroll
-  for (int j = 0; j < NT; ++j) {
-    const int e = w * EW + 8 * j + 2 * c;
-    *reinterpret_cast<float2 *>(dst + (crank * 2 + 0) * Ec + e) = make_float2(acc[j][0], acc[j][1]);
-    *reinterpret_cast<float2 *>(dst + (crank * 2 + 1) * Ec + e) = make_float2(acc[j][2], acc[j][3]);
-  }
-  cluster.sync();  // every partial of this CTA's two tokens has arrived
-  for (int i = tid; i < 2 * a.E; i += kRouterThreads) {
-    const int lr = i >= a.E ? 1 : 0, e = i - lr * a.E;
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int e = w * EW + 8 * j + 2 * c;
+      *reinterpret_cast<float2 *>(dst + (crank * R + 2 * m) * Ec + e) = make_float2(acc[m][j][0], acc[m][j][1]);
+      *reinterpret_cast<float2 *>(dst + (crank * R + 2 * m + 1) * Ec + e) = make_float2(acc[m][j][2], acc[m][j][3]);
+    }
+  cluster.sync();  // every partial of this CTA's tokens has arrived
+  for (int i = tid; i < R * a.E; i += kRouterThreads) {
+    const int r = i / a.E, e = i - r * a.E;
     float s = 0.f;
 #pragma unroll
-    for (int src = 0; src < kClusterCTAs; ++src) s += tc_part[(src * 2 + lr) * Ec + e];
-    const float r = Act<TA>::round(s);  // F.linear output in act dtype
-    tc_part[lr * Ec + e] = r;           // over source 0's partial, read above by this thread only
-    const int t = crank + 8 * lr;
-    if (a.logits_out && t < nt) a.logits_out[(int64_t)(t0 + t) * a.E + e] = Act<TA>::from_f(r);
+    for (int src = 0; src < kClusterCTAs; ++src) s += tc_part[(src * R + r) * Ec + e];
+    const float v = Act<TA>::round(s);  // F.linear output in act dtype
+    tc_part[r * Ec + e] = v;            // over source 0's partial, read above by this thread only
+    const int j = 8 * r + crank;        // token within the tile
+    if (a.logits_out && j < nt) a.logits_out[(int64_t)(t0 + j) * a.E + e] = Act<TA>::from_f(v);
   }
   __syncthreads();
-  if (w < 2 && crank + 8 * w < nt) topk_redux_dispatch<TA>(a, tc_part + w * Ec, t0 + crank + 8 * w);
+  if (w < R && 8 * w + crank < nt) {
+    const int j = 8 * w + crank;
+    int *tidx0 = cluster.map_shared_rank(s_tidx, 0);
+    topk_redux_dispatch<TA>(a, tc_part + w * Ec, t0 + j, tidx0 + j * a.k);
+  }
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrExit);
-  // CTA 0 reads the tile's indices the cluster wrote
-  __threadfence();
-  cluster.sync();
+  cluster.sync();  // CTA 0 holds the tile's top-k ids
   if (crank != 0) return;
   if (a.n_ttiles != 1) {
-    // the tile's routed pairs per expert, for k1_plan_scatter
-    int *h = reinterpret_cast<int *>(tc_part);
-    for (int e = tid; e < a.E; e += kRouterThreads) h[e] = 0;
+    // routed pairs per expert of each 16-token unit, for k1_plan_scatter
+    int *h = reinterpret_cast<int *>(tc_part);  // [MT][E]
+    for (int e = tid; e < MT * a.E; e += kRouterThreads) h[e] = 0;
     __syncthreads();
-    for (int p = tid; p < nt * a.k; p += kRouterThreads)
-      atomicAdd(&h[(int)__ldcg(a.idx_out + (int64_t)t0 * a.k + p)], 1);  // top-k ids are < E
+    for (int p = tid; p < nt * a.k; p += kRouterThreads) {
+      const int unit = p / (kTcTile * a.k);
+      atomicAdd(&h[unit * a.E + s_tidx[p]], 1);  // top-k ids are < E
+    }
     __syncthreads();
-    for (int e = tid; e < a.E; e += kRouterThreads) a.pp.unit_hist[(int64_t)blockIdx.y * a.E + e] = h[e];
+    const int units = (nt + kTcTile - 1) / kTcTile;
+    int *dst_h = a.pp.unit_hist + (int64_t)(t0 / kTcTile) * a.E;
+    for (int e = tid; e < units * a.E; e += kRouterThreads) dst_h[e] = h[e];
     return;
   }
   // one tile: CTA 0 builds the plan
-  const IdxSource src{a.idx_out, nullptr};
+  const IdxSource src{a.idx_out, s_tidx};
   if (nt * a.k <= 32) {
     if (w == 0) {
       plan_small_warp(src, nt, a.k, a.E, a.pp);
@@ -854,8 +886,9 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_tc(RouterArgs<TA> a)
   plan_build(src, nt, a.k, a.E, a.pp, reinterpret_cast<int *>(tc_part));
 }
 
-template <int NT> static size_t router_tc_smem(int E) {
-  return std::max((size_t)kClusterCTAs * 2 * kRouterWarps * 8 * NT * sizeof(float), plan_smem(kRouterWarps, E));
+template <int NT, int MT> static size_t router_tc_smem(int E) {
+  return std::max((size_t)kClusterCTAs * 2 * MT * kRouterWarps * 8 * NT * sizeof(float),
+                  std::max(plan_smem(kRouterWarps, E), (size_t)MT * E * sizeof(int)));
 }
 
 // Routing plan of a call with many (token, rank) pairs, on many CTAs, from
@@ -896,19 +929,39 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
     for (int i = tid; i < pp.k3_cnt_n; i += kScatterThreads) pp.k3_cnt[i] = 0;
   }
   __syncthreads();
-  // column sums of unit_hist: q threads per expert, each a strided set of units
-  const int q = max(1, kScatterThreads / E);
-  for (int col = tid; col < q * E; col += kScatterThreads) {
-    const int e = col % E, part = col / E;
-    int sb = 0, st = 0;
+  // column sums of unit_hist: q threads per group of 4 experts (16-byte loads)
+  // or per expert, each over a strided set of units
+  if ((E & 3) == 0) {
+    const int E4 = E >> 2;
+    const int q = max(1, kScatterThreads / E4);
+    for (int col = tid; col < q * E4; col += kScatterThreads) {
+      const int e4 = col % E4, part = col / E4;
+      int4 sb = make_int4(0, 0, 0, 0), st = make_int4(0, 0, 0, 0);
 #pragma unroll 8
-    for (int u = part; u < n_units; u += q) {
-      const int v = __ldcg(pp.unit_hist + (int64_t)u * E + e);
-      st += v;
-      sb += u < u_lo ? v : 0;
+      for (int u = part; u < n_units; u += q) {
+        const int4 v = __ldcg(reinterpret_cast<const int4 *>(pp.unit_hist + (int64_t)u * E) + e4);
+        st.x += v.x; st.y += v.y; st.z += v.z; st.w += v.w;
+        if (u < u_lo) { sb.x += v.x; sb.y += v.y; sb.z += v.z; sb.w += v.w; }
+      }
+      atomicAdd(&before[4 * e4 + 0], sb.x); atomicAdd(&before[4 * e4 + 1], sb.y);
+      atomicAdd(&before[4 * e4 + 2], sb.z); atomicAdd(&before[4 * e4 + 3], sb.w);
+      atomicAdd(&cnt[4 * e4 + 0], st.x); atomicAdd(&cnt[4 * e4 + 1], st.y);
+      atomicAdd(&cnt[4 * e4 + 2], st.z); atomicAdd(&cnt[4 * e4 + 3], st.w);
     }
-    atomicAdd(&before[e], sb);
-    atomicAdd(&cnt[e], st);
+  } else {
+    const int q = max(1, kScatterThreads / E);
+    for (int col = tid; col < q * E; col += kScatterThreads) {
+      const int e = col % E, part = col / E;
+      int sb = 0, st = 0;
+#pragma unroll 8
+      for (int u = part; u < n_units; u += q) {
+        const int v = __ldcg(pp.unit_hist + (int64_t)u * E + e);
+        st += v;
+        sb += u < u_lo ? v : 0;
+      }
+      atomicAdd(&before[e], sb);
+      atomicAdd(&cnt[e], st);
+    }
   }
   __syncthreads();
   for (int x = tid; x < E; x += kScatterThreads) {
@@ -938,12 +991,22 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
   // this CTA's pairs: per-warp histograms, then a stable scatter (as plan_build)
   const int n = max(0, hi - lo);
   const int wlo = lo + (int)((int64_t)w * n / kScatterWarps), whi = lo + (int)((int64_t)(w + 1) * n / kScatterWarps);
-  for (int b = wlo; b < whi; b += 32) {
-    const int p = b + lane;
-    if (p < whi) {
-      const int64_t v = __ldcg(idx + p);
-      if (v >= 0 && v < E) atomicAdd(&hist[w * E + (int)v], 1);
-    }
+  // the first kKeep groups of 32 ids stay in registers for the second pass
+  constexpr int kKeep = 4;
+  auto load_e = [&](int p) -> int {
+    if (p >= whi) return -2;
+    const int64_t v = __ldcg(idx + p);
+    return (v >= 0 && v < E) ? (int)v : -1;
+  };
+  int keep[kKeep];
+#pragma unroll
+  for (int it = 0; it < kKeep; ++it) keep[it] = load_e(wlo + it * 32 + lane);
+#pragma unroll
+  for (int it = 0; it < kKeep; ++it)
+    if (keep[it] >= 0) atomicAdd(&hist[w * E + keep[it]], 1);
+  for (int b = wlo + kKeep * 32; b < whi; b += 32) {
+    const int e = load_e(b + lane);
+    if (e >= 0) atomicAdd(&hist[w * E + e], 1);
   }
   __syncthreads();
   for (int x = tid; x < E; x += kScatterThreads) {
@@ -956,29 +1019,25 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
   }
   __syncthreads();
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int b = wlo; b < whi; b += 32) {
-    const int p = b + lane;
-    int e = -1;
-    if (p < whi) {
-      const int64_t v = __ldcg(idx + p);
-      e = (v >= 0 && v < E) ? (int)v : -1;
-    }
+  auto place = [&](int p, int e) {
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank = __popc(peers & lt_mask);
-    if (p < whi) {
-      if (e >= 0) {
-        const int slot = hist[w * E + e] + rank;
-        pp.slot_pair[slot] = p;
-        pp.slot_token[slot] = p / k;
-        pp.pair_slot[p] = slot;
-      } else {
-        pp.pair_slot[p] = -1;
-      }
+    if (e >= 0) {
+      const int slot = hist[w * E + e] + rank;
+      pp.slot_pair[slot] = p;
+      pp.slot_token[slot] = p / k;
+      pp.pair_slot[p] = slot;
+    } else if (e == -1) {
+      pp.pair_slot[p] = -1;
     }
     __syncwarp();
     if (e >= 0 && lane == __ffs(peers) - 1) hist[w * E + e] += __popc(peers);
     __syncwarp();
-  }
+  };
+#pragma unroll
+  for (int it = 0; it < kKeep; ++it)
+    if (wlo + it * 32 < whi) place(wlo + it * 32 + lane, keep[it]);
+  for (int b = wlo + kKeep * 32; b < whi; b += 32) place(b + lane, load_e(b + lane));
 }
 
 // unit_hist from top-k indices given by the caller: one CTA per 16-token unit.
@@ -1051,7 +1110,7 @@ struct RouterLaunch {
     a.T = T; a.H = H; a.E = E; a.k = k;
     if constexpr (sizeof(TA) == 2) {
       // decode-sized call: one thread-block cluster, no global synchronisation
-      if (T <= kClusterMaxT && E <= kClusterMaxE && H / 8 <= 32 * 8 && (H / 8) % 32 == 0 && k <= 32) {
+      if (T <= kClusterMaxTFast && E <= kClusterMaxE && H / 8 <= 32 * 8 && (H / 8) % 32 == 0 && k <= 32) {
         a.pp = plan_ptrs(ws, *L);
         a.TB = T;
         a.n_ttiles = 1;
@@ -1066,21 +1125,36 @@ struct RouterLaunch {
         }
       }
       // every other 16-bit call: tensor-core logits, one cluster per 16 tokens
+      // (64 for large calls: a quarter of the CTAs and of the weight re-reads)
+      const int nt64 = (E + 63) / 64;
+      const int NT = nt64 <= 1 ? 1 : nt64 <= 2 ? 2 : nt64 <= 4 ? 4 : nt64 <= 8 ? 8 : 16;
+      const int MT = (T > 512 && NT <= 4) ? 4 : 1;
       a.pp = plan_ptrs(ws, *L);
-      a.TB = kTcTile;
-      a.n_ttiles = (T + kTcTile - 1) / kTcTile;
+      a.TB = kTcTile * MT;
+      a.n_ttiles = (T + a.TB - 1) / a.TB;
       a.n_etiles = kClusterCTAs;
       if (a.n_ttiles > 65535) return fail(TM_ERR_UNSUPPORTED, "too many tokens for one router call (%d)", T);
       const dim3 grid(kClusterCTAs, a.n_ttiles), block(kRouterThreads);
-      const int nt64 = (E + 63) / 64;
       int rc;
-      switch (nt64 <= 1 ? 1 : nt64 <= 2 ? 2 : nt64 <= 4 ? 4 : nt64 <= 8 ? 8 : 16) {
-        case 1: rc = launch_cluster_pdl(k1_router_tc<TA, 1>, grid, block, router_tc_smem<1>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
-        case 2: rc = launch_cluster_pdl(k1_router_tc<TA, 2>, grid, block, router_tc_smem<2>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
-        case 4: rc = launch_cluster_pdl(k1_router_tc<TA, 4>, grid, block, router_tc_smem<4>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
-        case 8: rc = launch_cluster_pdl(k1_router_tc<TA, 8>, grid, block, router_tc_smem<8>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
-        default: rc = launch_cluster_pdl(k1_router_tc<TA, 16>, grid, block, router_tc_smem<16>(E), kClusterCTAs, s, "k1_router_tc launch", a); break;
+#define TM_ROUTER_TC(nt_, mt_)                                                                              \
+  rc = launch_cluster_pdl(k1_router_tc<TA, nt_, mt_>, grid, block, router_tc_smem<nt_, mt_>(E), kClusterCTAs, s, \
+                          "k1_router_tc launch", a)
+      if (MT == 4) {
+        switch (NT) {
+          case 1: TM_ROUTER_TC(1, 4); break;
+          case 2: TM_ROUTER_TC(2, 4); break;
+          default: TM_ROUTER_TC(4, 4); break;
+        }
+      } else {
+        switch (NT) {
+          case 1: TM_ROUTER_TC(1, 1); break;
+          case 2: TM_ROUTER_TC(2, 1); break;
+          case 4: TM_ROUTER_TC(4, 1); break;
+          case 8: TM_ROUTER_TC(8, 1); break;
+          default: TM_ROUTER_TC(16, 1); break;
+        }
       }
+#undef TM_ROUTER_TC
       if (rc || a.n_ttiles == 1) return rc;
       int ctas, units;
       plan_scatter_grid(T, &ctas, &units);
