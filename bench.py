@@ -303,12 +303,19 @@ def run_ours(args, rank, world, local):
         b_.record()
         torch.cuda.synchronize()
         us = a_.elapsed_time(b_) / 10 * 1000
+        a_.record()
+        for _ in range(10):
+            ops.router_topk(xp, router.routers[0], 8, wsp)
+        b_.record()
+        torch.cuda.synchronize()
+        router_us = a_.elapsed_time(b_) / 10 * 1000
         flops = 2.0 * Tp * 8 * 3 * shape.hidden * shape.inter
         wbytes = 128 * EXPERT_BYTES
         prefill = {"workload": f"one MoE layer call with {Tp} tokens (router excluded): tcgen05 grouped GEMMs",
                    "us_per_layer": round(us, 1), "tokens_per_s_per_layer": round(Tp / (us * 1e-6), 1),
                    "tflops": round(flops / (us * 1e-6) / 1e12, 1), "algorithmic_flops": flops,
                    "weight_bytes": wbytes, "hbm_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+                   "router_us": round(router_us, 1),
                    "status": ws.status() | wsp.status()}
         assert torch.isfinite(outp.float()).all(), "non-finite prefill output"
 
