@@ -230,6 +230,70 @@ int tm_moe_decode_layer_noalloc(const void *x, int64_t tokens, int hidden, int i
                                 const void *sh_gate_w, const void *residual, int64_t *topk_idx,
                                 void *topk_w, void *out, uint32_t *status, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Expert parallelism over NVLink peer memory (no counterpart in the reference,
+ * which runs batch 1 on one device: runtime/engine.py:103-107,158; per token
+ * the arithmetic is MoEExecutor.execute_layer, execution/moe.py:99-208).
+ * The experts of a layer are sharded over `world` ranks of one node (one
+ * process per GPU; rank r owns experts [r*E/world, (r+1)*E/world)).  Every
+ * rank creates a context (one device buffer of identical layout), exchanges
+ * the 64-byte IPC handles with its peers by any host means and connects.
+ * One layer call on every rank, in this order on one stream:
+ *   tm_router_topk(x, ..., ws)            top-k + routing plan of the local tokens
+ *   tm_ep_dispatch(ctx, x, T, idx, ws)    rows -> the owners' buffers (peer stores)
+ *   tm_ep_experts(ctx, local experts, owner_ws)
+ *                                         wait for all sources, grouped GEMMs on
+ *                                         the received rows, outputs -> sources
+ *   tm_ep_combine(ctx, w, T, ws, residual, out)
+ *                                         wait for all owners, weighted sum
+ * No host synchronisation: the sequence is CUDA-graph capturable.  Every
+ * device-side wait is bounded (tm_ep_set_timeout, default 2 s); on expiry
+ * TM_STATUS_TIMEOUT is set in the context status (tm_ep_status) and the call's
+ * outputs are invalid.  Tokens per call may differ between ranks (each at most
+ * max_tokens).  bf16/fp16 activations; hidden % 256 == 0, inter % 128 == 0. */
+#define TM_EP_MAX_RANKS 8
+#define TM_EP_HANDLE_BYTES 64
+typedef struct tm_ep_ctx tm_ep_ctx;
+/* Bytes of the device buffer each rank allocates (for reporting). */
+int64_t tm_ep_buffer_bytes(int world, int64_t max_tokens, int n_experts, int top_k, int hidden, int act_dtype);
+/* Allocate and zero this rank's buffer on the current device; writes its IPC
+ * handle (TM_EP_HANDLE_BYTES, host memory) to handle_out. */
+int tm_ep_create(int rank, int world, int n_experts, int top_k, int hidden, int inter, int act_dtype,
+                 int64_t max_tokens, void *handle_out, tm_ep_ctx **out);
+/* Map the peers' buffers: handles = world x TM_EP_HANDLE_BYTES in rank order
+ * (host memory; this rank's own entry is ignored). */
+int tm_ep_connect(tm_ep_ctx *ctx, const void *handles);
+/* Alternative to tm_ep_connect for hosts that map peer memory themselves:
+ * peer_bases[r] = rank r's buffer in this process (own entry ignored). */
+int tm_ep_connect_ptrs(tm_ep_ctx *ctx, void *const *peer_bases);
+/* This rank's buffer (device pointer), for tm_ep_connect_ptrs of other contexts. */
+void *tm_ep_local_buffer(tm_ep_ctx *ctx);
+int tm_ep_set_timeout(tm_ep_ctx *ctx, int64_t timeout_ns);
+/* Synchronises the device and unmaps the peers' buffers.  Call it on every
+ * rank after a host barrier (no peer may still be in a layer call). */
+int tm_ep_disconnect(tm_ep_ctx *ctx);
+/* Frees this rank's buffer and the context (disconnecting first if needed).
+ * Call it after every rank has disconnected (a second host barrier). */
+int tm_ep_destroy(tm_ep_ctx *ctx);
+/* Workspace bytes tm_ep_experts needs (zero it once with tm_workspace_init). */
+int64_t tm_ep_owner_workspace_bytes(const tm_ep_ctx *ctx);
+/* Copy the context's status word (TM_STATUS_* bits) to *host_status and clear
+ * it; synchronises `stream`. */
+int tm_ep_status(tm_ep_ctx *ctx, uint32_t *host_status, void *stream);
+/* Source: after tm_router_topk on `ws` for these `tokens`, send every routed
+ * (token, expert) row to the expert's owner.  topk_idx: the router's output. */
+int tm_ep_dispatch(tm_ep_ctx *ctx, const void *x, int64_t tokens, const int64_t *topk_idx, void *ws,
+                   int64_t ws_bytes, void *stream);
+/* Owner: wait for every source's rows, run this rank's experts on them (packed
+ * layout of tm_pack_experts for the n_experts/world local experts) and return
+ * each output row to its source. */
+int tm_ep_experts(tm_ep_ctx *ctx, const uint8_t *w13, const float *s13, const uint8_t *w2, const float *s2,
+                  void *owner_ws, int64_t owner_ws_bytes, void *stream);
+/* Source: wait for every owner's outputs, then out = residual + sum_k w * y in
+ * top-k order (residual may be NULL). */
+int tm_ep_combine(tm_ep_ctx *ctx, const void *topk_w, int64_t tokens, void *ws, int64_t ws_bytes,
+                  const void *residual, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -359,6 +359,13 @@ template <typename T> __host__ __device__ __forceinline__ T *ws_ptr(void *ws, in
   return reinterpret_cast<T *>(static_cast<char *>(ws) + off);
 }
 
+// The grouped GEMMs (gate/up + SwiGLU, down) of tm_moe_prefill_grouped
+// without the combine: per-slot expert outputs (act dtype, slot order) are
+// left in the workspace's ypart region.  The plan must already be in `ws`.
+int prefill_expert_outputs(const void *x, int64_t tokens, int hidden, int inter, int n_experts, int top_k,
+                           int act_dtype, const uint8_t *w13, const float *s13, const uint8_t *w2, const float *s2,
+                           void *ws, const WsLayout &L, cudaStream_t stream);
+
 constexpr int kMetaNActive = 0;
 constexpr int kMetaPairs = 1;
 constexpr int kMetaTokens = 2;

@@ -650,7 +650,15 @@ __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, cons
 __global__ void __launch_bounds__(256) k4_prep_x(const __nv_bfloat16 *x, const int *pair_slot, int H, int k,
                                                  __half *x16, float *slot_scale) {
   __shared__ float red[8];
+  __shared__ int s_used;
   const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int used = 0;
+    for (int r = 0; r < k; ++r) used |= __ldcg(pair_slot + (size_t)t * k + r) >= 0;
+    s_used = used;
+  }
+  __syncthreads();
+  if (!s_used) return;  // a row no slot reads (capacity rows of an expert-parallel owner)
   const __nv_bfloat16 *xr = x + (size_t)t * H;
   float m = 0.f;
   for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
@@ -695,6 +703,7 @@ struct PrefillLaunch {
   const void *x; int64_t T; int H, I, E, k;
   const void *topk_w; const uint8_t *w13; const float *s13; const uint8_t *w2; const float *s2;
   const void *residual; void *out; void *ws; const WsLayout *L; cudaStream_t s;
+  bool combine;  // false: stop after the down GEMM (per-slot outputs in the ypart region)
   template <typename TA> int run() {
     if constexpr (sizeof(TA) != 2) {
       return fail(TM_ERR_UNSUPPORTED, "tm_moe_prefill_grouped: fp32 activations are not supported (bf16, fp16)");
@@ -728,6 +737,7 @@ struct PrefillLaunch {
       if (rc) return rc;
       k4_gemm<TA, kPfDown><<<grid, kPfThreads, kPfSmem, s>>>(g);
       TM_LAUNCH_CHECK("k4_gemm down launch");
+      if (!combine) return TM_OK;
       k4_combine<TA><<<(unsigned)T, 256, 0, s>>>(y, (const TA *)topk_w, ws_ptr<int>(ws, L->pair_slot),
                                                    (const TA *)residual, (TA *)out, H, k);
       TM_LAUNCH_CHECK("k4_combine launch");
@@ -785,6 +795,19 @@ extern "C" int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden,
   int rc = ws_check(ws, ws_bytes, tokens, n_experts, top_k, hidden, inter, 0, &L);
   if (rc) return rc;
   PrefillLaunch f{x, tokens, hidden, inter, n_experts, top_k, topk_w, w13, s13, w2, s2, residual, out,
-                  ws, &L, as_stream(stream)};
+                  ws, &L, as_stream(stream), true};
   return dispatch_act(act_dtype, f);
 }
+
+namespace tmoe {
+int prefill_expert_outputs(const void *x, int64_t tokens, int hidden, int inter, int n_experts, int top_k,
+                           int act_dtype, const uint8_t *w13, const float *s13, const uint8_t *w2, const float *s2,
+                           void *ws, const WsLayout &L, cudaStream_t stream) {
+  TM_REQUIRE(hidden % 256 == 0 && hidden > 0 && hidden <= 128 * kPfMaxKBlocks, "hidden (%d) unsupported", hidden);
+  TM_REQUIRE(inter % 128 == 0 && inter > 0 && inter <= 128 * kPfMaxKBlocks, "inter (%d) unsupported", inter);
+  TM_REQUIRE(n_experts <= kPfMaxExperts, "n_experts %d > %d", n_experts, kPfMaxExperts);
+  PrefillLaunch f{x, tokens, hidden, inter, n_experts, top_k, nullptr, w13, s13, w2, s2, nullptr, nullptr,
+                  ws, &L, stream, false};
+  return dispatch_act(act_dtype, f);
+}
+}  // namespace tmoe

@@ -48,8 +48,24 @@ SIGNATURES = {
     "tm_combine_slots": (_i, [_p, _p, _p, _i64, _i, _i, _i, _p, _p, _p]),
     "tm_moe_decode_layer_noalloc": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                          _i, _p, _p, _p, _p, _p, _p, _p]),
+    "tm_ep_buffer_bytes": (_i64, [_i, _i64, _i, _i, _i, _i]),
+    "tm_ep_create": (_i, [_i, _i, _i, _i, _i, _i, _i, _i64, _p, C.POINTER(_p)]),
+    "tm_ep_connect": (_i, [_p, _p]),
+    "tm_ep_connect_ptrs": (_i, [_p, C.POINTER(_p)]),
+    "tm_ep_local_buffer": (_p, [_p]),
+    "tm_ep_set_timeout": (_i, [_p, _i64]),
+    "tm_ep_disconnect": (_i, [_p]),
+    "tm_ep_destroy": (_i, [_p]),
+    "tm_ep_owner_workspace_bytes": (_i64, [_p]),
+    "tm_ep_status": (_i, [_p, C.POINTER(C.c_uint32), _p]),
+    "tm_ep_dispatch": (_i, [_p, _p, _i64, _p, _p, _i64, _p]),
+    "tm_ep_experts": (_i, [_p, _p, _p, _p, _p, _p, _i64, _p]),
+    "tm_ep_combine": (_i, [_p, _p, _i64, _p, _i64, _p, _p, _p]),
 }
 TM_NOALLOC_SCRATCH_BYTES = 8 << 20
+TM_EP_MAX_RANKS = 8
+TM_EP_HANDLE_BYTES = 64
+TM_STATUS_TIMEOUT = 2
 
 _lock = threading.Lock()
 _lib = None

@@ -121,3 +121,99 @@ def cuda_functions(router_w: torch.Tensor, local_experts, top_k: int, n_experts:
         return ops.combine_slots(y_slots, r.w, r.pair_slot, out, residual)
 
     return route_fn, expert_fn, combine_fn
+
+
+class PeerExpertParallelMoE:
+    """Expert-parallel MoE layer over NVLink peer memory (the tm_ep_* entry
+    points of libturbomoe): dispatch, the owner's grouped GEMMs and the return
+    of the outputs are device kernels with bounded waits, so a call has no
+    collective, no host synchronisation and can be captured in a CUDA graph.
+
+    Every rank of `group` (one process per GPU of one node) constructs it with
+    its own shard `local_experts` (PackedExperts of experts
+    [rank * E/G, (rank + 1) * E/G)) - construction is collective (it exchanges
+    the buffers' IPC handles) - and calls `forward` in the same order.  Without
+    an initialised process group it runs as a single rank."""
+
+    def __init__(self, router_w: torch.Tensor, local_experts, top_k: int, max_tokens: int, group=None,
+                 timeout_s: float = 2.0):
+        import ctypes as C
+        from . import ops
+        from ._lib import TM_EP_HANDLE_BYTES, check, lib
+        self._C, self._ops, self._check, self._L = C, ops, check, lib()
+        single = not (dist.is_available() and dist.is_initialized())
+        self.group = group
+        self.G = 1 if single else dist.get_world_size(group)
+        self.rank = 0 if single else dist.get_rank(group)
+        E, H = router_w.shape
+        self.E, self.k, self.H, self.I = E, top_k, H, local_experts.inter
+        if E % self.G or local_experts.n_experts != E // self.G:
+            raise ValueError(f"{local_experts.n_experts} local experts do not match {E} over {self.G} ranks")
+        self.router_w = router_w.contiguous()
+        self.local = local_experts
+        self.max_tokens = max_tokens
+        dev = router_w.device
+        code = ops._code(router_w.dtype)
+        self.ctx = C.c_void_p()
+        handle = (C.c_char * TM_EP_HANDLE_BYTES)()
+        check(self._L.tm_ep_create(self.rank, self.G, E, top_k, H, self.I, code, max_tokens, handle,
+                                   C.byref(self.ctx)), "tm_ep_create")
+        mine = (bytes(handle), (E, top_k, H, self.I, code, max_tokens))
+        if single:
+            everyone = [mine]
+        else:
+            everyone = [None] * self.G
+            dist.all_gather_object(everyone, mine, group=group)
+        if any(s != mine[1] for _, s in everyone):
+            raise ValueError(f"ranks disagree on the expert-parallel shape: {[s for _, s in everyone]}")
+        check(self._L.tm_ep_connect(self.ctx, b"".join(h for h, _ in everyone)), "tm_ep_connect")
+        check(self._L.tm_ep_set_timeout(self.ctx, int(timeout_s * 1e9)), "tm_ep_set_timeout")
+        self.ws = ops.Workspace(dev, E, top_k, H, self.I, 0)
+        self.ws.ensure(max_tokens)
+        n = self._L.tm_ep_owner_workspace_bytes(self.ctx)
+        self.owner_ws = torch.empty(n, dtype=torch.uint8, device=dev)
+        check(self._L.tm_workspace_init(self.owner_ws.data_ptr(), n, ops._stream(self.owner_ws)), "tm_workspace_init")
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        ops, check, L = self._ops, self._check, self._L
+        x = x.contiguous()
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
+        idx, w = ops.router_topk(x, self.router_w, self.k, self.ws)
+        s = ops._stream(x)
+        buf = self.ws.buf
+        check(L.tm_ep_dispatch(self.ctx, x.data_ptr(), T, idx.data_ptr(), buf.data_ptr(), buf.numel(), s),
+              "tm_ep_dispatch")
+        le = self.local
+        check(L.tm_ep_experts(self.ctx, le.w13.data_ptr(), le.s13.data_ptr(), le.w2.data_ptr(), le.s2.data_ptr(),
+                              self.owner_ws.data_ptr(), self.owner_ws.numel(), s), "tm_ep_experts")
+        if out is None:
+            out = torch.empty_like(x)
+        res = residual.contiguous() if residual is not None else None
+        check(L.tm_ep_combine(self.ctx, w.data_ptr(), T, buf.data_ptr(), buf.numel(),
+                              res.data_ptr() if res is not None else None, out.data_ptr(), s), "tm_ep_combine")
+        return out
+
+    def status(self) -> int:
+        """TM_STATUS_* bits of the calls since the last status() (synchronises)."""
+        C, ops = self._C, self._ops
+        v = C.c_uint32(0)
+        self._check(self._L.tm_ep_status(self.ctx, C.byref(v), ops._stream(self.owner_ws)), "tm_ep_status")
+        o = C.c_uint32(0)
+        self._check(self._L.tm_workspace_status(self.owner_ws.data_ptr(), self.owner_ws.numel(), C.byref(o),
+                                                ops._stream(self.owner_ws)), "tm_workspace_status")
+        return int(v.value) | int(o.value) | self.ws.status()
+
+    def close(self):
+        """Collective: every rank, after its last forward."""
+        if self.ctx:
+            torch.cuda.synchronize()
+            if self.G > 1:
+                dist.barrier(group=self.group)
+            self._check(self._L.tm_ep_disconnect(self.ctx), "tm_ep_disconnect")
+            if self.G > 1:
+                dist.barrier(group=self.group)  # nobody maps a buffer that is freed
+            self._check(self._L.tm_ep_destroy(self.ctx), "tm_ep_destroy")
+            self.ctx = self._C.c_void_p()
