@@ -367,9 +367,12 @@ def run_ep(args, rank, world, local):
     """Expert-parallel batched decode: `--ep-tokens` sequences (one token each)
     split over the ranks, the 128 experts of every layer sharded over them;
     one step = the tokens through `--layers` MoE layers (dispatch / experts /
-    combine per layer).  Timed with CUDA events, max over ranks."""
+    combine per layer).  `--ep-impl peer` (default): the tm_ep_* kernels over
+    NVLink peer memory, the step captured in one CUDA graph; `nccl`: NCCL
+    all-to-all exchange with host-read row counts (eager).  Timed with CUDA
+    events, max over ranks."""
     from turbomoe import ops, synth
-    from turbomoe.ep import ExpertParallelMoE, cuda_functions
+    from turbomoe.ep import ExpertParallelMoE, PeerExpertParallelMoE, cuda_functions
     import torch.distributed as dist
     if world == 1 and not dist.is_initialized():
         dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % (29500 + os.getpid() % 1000),
@@ -380,6 +383,7 @@ def run_ep(args, rank, world, local):
     E, k, H, I = shape.experts, shape.top_k, shape.hidden, shape.inter
     E_loc = E // world
     T = args.ep_tokens // world
+    peer = args.ep_impl == "peer"
     layers = []
     for l in range(args.layers):
         lw = synth.make_layer(shape, SEED, l, device=dev)
@@ -388,40 +392,84 @@ def run_ep(args, rank, world, local):
                                          lw.down_s[sl])
         router_w = lw.router.to(torch.bfloat16).contiguous()
         del lw
-        layers.append(ExpertParallelMoE(E, k, *cuda_functions(router_w, local_experts, k, E, H, I)))
+        if peer:
+            layers.append(PeerExpertParallelMoE(router_w, local_experts, k, max_tokens=T))
+        else:
+            layers.append(ExpertParallelMoE(E, k, *cuda_functions(router_w, local_experts, k, E, H, I)))
     torch.cuda.empty_cache()
     x0 = synth.make_hidden(T, H, SEED + 100 + rank, rms_normalise=True, device=dev)
+    bufs = [torch.empty_like(x0) for _ in range(2)]
 
     def step(x):
-        for ep in layers:
-            x = ep.forward(x, residual=x)
+        for i, ep in enumerate(layers):
+            x = ep.forward(x, residual=x, out=bufs[i % 2]) if peer else ep.forward(x, residual=x)
         return x
 
     for _ in range(args.warmup):
         step(x0)
+    torch.cuda.synchronize()
+    eager_ms = None
+    run = lambda: step(x0)
+    graph = None
+    if peer:
+        barrier(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(args.steps):
+            step(x0)
+        ev1.record()
+        torch.cuda.synchronize()
+        eager_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step(x0)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y_graph = step(x0)
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        run = graph.replay
     torch.cuda.synchronize()
     barrier(world)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         ev0.record()
         for _ in range(args.steps):
-            y = step(x0)
+            y = run()
         ev1.record()
         torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    if peer:
+        y = y_graph
+        st = max_over_ranks(float(sum(ep.status() for ep in layers)), world)
+        assert st == 0, f"expert-parallel status {st}"
     assert torch.isfinite(y.float()).all(), "non-finite output"
-    sc, rc = layers[-1].last_counts
-    return {"metric": "expert-parallel batched decode tok/s, Qwen3-30B-A3B-FP8 MoE layers",
-            "value": round(T * world * args.steps / (ms / 1000.0), 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "e4m3 weights, bf16 act, fp32 math", "data": "synthetic (seeded weights, uniform routing)",
-            "config": {"workload": f"{args.ep_tokens} sequences x 1 token through {args.layers} MoE layers, "
-                                   f"experts sharded {E_loc} per GPU, all-to-all dispatch/combine (NCCL)",
-                       "tokens_per_rank": T, "experts_per_rank": E_loc, "parallelism": f"ep{world}"},
-            "rows_sent_last_layer_rank0": sc, "rows_recv_last_layer_rank0": rc,
-            "clocks": clk.summary()}
+    res = {"metric": "expert-parallel batched decode tok/s, Qwen3-30B-A3B-FP8 MoE layers",
+           "value": round(T * world * args.steps / (ms / 1000.0), 1), "unit": "tokens/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "e4m3 weights, bf16 act, fp32 math", "data": "synthetic (seeded weights, uniform routing)",
+           "config": {"workload": f"{args.ep_tokens} sequences x 1 token through {args.layers} MoE layers, "
+                                  f"experts sharded {E_loc} per GPU, " +
+                                  ("dispatch/return by NVLink peer stores (tm_ep_*), step in one CUDA graph"
+                                   if peer else "all-to-all dispatch/combine (NCCL), eager"),
+                      "tokens_per_rank": T, "experts_per_rank": E_loc, "parallelism": f"ep{world}",
+                      "ep_impl": args.ep_impl},
+           "us_per_layer": round(ms / args.steps / args.layers * 1000, 1),
+           "clocks": clk.summary()}
+    if peer:
+        res["eager_value"] = round(T * world * args.steps / (eager_ms / 1000.0), 1)
+        del graph
+        torch.cuda.synchronize()
+        for ep in layers:
+            ep.close()
+    else:
+        sc, rc = layers[-1].last_counts
+        res["rows_sent_last_layer_rank0"], res["rows_recv_last_layer_rank0"] = sc, rc
+    return res
 
 
 # ------------------------------------------------------- CPU reference ----
@@ -493,6 +541,8 @@ def main():
     ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
                     help="decode: batch-1 decode (replicas for N>1); ep: expert-parallel batched decode")
     ap.add_argument("--ep-tokens", type=int, default=256, help="ep workload: sequences over all ranks")
+    ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",
+                    help="ep workload: NVLink peer-memory kernels (tm_ep_*) or NCCL all-to-all")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
