@@ -319,6 +319,59 @@ def run_ours(args, rank, world, local):
                    "status": ws.status() | wsp.status()}
         assert torch.isfinite(outp.float()).all(), "non-finite prefill output"
 
+    # ---- Qwen3.5-shaped layer (256 experts, I 512, FP8 shared expert), 64 tokens ----
+    c3 = None
+    if args.c3_tokens > 0:
+        T3 = args.c3_tokens
+        sh3 = synth.QWEN35_LAYER
+        lw3 = synth.make_layer(sh3, SEED + 3, 0, device=dev)
+        ex3 = ops.pack_experts(lw3.gate, lw3.gate_s, lw3.up, lw3.up_s, lw3.down, lw3.down_s)
+        shx3 = ops.pack_experts(lw3.sh_gate, lw3.sh_gate_s, lw3.sh_up, lw3.sh_up_s, lw3.sh_down, lw3.sh_down_s)
+        r3 = lw3.router.to(torch.bfloat16).contiguous()
+        g3 = lw3.sh_router.to(torch.bfloat16).reshape(-1).contiguous()
+        del lw3
+        ws3 = ops.Workspace(dev, sh3.experts, sh3.top_k, sh3.hidden, sh3.inter, sh3.shared_inter)
+        ws3.ensure(T3)
+        x3 = synth.make_hidden(T3, sh3.hidden, SEED + 13, device=dev)
+        out3 = torch.empty_like(x3)
+
+        def call3():
+            idx3, w3 = ops.router_topk(x3, r3, sh3.top_k, ws3)
+            ops.moe_experts(x3, idx3, w3, ex3, ws3, shared=shx3, shared_gate_w=g3, residual=x3, out=out3)
+            return idx3
+
+        s3 = torch.cuda.Stream(device=dev)
+        s3.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s3):
+            for _ in range(2):
+                call3()
+        torch.cuda.current_stream().wait_stream(s3)
+        g3r = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g3r):
+            idx3 = call3()
+        for _ in range(3):
+            g3r.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            g3r.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us3 = e0.elapsed_time(e1) / 20 * 1000
+        U = int(torch.unique(idx3).numel())
+        e_bytes = 3 * sh3.inter * sh3.hidden
+        e_scales = 3 * (sh3.inter // 128) * (sh3.hidden // 128) * 4
+        b3 = (U + 1) * (e_bytes + e_scales) + sh3.experts * sh3.hidden * 2 + sh3.hidden * 2 + 2 * T3 * sh3.hidden * 2
+        hbm, _src = _peaks()
+        c3 = {"workload": f"one Qwen3.5-shaped MoE layer call (E 256, top-8, I 512, FP8 shared expert I 512) "
+                          f"with {T3} tokens: router + experts + shared expert + residual (CUDA graph)",
+              "us_per_layer": round(us3, 1), "unique_experts": U, "algorithmic_bytes": b3,
+              "hbm_gbs": round(b3 / (us3 * 1e-6) / 1e9, 1), "frac": round(b3 / (us3 * 1e-6) / 1e9 / hbm, 4),
+              "status": ws3.status()}
+        del g3r
+        assert torch.isfinite(out3.float()).all(), "non-finite C3 output"
+
     reps = max(5, args.steps)
     t_b = graph_time(False, False, reps)
     t_a = graph_time(True, False, reps)
@@ -359,6 +412,8 @@ def run_ours(args, rank, world, local):
     }
     if prefill is not None:
         res["prefill"] = prefill
+    if c3 is not None:
+        res["qwen35_layer"] = c3
     return res
 
 
@@ -538,6 +593,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="also time one prefill layer call of this many tokens (0 = skip)")
+    ap.add_argument("--c3-tokens", type=int, default=64,
+                    help="also time one Qwen3.5-shaped layer call (shared expert) of this many tokens (0 = skip)")
     ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
                     help="decode: batch-1 decode (replicas for N>1); ep: expert-parallel batched decode")
     ap.add_argument("--ep-tokens", type=int, default=256, help="ep workload: sequences over all ranks")

@@ -180,12 +180,18 @@ int tm_moe_decode_down_combine(int64_t tokens, int hidden, int inter, int n_expe
  * h and y are rounded to act dtype (as the reference's F.linear outputs are).
  * Needs the routing plan of tm_router_topk / tm_route_plan in `ws`; uses the
  * workspace's h and partial-output regions.  act_dtype bf16 or fp16;
- * hidden % 256 == 0, inter % 128 == 0, no shared expert (a shared expert runs
- * through the decode entry points).  |weight_scale_inv| must stay below 255
- * (the on-chip dequantisation scales by 2^120 (bf16) / 2^8 (fp16)). */
+ * hidden % 256 == 0, inter % 128 == 0.  Optional shared expert (Qwen3.5;
+ * moe.py:191-200): sh_w13/sh_s13/sh_w2/sh_s2 in the packed layout of one
+ * expert, shared_inter == inter, gate row sh_gate_w [hidden] act; it runs as
+ * one more group of the same GEMMs over every token and adds
+ * sigmoid(x . sh_gate_w) * y_sh after the routed sum (all NULL / 0 = none;
+ * needs n_experts > top_k).  |weight_scale_inv| must stay below 255 (the
+ * on-chip dequantisation scales by 2^120 (bf16) / 2^8 (fp16)). */
 int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden, int inter, int n_experts,
                            int top_k, int act_dtype, const void *topk_w, const uint8_t *w13,
                            const float *s13, const uint8_t *w2, const float *s2,
+                           const uint8_t *sh_w13, const float *sh_s13, const uint8_t *sh_w2,
+                           const float *sh_s2, int shared_inter, const void *sh_gate_w,
                            const void *residual, void *out, void *ws, int64_t ws_bytes,
                            void *stream);
 

@@ -163,3 +163,64 @@ def test_prefill_qwen3_layer_vs_reference_golden():
     sub = rows[:64]
     ref = emulate(lw, x[sub], idx[sub], w[sub])
     _check(out[sub], ref, "q3_c1 vs emulation")
+
+
+def emulate_shared(lw, x):
+    """The shared expert's term as the kernels compute it: one more group of
+    the same GEMMs over every token, times sigmoid(x . gate) with F.linear's
+    output and the sigmoid each rounded to the act dtype (moe.py:191-200)."""
+    dt = x.dtype
+    xf = x.float()
+    wg = gateup_weight(lw.sh_gate, lw.sh_gate_s, dt)
+    wu = gateup_weight(lw.sh_up, lw.sh_up_s, dt)
+    wd = O.dequantize_weight(lw.sh_down, lw.sh_down_s, dt).float()
+    h = (F.silu(xf @ wg.T) * (xf @ wu.T)).to(dt).float()
+    y = (h @ wd.T).to(dt).float()
+    logit = (xf @ lw.sh_router.to(dt).float().reshape(-1)).to(dt).float()
+    score = torch.sigmoid(logit).to(dt).float()
+    return score.unsqueeze(1) * y
+
+
+@pytest.mark.parametrize("dt,T", [(torch.bfloat16, 64), (torch.bfloat16, 17), (torch.float16, 40)])
+def test_prefill_shared_expert(dt, T):
+    """Qwen3.5-style layer (FP8 shared expert of the routed experts' size):
+    the shared expert runs as one more group of the grouped GEMMs; the output
+    matches the CPU restatement of that arithmetic and, within the
+    north-star bar, the fp32 oracle of the reference's layer."""
+    from turbomoe import ops, synth
+    from gpu_util import oracle_fp32
+    shape = synth.MoEShape(512, 256, 16, 4, 256)
+    lw = synth.make_layer(shape, 31 + T, 0)
+    x = synth.make_hidden(T, 512, 7 + T, dtype=dt)
+    layer = O.OracleLayer(lw, dt)
+    idx, w = O.compute_routing(x, layer.router, shape.top_k)
+    res = torch.randn(T, 512, generator=torch.Generator().manual_seed(T)).to(dt)
+    experts, shared, gate = packed_from_layer(lw)
+    ws = workspace_for(shape)
+    xd, idd, wd = x.cuda(), idx.cuda(), w.to(dt).cuda()
+    ops.route_plan(idd, shape.experts, ws)
+    ws.ensure(T, shape.top_k)
+    assert ops.prefill_eligible(T, dt, experts, shared, shape.top_k)
+    out = torch.empty_like(xd)
+    ops.moe_prefill(xd, wd, experts, ws, out, res.cuda(), shared, gate.to(dt).cuda())
+    assert ws.status() == 0
+    out = out.cpu()
+    # routed part as emulate() (unrounded), plus the shared term, in the kernels' order
+    dtp = x.dtype
+    xf = x.float()
+    k = idx.shape[1]
+    ypair = torch.zeros(T, k, 512)
+    for e in torch.unique(idx).tolist():
+        t, r = torch.where(idx == e)
+        wg = gateup_weight(lw.gate[e], lw.gate_s[e], dtp)
+        wu = gateup_weight(lw.up[e], lw.up_s[e], dtp)
+        wdn = O.dequantize_weight(lw.down[e], lw.down_s[e], dtp).float()
+        h = (F.silu(xf[t] @ wg.T) * (xf[t] @ wu.T)).to(dtp).float()
+        ypair[t, r] = (h @ wdn.T).to(dtp).float()
+    acc = torch.zeros(T, 512)
+    for r in range(k):
+        acc = acc + w.to(dtp)[:, r].float().unsqueeze(1) * ypair[:, r]
+    want = (acc + emulate_shared(lw, x) + res.float()).to(dtp)
+    _check(out, want, f"shared {dt} T={T}", min_equal=0.8)
+    ref32 = oracle_fp32(lw, x, idx, w) + res.float()
+    assert_close(out.float(), ref32, 2e-2, 0.9995, f"shared {dt} T={T} vs fp32 oracle")

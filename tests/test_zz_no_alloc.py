@@ -31,11 +31,15 @@ def _layer(shape, seed):
 
 
 def _workspace_path(shape, lw, experts, shared, gate, x, residual):
+    """The same three kernels through the workspace entry points (K1, K2, K3:
+    the no-alloc call never uses the grouped GEMMs)."""
     from turbomoe import ops
     ws = workspace_for(shape)
     idx, w = ops.router_topk(x, lw.router.cuda().to(x.dtype), shape.top_k, ws)
-    out = ops.moe_experts(x, idx, w, experts, ws, shared=shared,
-                          shared_gate_w=gate.to(x.dtype) if gate is not None else None, residual=residual)
+    ws.ensure(x.shape[0], shape.top_k)
+    out = torch.empty_like(x)
+    ops.moe_gateup(x, shape.top_k, experts, ws, shared, gate.to(x.dtype) if gate is not None else None)
+    ops.moe_down_combine(w, experts, ws, out, shared, residual)
     return idx, w, out
 
 

@@ -135,7 +135,12 @@ template <typename TA> struct PfArgs {
   const int4 *act_rec; // {expert, count, first slot, 0} per active expert
   const int *slot_token;
   uint32_t *status;
+  // optional shared expert (same inter size): one more tile group with every
+  // token, slots [P, P + T), token of slot s = s - P; expert id E marks it
+  const uint8_t *sh_w;
+  const float *sh_s;
   int H, I, E;
+  int P, T, has_shared;
 };
 
 struct PfTile {
@@ -145,14 +150,15 @@ struct PfTile {
 // Tile u of the call: active experts in ascending order, then the weight-row
 // block, then the token tile (fastest), so CTAs working at the same time on
 // one expert's token tiles share its weight stream through L2.
-__device__ __forceinline__ PfTile pf_tile(int u, const int *prefix, int na, const int4 *act_rec, int MT) {
+__device__ __forceinline__ PfTile pf_tile(int u, const int *prefix, int na, const int4 *act_rec, int MT,
+                                          int na_routed, int4 shared_rec) {
   int lo = 0, hi = na - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (prefix[mid] <= u) lo = mid;
     else hi = mid - 1;
   }
-  const int4 r = __ldcg(act_rec + lo);
+  const int4 r = lo >= na_routed ? shared_rec : __ldcg(act_rec + lo);
   const int cnt = max(r.y, 1);
   const int nt = (cnt + kPfNMax - 1) / kPfNMax;
   const int local = u - prefix[lo];
@@ -256,13 +262,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   __shared__ __align__(8) uint64_t a_full[kPfAStages], a_empty[kPfAStages];
   __shared__ __align__(8) uint64_t b_full[kPfBStages], b_empty[kPfBStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
-  __shared__ int prefix[kPfMaxExperts + 1];
+  __shared__ int prefix[kPfMaxExperts + 2];  // active experts (+ the shared expert) + end
   __shared__ int4 tl_a[kPfMaxLocalTiles];  // {e, slot0, nvalid, npad}
   __shared__ int tl_mt[kPfMaxLocalTiles];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
   __shared__ volatile int conv_done;       // K slices the converters have finished (prefetch throttle)
-  __shared__ int s_na, s_tiles;
+  __shared__ int s_na, s_na_r, s_tiles;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool gate_up = kMode == kPfGateUp;
@@ -277,14 +283,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   const int KB = K / 128;
 
   // ---- tile table: prefix[a] = first tile of active expert a ----
+  const int4 shared_rec = make_int4(a.E, a.T, a.P, 0);
   if (warp == 0) {
-    const int na = min(__ldcg(a.meta + kMetaNActive), a.E);
+    const int na_r = min(__ldcg(a.meta + kMetaNActive), a.E);
+    const int na = na_r + (a.has_shared ? 1 : 0);
     int run = 0;
     for (int base = 0; base < na; base += 32) {
       const int i = base + lane;
       int v = 0;
       if (i < na) {
-        const int cnt = max(__ldcg(&a.act_rec[i].y), 1);
+        const int cnt = max(i >= na_r ? a.T : __ldcg(&a.act_rec[i].y), 1);
         v = MT * ((cnt + kPfNMax - 1) / kPfNMax);
       }
       int incl = v;
@@ -299,19 +307,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
     if (lane == 0) {
       prefix[na] = run;
       s_na = na;
+      s_na_r = na_r;
       s_tiles = run;
       abort_flag = 0;
       conv_done = 0;
     }
   }
   __syncthreads();
-  const int na = s_na, tiles = s_tiles;
+  const int na = s_na, na_r = s_na_r, tiles = s_tiles;
   if ((int)blockIdx.x >= tiles) return;  // CTA-uniform
   const int n_local = (tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
   if (warp == 0) {
     for (int j = lane; j < min(n_local, kPfMaxLocalTiles); j += 32) {
-      const PfTile t = pf_tile(blockIdx.x + j * gridDim.x, prefix, na, a.act_rec, MT);
+      const PfTile t = pf_tile(blockIdx.x + j * gridDim.x, prefix, na, a.act_rec, MT, na_r, shared_rec);
       tl_a[j] = make_int4(t.e, t.slot0, t.nvalid, t.npad);
       tl_mt[j] = t.mt;
     }
@@ -349,7 +358,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
       t.e = v.x; t.slot0 = v.y; t.nvalid = v.z; t.npad = v.w; t.mt = tl_mt[j];
       return t;
     }
-    return pf_tile(blockIdx.x + j * gridDim.x, prefix, na, a.act_rec, MT);
+    return pf_tile(blockIdx.x + j * gridDim.x, prefix, na, a.act_rec, MT, na_r, shared_rec);
   };
   // Raw slice (tile t, stage kt) of weight rows: gate/up = 8 row groups x 2 KB
   // (4 chunks x gate,up x 16 rows x 16 B), down = 16 row groups x 1 KB.
@@ -357,8 +366,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   const uint32_t gbytes = gate_up ? 2048 : 1024;
   const size_t gstride = gate_up ? (size_t)32 * a.H : (size_t)16 * a.I;
   auto slice_src = [&](const PfTile &t, int kt) -> const uint8_t * {
-    return gate_up ? a.w + (size_t)t.e * 2 * a.I * a.H + (size_t)(t.mt * 8) * 32 * a.H + (size_t)kt * 4 * 512
-                   : a.w + (size_t)t.e * a.H * a.I + (size_t)(t.mt * 16) * 16 * a.I + (size_t)kt * 4 * 256;
+    const bool sh = t.e == a.E;
+    return gate_up ? (sh ? a.sh_w : a.w + (size_t)t.e * 2 * a.I * a.H) + (size_t)(t.mt * 8) * 32 * a.H +
+                         (size_t)kt * 4 * 512
+                   : (sh ? a.sh_w : a.w + (size_t)t.e * a.H * a.I) + (size_t)(t.mt * 16) * 16 * a.I +
+                         (size_t)kt * 4 * 256;
   };
 
   if (warp == kPfWPre) {
@@ -447,7 +459,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
 #pragma unroll
       for (int q = 0; q < kPfNMax / 8; ++q) {
         const int slot = t.slot0 + min(8 * q + rsub, t.nvalid - 1);
-        rowv[q] = gate_up ? __ldcg(a.slot_token + slot) : slot;
+        rowv[q] = !gate_up ? slot : slot >= a.P ? slot - a.P : __ldcg(a.slot_token + slot);
       }
       for (int kt = 0; kt < nk; ++kt, ++i) {
         const int bs = i % kPfBStages;
@@ -485,6 +497,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
                                    : (size_t)(h * 8 + (m >> 4)) * 16 * a.I + (m & 15) * 16;
     const int cstride = gate_up ? 512 : 256;
     auto scale_ptr = [&](const PfTile &t) -> const float * {
+      if (t.e == a.E)
+        return gate_up ? a.sh_s + ((size_t)t.mt * 2 + h) * KB : a.sh_s + ((size_t)t.mt * 2 + h) * (a.I / 128);
       return gate_up ? a.s + ((size_t)(t.e * (a.I / 128) + t.mt) * 2 + h) * KB
                      : a.s + ((size_t)t.e * (a.H / 128) + t.mt * 2 + h) * (a.I / 128);
     };
@@ -614,7 +628,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
 // out[t] = residual[t] + sum_r w[t,r] * y[slot(t,r)] (top-k order, fp32).
 template <typename TA>
 __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, const int *pair_slot, const TA *residual,
-                                                  TA *out, int H, int k) {
+                                                  TA *out, int H, int k, const float *sh_w, int sh_slot0) {
   const int t = blockIdx.x;
   for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -626,6 +640,13 @@ __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, cons
       const TA *yv = reinterpret_cast<const TA *>(&v);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = fmaf(wr, Act<TA>::to_f(yv[j]), acc[j]);
+    }
+    if (sh_w) {  // gated shared expert (moe.py:200): after the routed sum
+      const float ws = __ldcg(sh_w + t);
+      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(y + (size_t)(sh_slot0 + t) * H + o));
+      const TA *yv = reinterpret_cast<const TA *>(&v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = fmaf(ws, Act<TA>::to_f(yv[j]), acc[j]);
     }
     uint4 res;
     TA *rv = reinterpret_cast<TA *>(&res);
@@ -642,51 +663,79 @@ __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, cons
   }
 }
 
-// bf16 activations only: x[t] -> f16 x16[t] = x[t] * 2^-s_t with s_t from the
-// row's max |x| (exact for bf16 values: 8 significant bits into f16's 11, the
-// row maximum scaled into [2^13, 2^14)), and for each of the token's k slots
-// slot_scale = 2^(s_t - 8), which undoes the shift and the weights' 2^8 in the
-// gate/up epilogue.  One CTA per token.
-__global__ void __launch_bounds__(256) k4_prep_x(const __nv_bfloat16 *x, const int *pair_slot, int H, int k,
-                                                 __half *x16, float *slot_scale) {
-  __shared__ float red[8];
+// Per token, one CTA:
+//  * bf16 activations (x16 != NULL): x[t] -> f16 x16[t] = x[t] * 2^-s_t with
+//    s_t from the row's max |x| (exact for bf16 values: 8 significant bits into
+//    f16's 11, the row maximum scaled into [2^13, 2^14)), and for each of the
+//    token's slots (its k routed ones and, with a shared expert, slot
+//    sh_slot0 + t) slot_scale = 2^(s_t - 8), which undoes the shift and the
+//    weights' 2^8 in the gate/up epilogue;
+//  * with a shared expert (sh_gate_w != NULL): its gate score
+//    sh_w[t] = sigmoid(x[t] . sh_gate_w), F.linear's output and the sigmoid
+//    each rounded to the act dtype (moe.py:196-198).
+template <typename TA>
+__global__ void __launch_bounds__(256) k4_prep(const TA *x, const int *pair_slot, int H, int k, __half *x16,
+                                               float *slot_scale, const TA *sh_gate_w, float *sh_w, int sh_slot0) {
+  __shared__ float red[8], redg[8];
   __shared__ int s_used;
   const int t = blockIdx.x;
   if (threadIdx.x == 0) {
-    int used = 0;
+    int used = sh_gate_w != nullptr;
     for (int r = 0; r < k; ++r) used |= __ldcg(pair_slot + (size_t)t * k + r) >= 0;
     s_used = used;
   }
   __syncthreads();
   if (!s_used) return;  // a row no slot reads (capacity rows of an expert-parallel owner)
-  const __nv_bfloat16 *xr = x + (size_t)t * H;
-  float m = 0.f;
+  const TA *xr = x + (size_t)t * H;
+  float m = 0.f, gl = 0.f;
   for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
     const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(xr + o));
-    const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(&v);
+    const TA *p = reinterpret_cast<const TA *>(&v);
+    if (sh_gate_w) {
+      const uint4 gv = __ldg(reinterpret_cast<const uint4 *>(sh_gate_w + o));
+      const TA *gp = reinterpret_cast<const TA *>(&gv);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(__bfloat162float(p[j])));
+      for (int j = 0; j < 8; ++j) gl = fmaf(Act<TA>::to_f(p[j]), Act<TA>::to_f(gp[j]), gl);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(Act<TA>::to_f(p[j])));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    gl += __shfl_xor_sync(0xffffffffu, gl, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[threadIdx.x >> 5] = m;
+    redg[threadIdx.x >> 5] = gl;
+  }
   __syncthreads();
   m = red[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+  gl = redg[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+    m = fmaxf(m, red[w]);
+    gl += redg[w];
+  }
+  if (sh_gate_w && threadIdx.x == 0) {
+    const float logit = Act<TA>::round(gl);
+    sh_w[t] = Act<TA>::round(1.0f / (1.0f + __expf(-logit)));
+  }
+  if (!x16) return;
   const int sh = f16_shift(m);
   for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
     const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(xr + o));
-    const __nv_bfloat16 *p = reinterpret_cast<const __nv_bfloat16 *>(&v);
+    const TA *p = reinterpret_cast<const TA *>(&v);
     uint4 r;
     __half *q = reinterpret_cast<__half *>(&r);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) q[j] = __float2half_rn(ldexpf(__bfloat162float(p[j]), -sh));
+    for (int j = 0; j < 8; ++j) q[j] = __float2half_rn(ldexpf(Act<TA>::to_f(p[j]), -sh));
     *reinterpret_cast<uint4 *>(x16 + (size_t)t * H + o) = r;
   }
   if ((int)threadIdx.x < k) {
     const int s = __ldcg(pair_slot + (size_t)t * k + threadIdx.x);
     if (s >= 0) slot_scale[s] = ldexpf(1.f, sh - 8);
   }
+  if (sh_gate_w && threadIdx.x == 32) slot_scale[sh_slot0 + t] = ldexpf(1.f, sh - 8);
 }
 
 static int num_sms() {
@@ -704,42 +753,56 @@ struct PrefillLaunch {
   const void *topk_w; const uint8_t *w13; const float *s13; const uint8_t *w2; const float *s2;
   const void *residual; void *out; void *ws; const WsLayout *L; cudaStream_t s;
   bool combine;  // false: stop after the down GEMM (per-slot outputs in the ypart region)
+  // optional shared expert (inter size I): packed weights and the gate row [H]
+  const uint8_t *sh_w13; const float *sh_s13; const uint8_t *sh_w2; const float *sh_s2; const void *sh_gate_w;
   template <typename TA> int run() {
     if constexpr (sizeof(TA) != 2) {
       return fail(TM_ERR_UNSUPPORTED, "tm_moe_prefill_grouped: fp32 activations are not supported (bf16, fp16)");
     } else {
+      const bool shared = sh_w13 != nullptr;
+      const int64_t P = T * k;
       PfArgs<TA> g;
       g.meta = ws_ptr<int>(ws, L->meta);
       g.act_rec = ws_ptr<int4>(ws, L->act_rec);
       g.slot_token = ws_ptr<int>(ws, L->slot_token);
       g.status = ws_ptr<uint32_t>(ws, L->status);
       g.H = H; g.I = I; g.E = E;
-      TA *h = ws_ptr<TA>(ws, L->h);        // [P][I] act dtype (region sized for fp32)
-      TA *y = ws_ptr<TA>(ws, L->ypart);    // [P][H] act dtype
+      g.P = (int)P; g.T = (int)T; g.has_shared = shared ? 1 : 0;
+      g.sh_w = sh_w13; g.sh_s = sh_s13;
+      // slots: routed [0, P), shared [P, P + T)
+      TA *h = ws_ptr<TA>(ws, L->h);        // [P (+T)][I] act dtype (region sized for P x I fp32)
+      TA *y = ws_ptr<TA>(ws, L->ypart);    // [P (+T)][H] act dtype (region sized for (P + T) x H fp32)
+      float *sh_w = ws_ptr<float>(ws, L->sh_w);  // [T]
       const int grid = num_sms();
       g.act = (const TA *)x; g.w = w13; g.s = s13; g.out = h; g.slot_scale = nullptr;
       if constexpr (PfConv<TA>::kFmt == 1) {
-        // bf16: the gate/up GEMM runs on f16 operands (x16 after y in the partial-output region)
-        __half *x16 = reinterpret_cast<__half *>(reinterpret_cast<char *>(y) + (size_t)T * k * H * sizeof(TA));
-        float *slot_scale = ws_ptr<float>(ws, L->logits);  // [P] (the region holds T * E >= P floats)
-        k4_prep_x<<<(unsigned)T, 256, 0, s>>>((const __nv_bfloat16 *)x, ws_ptr<int>(ws, L->pair_slot), H, k, x16,
-                                               slot_scale);
-        TM_LAUNCH_CHECK("k4_prep_x launch");
+        // bf16: the gate/up GEMM runs on f16 operands (x16 after the slots' outputs in the ypart region)
+        __half *x16 = reinterpret_cast<__half *>(reinterpret_cast<char *>(y) + (size_t)(P + T) * H * sizeof(TA));
+        float *slot_scale = ws_ptr<float>(ws, L->logits);  // [P + T] (the region holds T * E floats)
+        k4_prep<TA><<<(unsigned)T, 256, 0, s>>>((const TA *)x, ws_ptr<int>(ws, L->pair_slot), H, k, x16, slot_scale,
+                                                shared ? (const TA *)sh_gate_w : nullptr, sh_w, (int)P);
+        TM_LAUNCH_CHECK("k4_prep launch");
         g.act = (const TA *)x16;
         g.slot_scale = slot_scale;
+      } else if (shared) {
+        k4_prep<TA><<<(unsigned)T, 256, 0, s>>>((const TA *)x, ws_ptr<int>(ws, L->pair_slot), H, k, nullptr, nullptr,
+                                                (const TA *)sh_gate_w, sh_w, (int)P);
+        TM_LAUNCH_CHECK("k4_prep launch");
       }
       int rc = ensure_smem(reinterpret_cast<const void *>(k4_gemm<TA, kPfGateUp>), kPfSmem);
       if (rc) return rc;
       k4_gemm<TA, kPfGateUp><<<grid, kPfThreads, kPfSmem, s>>>(g);
       TM_LAUNCH_CHECK("k4_gemm gate/up launch");
       g.act = h; g.w = w2; g.s = s2; g.out = y; g.slot_scale = nullptr;
+      g.sh_w = sh_w2; g.sh_s = sh_s2;
       rc = ensure_smem(reinterpret_cast<const void *>(k4_gemm<TA, kPfDown>), kPfSmem);
       if (rc) return rc;
       k4_gemm<TA, kPfDown><<<grid, kPfThreads, kPfSmem, s>>>(g);
       TM_LAUNCH_CHECK("k4_gemm down launch");
       if (!combine) return TM_OK;
       k4_combine<TA><<<(unsigned)T, 256, 0, s>>>(y, (const TA *)topk_w, ws_ptr<int>(ws, L->pair_slot),
-                                                   (const TA *)residual, (TA *)out, H, k);
+                                                   (const TA *)residual, (TA *)out, H, k,
+                                                   shared ? sh_w : nullptr, (int)P);
       TM_LAUNCH_CHECK("k4_combine launch");
       return TM_OK;
     }
@@ -759,7 +822,7 @@ struct CombineLaunch {
       return fail(TM_ERR_UNSUPPORTED, "tm_combine_slots: act dtype must be bf16 or fp16");
     } else {
       k4_combine<TA><<<(unsigned)T, 256, 0, s>>>((const TA *)y, (const TA *)w, pair_slot, (const TA *)residual,
-                                                   (TA *)out, H, k);
+                                                   (TA *)out, H, k, nullptr, 0);
       TM_LAUNCH_CHECK("k4_combine launch");
       return TM_OK;
     }
@@ -780,9 +843,20 @@ extern "C" int tm_combine_slots(const void *y, const void *topk_w, const int32_t
 
 extern "C" int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden, int inter, int n_experts,
                                       int top_k, int act_dtype, const void *topk_w, const uint8_t *w13,
-                                      const float *s13, const uint8_t *w2, const float *s2, const void *residual,
-                                      void *out, void *ws, int64_t ws_bytes, void *stream) {
+                                      const float *s13, const uint8_t *w2, const float *s2, const uint8_t *sh_w13,
+                                      const float *sh_s13, const uint8_t *sh_w2, const float *sh_s2,
+                                      int shared_inter, const void *sh_gate_w, const void *residual, void *out,
+                                      void *ws, int64_t ws_bytes, void *stream) {
   TM_REQUIRE(x && topk_w && w13 && s13 && w2 && s2 && out, "null pointer");
+  const bool shared = sh_w13 != nullptr;
+  TM_REQUIRE(!shared || (sh_s13 && sh_w2 && sh_s2 && sh_gate_w), "shared expert: every pointer or none");
+  if (shared) {
+    TM_REQUIRE(shared_inter == inter, "shared expert inter %d != inter %d (the grouped GEMMs need one size)",
+               shared_inter, inter);
+    TM_REQUIRE(n_experts > top_k, "shared expert needs n_experts > top_k (slot scale region)");
+    TM_REQUIRE(aligned(sh_w13, 16) && aligned(sh_w2, 16) && aligned(sh_gate_w, 16),
+               "shared weights must be 16-byte aligned");
+  }
   TM_REQUIRE(hidden % 256 == 0 && hidden > 0 && hidden <= 128 * kPfMaxKBlocks,
              "hidden (%d) must be a positive multiple of 256, at most %d", hidden, 128 * kPfMaxKBlocks);
   TM_REQUIRE(inter % 128 == 0 && inter > 0 && inter <= 128 * kPfMaxKBlocks,
@@ -792,10 +866,13 @@ extern "C" int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden,
                  (!residual || aligned(residual, 16)),
              "x, weights, residual and out must be 16-byte aligned");
   WsLayout L;
-  int rc = ws_check(ws, ws_bytes, tokens, n_experts, top_k, hidden, inter, 0, &L);
+  int rc = ws_check(ws, ws_bytes, tokens, n_experts, top_k, hidden, inter, shared ? shared_inter : 0, &L);
   if (rc) return rc;
   PrefillLaunch f{x, tokens, hidden, inter, n_experts, top_k, topk_w, w13, s13, w2, s2, residual, out,
                   ws, &L, as_stream(stream), true};
+  if (shared) {
+    f.sh_w13 = sh_w13; f.sh_s13 = sh_s13; f.sh_w2 = sh_w2; f.sh_s2 = sh_s2; f.sh_gate_w = sh_gate_w;
+  }
   return dispatch_act(act_dtype, f);
 }
 
@@ -807,7 +884,7 @@ int prefill_expert_outputs(const void *x, int64_t tokens, int hidden, int inter,
   TM_REQUIRE(inter % 128 == 0 && inter > 0 && inter <= 128 * kPfMaxKBlocks, "inter (%d) unsupported", inter);
   TM_REQUIRE(n_experts <= kPfMaxExperts, "n_experts %d > %d", n_experts, kPfMaxExperts);
   PrefillLaunch f{x, tokens, hidden, inter, n_experts, top_k, nullptr, w13, s13, w2, s2, nullptr, nullptr,
-                  ws, &L, stream, false};
+                  ws, &L, stream, false, nullptr, nullptr, nullptr, nullptr, nullptr};
   return dispatch_act(act_dtype, f);
 }
 }  // namespace tmoe

@@ -305,21 +305,35 @@ def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out:
 PREFILL_MIN_TOKENS = 16
 
 
-def prefill_eligible(T: int, dtype, packed: PackedExperts, shared) -> bool:
-    return (T >= PREFILL_MIN_TOKENS and shared is None and dtype in (torch.bfloat16, torch.float16)
-            and packed.hidden % 256 == 0)
+def prefill_eligible(T: int, dtype, packed: PackedExperts, shared, top_k: int = 8) -> bool:
+    """Whether a call of T tokens runs on the tcgen05 grouped GEMMs (K4): 16-bit
+    activations, hidden % 256 == 0, and a shared expert (if any) of the routed
+    experts' inter size."""
+    if shared is not None and (shared.inter != packed.inter or packed.n_experts <= top_k):
+        return False
+    return T >= PREFILL_MIN_TOKENS and dtype in (torch.bfloat16, torch.float16) and packed.hidden % 256 == 0
 
 
 def moe_prefill(x: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Workspace, out: torch.Tensor,
-                residual: torch.Tensor | None = None):
-    """K4: grouped-GEMM expert FFN + combine for the plan already in ``ws``."""
+                residual: torch.Tensor | None = None, shared: PackedExperts | None = None,
+                shared_gate_w: torch.Tensor | None = None):
+    """K4: grouped-GEMM expert FFN (+ gated shared expert) + combine for the
+    plan already in ``ws``."""
     T, H = x.shape
     k = w.shape[1]
+    if shared is not None and shared_gate_w is None:
+        raise TurboMoEError("shared expert needs its gate weight")
+    if shared is not None and ws.Is < shared.inter:
+        raise TurboMoEError("workspace was sized without the shared expert")
     buf = ws.buf
+    gate = shared_gate_w.reshape(-1).to(x.dtype).contiguous() if shared is not None else None
+    sh = (shared.w13.data_ptr(), shared.s13.data_ptr(), shared.w2.data_ptr(), shared.s2.data_ptr(), shared.inter,
+          gate.data_ptr()) if shared is not None else (None, None, None, None, 0, None)
     check(lib().tm_moe_prefill_grouped(x.data_ptr(), T, H, packed.inter, packed.n_experts, k, _code(x.dtype),
                                        w.data_ptr(), packed.w13.data_ptr(), packed.s13.data_ptr(),
-                                       packed.w2.data_ptr(), packed.s2.data_ptr(), _ptr(residual), out.data_ptr(),
-                                       buf.data_ptr(), buf.numel(), _stream(x)), "tm_moe_prefill_grouped")
+                                       packed.w2.data_ptr(), packed.s2.data_ptr(), *sh, _ptr(residual),
+                                       out.data_ptr(), buf.data_ptr(), buf.numel(), _stream(x)),
+          "tm_moe_prefill_grouped")
 
 
 def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Workspace,
@@ -340,8 +354,9 @@ def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: Pac
     w = w.contiguous()
     if out is None:
         out = torch.empty_like(x)
-    if prefill_eligible(T, x.dtype, packed, shared):
-        moe_prefill(x, w, packed, ws, out, residual.contiguous() if residual is not None else None)
+    if prefill_eligible(T, x.dtype, packed, shared, k):
+        moe_prefill(x, w, packed, ws, out, residual.contiguous() if residual is not None else None, shared,
+                    shared_gate_w)
         return out
     moe_gateup(x, k, packed, ws, shared, shared_gate_w)
     moe_down_combine(w, packed, ws, out, shared, residual.contiguous() if residual is not None else None)
