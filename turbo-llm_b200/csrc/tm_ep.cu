@@ -47,8 +47,9 @@ namespace tmoe {
 
 constexpr int kEpMaxRanks = TM_EP_MAX_RANKS;
 constexpr int kEpThreads = 256;
-constexpr int kEpDispatchCTAs = 16;  // per owner rank
-constexpr int kEpReturnCTAs = 148;
+constexpr int kEpWarps = kEpThreads / 32;
+constexpr int kEpCopyCTAs = 296;      // row copies: two CTAs per SM, one warp per row
+constexpr int kEpRowVecs = 8;         // 16-byte vectors a lane keeps in flight per row (H <= 2048 bf16: all)
 constexpr uint64_t kEpDefaultTimeoutNs = 2000000000ull;
 
 struct EpLayout {
@@ -123,12 +124,31 @@ __device__ __forceinline__ uint64_t ep_next(const EpDev &d) {
   return *reinterpret_cast<volatile uint64_t *>(d.local + d.L.epoch) + 1;
 }
 
-// Source: send the rows of every owner's slot range.  grid (kEpDispatchCTAs, G).
+// One warp copies one row of nv 16-byte vectors (local or peer memory): every
+// load of a batch is issued before its stores.
+__device__ __forceinline__ void ep_copy_row(uint4 *dst, const uint4 *src, int nv, int lane) {
+  for (int b = 0; b < nv; b += 32 * kEpRowVecs) {
+    uint4 v[kEpRowVecs];
+#pragma unroll
+    for (int u = 0; u < kEpRowVecs; ++u) {
+      const int i = b + u * 32 + lane;
+      if (i < nv) v[u] = __ldcg(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kEpRowVecs; ++u) {
+      const int i = b + u * 32 + lane;
+      if (i < nv) dst[i] = v[u];
+    }
+  }
+}
+
+// Source: send the rows of every owner's slot range, one warp per row.
+// grid (CTAs per owner, G).
 template <typename TA>
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch(EpDev d, const TA *x, const int64_t *idx,
                                                           const int *offsets, const int *slot_token,
                                                           const int *slot_pair) {
-  const int tid = threadIdx.x, o = blockIdx.y;
+  const int tid = threadIdx.x, o = blockIdx.y, lane = tid & 31;
   const uint64_t ep = ep_next(d);
   const int s0 = __ldcg(offsets + o * d.E_loc), s1 = __ldcg(offsets + (o + 1) * d.E_loc);
   int n = s1 - s0;
@@ -139,13 +159,12 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch(EpDev d, const TA *x, 
   TA *dst_rows = reinterpret_cast<TA *>(d.peer[o] + d.L.rows) + (int64_t)d.rank * d.cap * d.H;
   int2 *dst_meta = reinterpret_cast<int2 *>(d.peer[o] + d.L.meta) + (int64_t)d.rank * d.cap;
   const int nv = d.H * (int)sizeof(TA) / 16;
-  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+  for (int i = blockIdx.x * kEpWarps + (tid >> 5); i < n; i += gridDim.x * kEpWarps) {
     const int s = s0 + i;
     const int t = __ldcg(slot_token + s);
-    const uint4 *src = reinterpret_cast<const uint4 *>(x + (int64_t)t * d.H);
-    uint4 *dst = reinterpret_cast<uint4 *>(dst_rows + (int64_t)i * d.H);
-    for (int v = tid; v < nv; v += kEpThreads) dst[v] = __ldcg(src + v);
-    if (tid == 0) {
+    ep_copy_row(reinterpret_cast<uint4 *>(dst_rows + (int64_t)i * d.H),
+                reinterpret_cast<const uint4 *>(x + (int64_t)t * d.H), nv, lane);
+    if (lane == 0) {
       const int e = (int)__ldcg(idx + __ldcg(slot_pair + s));
       dst_meta[i] = make_int2(e - o * d.E_loc, s);
     }
@@ -328,19 +347,18 @@ __global__ void __launch_bounds__(1024) ep_owner_plan(EpDev d, OwnerPlan pp) {
 template <typename TA>
 __global__ void __launch_bounds__(kEpThreads) ep_return(EpDev d, const TA *y, const int *slot_token,
                                                         const int *plan_meta) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const uint64_t ep = ep_next(d);
   const int R = __ldcg(plan_meta + kMetaPairs);
   const int nv = d.H * (int)sizeof(TA) / 16;
   const int2 *meta = reinterpret_cast<const int2 *>(d.local + d.L.meta);
-  for (int s = blockIdx.x; s < R; s += gridDim.x) {
+  for (int s = blockIdx.x * kEpWarps + (tid >> 5); s < R; s += gridDim.x * kEpWarps) {
     const int row = __ldcg(slot_token + s);
     const int g = (int)(row / d.cap);
     const int src_slot = __ldcg(&meta[row].y);
     if (g < 0 || g >= d.G || src_slot < 0 || src_slot >= d.pmax) continue;  // not from a valid dispatch
-    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<TA *>(d.peer[g] + d.L.ret) + (int64_t)src_slot * d.H);
-    const uint4 *src = reinterpret_cast<const uint4 *>(y + (int64_t)s * d.H);
-    for (int v = tid; v < nv; v += kEpThreads) dst[v] = __ldcg(src + v);
+    ep_copy_row(reinterpret_cast<uint4 *>(reinterpret_cast<TA *>(d.peer[g] + d.L.ret) + (int64_t)src_slot * d.H),
+                reinterpret_cast<const uint4 *>(y + (int64_t)s * d.H), nv, lane);
   }
   __threadfence_system();
   __syncthreads();
@@ -548,7 +566,7 @@ struct EpDispatchLaunch {
     if constexpr (sizeof(TA) != 2) {
       return fail(TM_ERR_UNSUPPORTED, "expert parallelism needs bf16 or fp16 activations");
     } else {
-      const dim3 grid(kEpDispatchCTAs, c->world);
+      const dim3 grid((kEpCopyCTAs + c->world - 1) / c->world, c->world);
       ep_dispatch<TA><<<grid, kEpThreads, 0, s>>>(ep_dev(c), (const TA *)x, idx, ws_ptr<int>(ws, L->offsets),
                                                   ws_ptr<int>(ws, L->slot_token), ws_ptr<int>(ws, L->slot_pair));
       TM_LAUNCH_CHECK("ep_dispatch launch");
@@ -562,7 +580,7 @@ struct EpReturnLaunch {
     if constexpr (sizeof(TA) != 2) {
       return fail(TM_ERR_UNSUPPORTED, "expert parallelism needs bf16 or fp16 activations");
     } else {
-      ep_return<TA><<<kEpReturnCTAs, kEpThreads, 0, s>>>(ep_dev(c), ws_ptr<TA>(ws, L->ypart),
+      ep_return<TA><<<kEpCopyCTAs, kEpThreads, 0, s>>>(ep_dev(c), ws_ptr<TA>(ws, L->ypart),
                                                         ws_ptr<int>(ws, L->slot_token), ws_ptr<int>(ws, L->meta));
       TM_LAUNCH_CHECK("ep_return launch");
       return TM_OK;
