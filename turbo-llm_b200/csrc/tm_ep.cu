@@ -169,9 +169,11 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch(EpDev d, const TA *x, 
       dst_meta[i] = make_int2(e - o * d.E_loc, s);
     }
   }
-  __threadfence_system();
+  // the CTA's stores are ordered before thread 0's system-scope fence by the
+  // barrier (fence cumulativity): one fence per CTA, not per thread
   __syncthreads();
   if (tid == 0) {
+    __threadfence_system();
     int *done = reinterpret_cast<int *>(d.local + d.L.done) + o;
     if (atomicAdd(done, 1) == (int)gridDim.x - 1) {
       atomicExch(done, 0);
@@ -360,9 +362,9 @@ __global__ void __launch_bounds__(kEpThreads) ep_return(EpDev d, const TA *y, co
     ep_copy_row(reinterpret_cast<uint4 *>(reinterpret_cast<TA *>(d.peer[g] + d.L.ret) + (int64_t)src_slot * d.H),
                 reinterpret_cast<const uint4 *>(y + (int64_t)s * d.H), nv, lane);
   }
-  __threadfence_system();
   __syncthreads();
   if (tid == 0) {
+    __threadfence_system();
     int *done = reinterpret_cast<int *>(d.local + d.L.done) + kEpMaxRanks;
     if (atomicAdd(done, 1) == (int)gridDim.x - 1) {
       atomicExch(done, 0);

@@ -626,20 +626,42 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
 }
 
 // out[t] = residual[t] + sum_r w[t,r] * y[slot(t,r)] (top-k order, fp32).
+constexpr int kPfMaxTopK = 64;  // combine: slot ids and weights of one token in shared memory
+
+// out[t] = sum_r w[t,r] * y[slot(t,r)] (top-k order, fp32) (+ gated shared
+// expert) (+ residual), rounded once.  One CTA per token; each thread owns 8
+// columns and issues its loads of up to 8 ranks before accumulating them.
 template <typename TA>
 __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, const int *pair_slot, const TA *residual,
                                                   TA *out, int H, int k, const float *sh_w, int sh_slot0) {
+  __shared__ int s_slot[kPfMaxTopK];
+  __shared__ float s_w[kPfMaxTopK];
   const int t = blockIdx.x;
+  for (int r = threadIdx.x; r < k; r += blockDim.x) {
+    s_slot[r] = __ldcg(pair_slot + (size_t)t * k + r);
+    s_w[r] = Act<TA>::to_f(w[(size_t)t * k + r]);
+  }
+  __syncthreads();
   for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < k; ++r) {
-      const int s = __ldcg(pair_slot + (size_t)t * k + r);
-      if (s < 0) continue;
-      const float wr = Act<TA>::to_f(w[(size_t)t * k + r]);
-      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(y + (size_t)s * H + o));
-      const TA *yv = reinterpret_cast<const TA *>(&v);
+    for (int r0 = 0; r0 < k; r0 += 8) {
+      uint4 v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = fmaf(wr, Act<TA>::to_f(yv[j]), acc[j]);
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u;
+        const int sl = r < k ? s_slot[r] : -1;
+        v[u] = sl >= 0 ? __ldcg(reinterpret_cast<const uint4 *>(y + (size_t)sl * H + o)) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u;
+        if (r < k && s_slot[r] >= 0) {
+          const float wr = s_w[r];
+          const TA *yv = reinterpret_cast<const TA *>(&v[u]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = fmaf(wr, Act<TA>::to_f(yv[j]), acc[j]);
+        }
+      }
     }
     if (sh_w) {  // gated shared expert (moe.py:200): after the routed sum
       const float ws = __ldcg(sh_w + t);
@@ -663,7 +685,8 @@ __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, cons
   }
 }
 
-// Per token, one CTA:
+// Per token, one warp (8 tokens per CTA; a row of up to 2048 16-bit values
+// stays in the lane's registers between the two passes):
 //  * bf16 activations (x16 != NULL): x[t] -> f16 x16[t] = x[t] * 2^-s_t with
 //    s_t from the row's max |x| (exact for bf16 values: 8 significant bits into
 //    f16's 11, the row maximum scaled into [2^13, 2^14)), and for each of the
@@ -673,69 +696,74 @@ __global__ void __launch_bounds__(256) k4_combine(const TA *y, const TA *w, cons
 //  * with a shared expert (sh_gate_w != NULL): its gate score
 //    sh_w[t] = sigmoid(x[t] . sh_gate_w), F.linear's output and the sigmoid
 //    each rounded to the act dtype (moe.py:196-198).
+constexpr int kPrepWarps = 8;
+constexpr int kPrepVecs = 8;  // 16-byte vectors per lane kept in registers
 template <typename TA>
-__global__ void __launch_bounds__(256) k4_prep(const TA *x, const int *pair_slot, int H, int k, __half *x16,
-                                               float *slot_scale, const TA *sh_gate_w, float *sh_w, int sh_slot0) {
-  __shared__ float red[8], redg[8];
-  __shared__ int s_used;
-  const int t = blockIdx.x;
-  if (threadIdx.x == 0) {
-    int used = sh_gate_w != nullptr;
-    for (int r = 0; r < k; ++r) used |= __ldcg(pair_slot + (size_t)t * k + r) >= 0;
-    s_used = used;
-  }
-  __syncthreads();
-  if (!s_used) return;  // a row no slot reads (capacity rows of an expert-parallel owner)
-  const TA *xr = x + (size_t)t * H;
+__global__ void __launch_bounds__(kPrepWarps * 32) k4_prep(const TA *x, const int *pair_slot, int T, int H, int k,
+                                                           __half *x16, float *slot_scale, const TA *sh_gate_w,
+                                                           float *sh_w, int sh_slot0) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
+  if (t >= T) return;  // warp-uniform
+  int used = sh_gate_w != nullptr;
+  for (int r = lane; r < k && !used; r += 32) used = __ldcg(pair_slot + (size_t)t * k + r) >= 0;
+  if (!__any_sync(0xffffffffu, used)) return;  // a row no slot reads (capacity rows of an expert-parallel owner)
+  const uint4 *xr = reinterpret_cast<const uint4 *>(x + (size_t)t * H);
+  const uint4 *gr = reinterpret_cast<const uint4 *>(sh_gate_w);
+  const int nv = H / 8;
   float m = 0.f, gl = 0.f;
-  for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
-    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(xr + o));
-    const TA *p = reinterpret_cast<const TA *>(&v);
-    if (sh_gate_w) {
-      const uint4 gv = __ldg(reinterpret_cast<const uint4 *>(sh_gate_w + o));
-      const TA *gp = reinterpret_cast<const TA *>(&gv);
+  uint4 keep[kPrepVecs];
+  for (int b = 0; b < nv; b += 32 * kPrepVecs) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) gl = fmaf(Act<TA>::to_f(p[j]), Act<TA>::to_f(gp[j]), gl);
+    for (int u = 0; u < kPrepVecs; ++u) {
+      const int i = b + u * 32 + lane;
+      if (i < nv) {
+        const uint4 v = __ldcg(xr + i);
+        if (b == 0) keep[u] = v;
+        const TA *p = reinterpret_cast<const TA *>(&v);
+        if (sh_gate_w) {
+          const uint4 gv = __ldg(gr + i);
+          const TA *gp = reinterpret_cast<const TA *>(&gv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) gl = fmaf(Act<TA>::to_f(p[j]), Act<TA>::to_f(gp[j]), gl);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(Act<TA>::to_f(p[j])));
+      }
     }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(Act<TA>::to_f(p[j])));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     gl += __shfl_xor_sync(0xffffffffu, gl, o);
   }
-  if ((threadIdx.x & 31) == 0) {
-    red[threadIdx.x >> 5] = m;
-    redg[threadIdx.x >> 5] = gl;
-  }
-  __syncthreads();
-  m = red[0];
-  gl = redg[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
-    m = fmaxf(m, red[w]);
-    gl += redg[w];
-  }
-  if (sh_gate_w && threadIdx.x == 0) {
+  if (sh_gate_w && lane == 0) {
     const float logit = Act<TA>::round(gl);
     sh_w[t] = Act<TA>::round(1.0f / (1.0f + __expf(-logit)));
   }
   if (!x16) return;
   const int sh = f16_shift(m);
-  for (int o = threadIdx.x * 8; o < H; o += blockDim.x * 8) {
-    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(xr + o));
-    const TA *p = reinterpret_cast<const TA *>(&v);
-    uint4 r;
-    __half *q = reinterpret_cast<__half *>(&r);
+  for (int b = 0; b < nv; b += 32 * kPrepVecs) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) q[j] = __float2half_rn(ldexpf(Act<TA>::to_f(p[j]), -sh));
-    *reinterpret_cast<uint4 *>(x16 + (size_t)t * H + o) = r;
+    for (int u = 0; u < kPrepVecs; ++u) {
+      const int i = b + u * 32 + lane;
+      if (i < nv) {
+        const uint4 v = b == 0 ? keep[u] : __ldcg(xr + i);
+        const TA *p = reinterpret_cast<const TA *>(&v);
+        uint4 r;
+        __half *q = reinterpret_cast<__half *>(&r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = __float2half_rn(ldexpf(Act<TA>::to_f(p[j]), -sh));
+        reinterpret_cast<uint4 *>(x16 + (size_t)t * H)[i] = r;
+      }
+    }
   }
-  if ((int)threadIdx.x < k) {
-    const int s = __ldcg(pair_slot + (size_t)t * k + threadIdx.x);
-    if (s >= 0) slot_scale[s] = ldexpf(1.f, sh - 8);
+  const float scale = ldexpf(1.f, sh - 8);
+  for (int r = lane; r < k; r += 32) {
+    const int sl = __ldcg(pair_slot + (size_t)t * k + r);
+    if (sl >= 0) slot_scale[sl] = scale;
   }
-  if (sh_gate_w && threadIdx.x == 32) slot_scale[sh_slot0 + t] = ldexpf(1.f, sh - 8);
+  if (sh_gate_w && lane == 0) slot_scale[sh_slot0 + t] = scale;
 }
 
 static int num_sms() {
@@ -779,13 +807,15 @@ struct PrefillLaunch {
         // bf16: the gate/up GEMM runs on f16 operands (x16 after the slots' outputs in the ypart region)
         __half *x16 = reinterpret_cast<__half *>(reinterpret_cast<char *>(y) + (size_t)(P + T) * H * sizeof(TA));
         float *slot_scale = ws_ptr<float>(ws, L->logits);  // [P + T] (the region holds T * E floats)
-        k4_prep<TA><<<(unsigned)T, 256, 0, s>>>((const TA *)x, ws_ptr<int>(ws, L->pair_slot), H, k, x16, slot_scale,
+        k4_prep<TA><<<(unsigned)((T + kPrepWarps - 1) / kPrepWarps), kPrepWarps * 32, 0, s>>>(
+            (const TA *)x, ws_ptr<int>(ws, L->pair_slot), (int)T, H, k, x16, slot_scale,
                                                 shared ? (const TA *)sh_gate_w : nullptr, sh_w, (int)P);
         TM_LAUNCH_CHECK("k4_prep launch");
         g.act = (const TA *)x16;
         g.slot_scale = slot_scale;
       } else if (shared) {
-        k4_prep<TA><<<(unsigned)T, 256, 0, s>>>((const TA *)x, ws_ptr<int>(ws, L->pair_slot), H, k, nullptr, nullptr,
+        k4_prep<TA><<<(unsigned)((T + kPrepWarps - 1) / kPrepWarps), kPrepWarps * 32, 0, s>>>(
+            (const TA *)x, ws_ptr<int>(ws, L->pair_slot), (int)T, H, k, nullptr, nullptr,
                                                 (const TA *)sh_gate_w, sh_w, (int)P);
         TM_LAUNCH_CHECK("k4_prep launch");
       }
@@ -834,7 +864,7 @@ extern "C" int tm_combine_slots(const void *y, const void *topk_w, const int32_t
                                 int hidden, int top_k, int act_dtype, const void *residual, void *out,
                                 void *stream) {
   TM_REQUIRE(y && topk_w && pair_slot && out, "null pointer");
-  TM_REQUIRE(tokens >= 1 && top_k >= 1 && hidden > 0 && hidden % 8 == 0, "bad shape");
+  TM_REQUIRE(tokens >= 1 && top_k >= 1 && top_k <= kPfMaxTopK && hidden > 0 && hidden % 8 == 0, "bad shape");
   TM_REQUIRE(aligned(y, 16) && aligned(out, 16) && (!residual || aligned(residual, 16)),
              "y, residual and out must be 16-byte aligned");
   CombineLaunch f{y, topk_w, pair_slot, residual, out, tokens, hidden, top_k, as_stream(stream)};
@@ -862,6 +892,7 @@ extern "C" int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden,
   TM_REQUIRE(inter % 128 == 0 && inter > 0 && inter <= 128 * kPfMaxKBlocks,
              "inter (%d) must be a positive multiple of 128, at most %d", inter, 128 * kPfMaxKBlocks);
   TM_REQUIRE(n_experts <= kPfMaxExperts, "n_experts %d > %d", n_experts, kPfMaxExperts);
+  TM_REQUIRE(top_k >= 1 && top_k <= kPfMaxTopK, "top_k %d outside [1, %d]", top_k, kPfMaxTopK);
   TM_REQUIRE(aligned(x, 16) && aligned(w13, 16) && aligned(w2, 16) && aligned(out, 16) &&
                  (!residual || aligned(residual, 16)),
              "x, weights, residual and out must be 16-byte aligned");
