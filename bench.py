@@ -319,6 +319,57 @@ def run_ours(args, rank, world, local):
                    "status": ws.status() | wsp.status()}
         assert torch.isfinite(outp.float()).all(), "non-finite prefill output"
 
+    # ---- FP8 attention projections (q/k/v/o of Qwen3-30B-A3B), one decode token ----
+    attn = None
+    if args.attn_layers > 0:
+        La = args.attn_layers
+        # q, k, v share their input: their rows are packed as one [5120, 2048]
+        # weight (one launch); o [2048, 4096] follows attention (one launch)
+        shapes = [(4096 + 512 + 512, 2048), (2048, 4096)]  # [out, in]
+        ga = torch.Generator(device=dev)
+        ga.manual_seed(SEED + 21)
+        lins = []
+        for _l in range(La):
+            for N, K in shapes:
+                qa, sa = synth.quantize_fp8_block(torch.randn(N, K, generator=ga, device=dev) * 0.02)
+                lins.append(ops.pack_linear(qa, sa))
+                del qa
+        xa = synth.make_hidden(1, 2048, SEED + 22, rms_normalise=True, device=dev)
+        xo = synth.make_hidden(1, 4096, SEED + 23, device=dev)
+        outs = {N: torch.empty(1, N, dtype=torch.bfloat16, device=dev) for N in (5120, 2048)}
+
+        def attn_step():
+            for pl in lins:
+                ops.fp8_linear(xo if pl.in_features == 4096 else xa, pl, out=outs[pl.out_features])
+
+        sa_ = torch.cuda.Stream(device=dev)
+        sa_.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(sa_):
+            attn_step()
+        torch.cuda.current_stream().wait_stream(sa_)
+        ga_ = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ga_):
+            attn_step()
+        for _ in range(3):
+            ga_.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            ga_.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        usa = e0.elapsed_time(e1) / 10 * 1000 / La
+        ba = sum(N * K + (N // 128) * (K // 128) * 4 + (K + N) * 2 for N, K in shapes)
+        hbm, _src = _peaks()
+        attn = {"workload": f"FP8 block-scaled attention projections (tm_fp8_linear) of {La} Qwen3-30B-A3B "
+                            f"layers, one decode token: fused q/k/v [5120, 2048] + o [2048, 4096], CUDA graph",
+                "us_per_layer": round(usa, 2), "algorithmic_bytes_per_layer": ba,
+                "hbm_gbs": round(ba / (usa * 1e-6) / 1e9, 1), "frac": round(ba / (usa * 1e-6) / 1e9 / hbm, 4),
+                "launches_per_layer": len(shapes)}
+        del ga_, lins
+        assert all(torch.isfinite(o.float()).all() for o in outs.values()), "non-finite linear output"
+
     # ---- Qwen3.5-shaped layer (256 experts, I 512, FP8 shared expert), 64 tokens ----
     c3 = None
     if args.c3_tokens > 0:
@@ -414,6 +465,8 @@ def run_ours(args, rank, world, local):
         res["prefill"] = prefill
     if c3 is not None:
         res["qwen35_layer"] = c3
+    if attn is not None:
+        res["attention_linears"] = attn
     return res
 
 
@@ -593,6 +646,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="also time one prefill layer call of this many tokens (0 = skip)")
+    ap.add_argument("--attn-layers", type=int, default=48,
+                    help="also time the FP8 q/k/v/o projections of this many layers, one token (0 = skip)")
     ap.add_argument("--c3-tokens", type=int, default=64,
                     help="also time one Qwen3.5-shaped layer call (shared expert) of this many tokens (0 = skip)")
     ap.add_argument("--workload", choices=["decode", "ep"], default="decode",

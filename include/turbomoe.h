@@ -237,6 +237,25 @@ int tm_moe_decode_layer_noalloc(const void *x, int64_t tokens, int hidden, int i
                                 void *topk_w, void *out, uint32_t *status, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Dense FP8 block-scaled linear (attention q/k/v/o and other projections of
+ * an FP8 checkpoint).  Replaces ExpertLoader.load_weight's dequantisation
+ * (loader/expert_loader.py:109-112, arithmetic of :150-160) followed by
+ * F.linear for the projections of execution/layouts/qwen3.py:6-17:
+ *   out[t, n] = sum_k x[t, k] * W[n, k] * scale_inv[n/128, k/128]
+ *               (+ residual[t, n]), fp32 accumulation, rounded once to act.
+ * W is e4m3 [out_features, in_features] packed by tm_pack_linear
+ * (tm_packed_w2_bytes(out_features, in_features) bytes, the layout of one
+ * expert's down projection); scale_inv is the checkpoint's fp32
+ * [out_features/128, in_features/128] as is.  x [tokens, in_features] and out
+ * [tokens, out_features] act (bf16 or fp16); in_features % 512 == 0 (at most
+ * 6144), out_features % 128 == 0.  One pass over W per call (decode-sized
+ * calls are HBM-bound).  status: optional device uint32 for TM_STATUS_*. */
+int tm_pack_linear(const uint8_t *w, int out_features, int in_features, uint8_t *w_packed, void *stream);
+int tm_fp8_linear(const void *x, int64_t tokens, int in_features, int out_features, int act_dtype,
+                  const uint8_t *w_packed, const float *scale_inv, const void *residual, void *out,
+                  uint32_t *status, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Expert parallelism over NVLink peer memory (no counterpart in the reference,
  * which runs batch 1 on one device: runtime/engine.py:103-107,158; per token
  * the arithmetic is MoEExecutor.execute_layer, execution/moe.py:99-208).

@@ -210,6 +210,20 @@ extern "C" int tm_pack_experts(const uint8_t *gate, const float *gate_s, const u
                     "k5 s2 copy");
 }
 
+extern "C" int tm_pack_linear(const uint8_t *w, int out_features, int in_features, uint8_t *w_packed,
+                              void *stream) {
+  TM_REQUIRE(w && w_packed, "null pointer");
+  TM_REQUIRE(out_features % 128 == 0 && in_features % 128 == 0 && out_features > 0 && in_features > 0,
+             "out_features (%d) and in_features (%d) must be positive multiples of 128", out_features, in_features);
+  TM_REQUIRE(aligned(w, 16) && aligned(w_packed, 16), "weight pointers must be 16-byte aligned");
+  const int threads = 256;
+  // a dense [N, K] matrix packs exactly like one expert's down projection ([H, I])
+  k5_pack_w2<<<grid_for((int64_t)out_features * (in_features / 16), threads), threads, 0, as_stream(stream)>>>(
+      w, 1, out_features, in_features, w_packed);
+  TM_LAUNCH_CHECK("k5_pack_w2 (linear)");
+  return TM_OK;
+}
+
 namespace {
 struct Unpack {
   const uint8_t *w13; const float *s13; const uint8_t *w2; const float *s2;

@@ -1,0 +1,218 @@
+// Dense FP8 block-scaled linear: y = x W^T (+ residual) for the attention and
+// other projections of an FP8 checkpoint, without materialising W in the act
+// dtype.
+//
+// Reference: the q/k/v/o projections of execution/layouts/qwen3.py:6-17 are
+// loaded by ExpertLoader.load_weight (loader/expert_loader.py:89-114), which
+// dequantises W to the act dtype (loader/expert_loader.py:109-112, the same
+// arithmetic as dequantize_weight :150-160), and applied with F.linear.
+//
+// Layout: W [N, K] e4m3 packed like one expert's down projection,
+// [N/16][K/16][16 rows][16 B] (each 16x16 chunk one m16k16 MMA A tile, a
+// 16-row group one contiguous 16*K-byte tile); scales are the checkpoint's
+// weight_scale_inv [N/128][K/128] unchanged.
+//
+// k6_linear: CTA = 16 output rows.  Its weight tile arrives by four TMA bulk
+// copies (one quarter of K per warp) issued before griddepcontrol.wait (W does
+// not depend on the previous kernel).  Tokens are taken 8 at a time (the MMA's
+// N): their rows are copied in by TMA, scaled by an exact per-token power of 2
+// into f16 (exact for bf16/fp16 values) and multiplied on mma.sync m16n8k16
+// (e4m3 -> f16 exact, fp32 accumulation, block scale per 128 columns); the
+// four warps' K partial sums are added in warp order and rounded once to the
+// act dtype.  HBM-bound for decode-sized calls (one pass over W).
+#include "tm_common.cuh"
+
+namespace tmoe {
+
+constexpr int kLinWarps = 4;
+constexpr int kLinThreads = kLinWarps * 32;
+constexpr int kLinNT = 8;     // tokens per MMA pass
+constexpr int kLinRows = 16;  // output rows per CTA
+
+template <typename TA> struct LinArgs {
+  const TA *x;
+  const uint8_t *w;
+  const float *s;
+  const TA *residual;
+  TA *out;
+  uint32_t *status;  // optional TM_STATUS_* word
+  int T, K, N;
+};
+
+template <typename TA>
+__global__ void __launch_bounds__(kLinThreads) k6_linear(LinArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t lin_smem[];
+  const int tile_bytes = kLinRows * a.K;
+  const int quarter = tile_bytes / kLinWarps;
+  const int xstride = a.K + 8;  // f16 per staged token row (+16 bytes: no bank conflicts)
+  uint8_t *wtile = lin_smem;
+  __half *xs = reinterpret_cast<__half *>(lin_smem + tile_bytes);  // [kLinNT][xstride]
+  const TA *xraw = reinterpret_cast<const TA *>(xs);
+  float *ssc = reinterpret_cast<float *>(lin_smem + tile_bytes + (size_t)kLinNT * xstride * 2);  // [K/128]
+  __shared__ float red[kLinWarps][kLinRows][kLinNT];
+  __shared__ float xmax[kLinWarps][kLinNT];
+  __shared__ int s_shift[kLinNT];
+  __shared__ __align__(8) uint64_t bar[kLinWarps];
+  __shared__ __align__(8) uint64_t xbar;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int rg = blockIdx.x;
+  const int KB = a.K / 128;
+  if (tid == 0) {
+    for (int q = 0; q < kLinWarps; ++q) mbar_init(&bar[q], 1);
+    mbar_init(&xbar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const uint8_t *src = a.w + (int64_t)rg * tile_bytes;
+    for (int q = 0; q < kLinWarps; ++q) {
+      mbar_arrive_expect_tx(&bar[q], quarter);
+      tma_bulk_g2s(wtile + q * quarter, src + q * quarter, quarter, &bar[q]);
+    }
+  }
+  for (int i = tid; i < KB; i += kLinThreads) ssc[i] = __ldg(a.s + (int64_t)((rg * kLinRows) / 128) * KB + i);
+  pdl_trigger();
+  pdl_wait();  // x (and the residual) come from earlier kernels
+  const int cpw = (a.K / 16) / kLinWarps;  // 16-column chunks per warp (multiple of 8: K % 512 == 0)
+  const int kc0 = w * cpw;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t wsm = smem_u32(wtile) + (lane & 15) * 16;
+  bool first = true;
+  for (int tg = 0, grp = 0; tg < a.T; tg += kLinNT, ++grp) {
+    const int nt = min(kLinNT, a.T - tg);
+    if (tg) __syncthreads();  // everyone is done with the previous group's rows
+    if (tid == 0) {
+      fence_proxy_async();
+      const uint32_t rowb = (uint32_t)a.K * sizeof(TA);
+      mbar_arrive_expect_tx(&xbar, nt * rowb);
+      for (int j = 0; j < nt; ++j) tma_bulk_g2s(xs + (size_t)j * xstride, a.x + (int64_t)(tg + j) * a.K, rowb, &xbar);
+    }
+    const bool xok = mbar_wait_bounded(&xbar, grp & 1);
+    if (__syncthreads_or(!xok)) {
+      if (tid == 0) {
+        if (a.status) atomicOr(a.status, TM_STATUS_TIMEOUT);
+        mbar_wait_bounded(&xbar, grp & 1);
+        for (int q = 0; q < kLinWarps; ++q) mbar_wait_bounded(&bar[q], 0);
+      }
+      return;
+    }
+    // per-token max |x| over this warp's quarter of K -> exact power-of-2 shift
+    for (int j = 0; j < nt; ++j) {
+      float m = 0.f;
+      const int c_lo = w * (a.K / kLinWarps), c_hi = c_lo + a.K / kLinWarps;
+      for (int c = c_lo + lane; c < c_hi; c += 32) m = fmaxf(m, fabsf(Act<TA>::to_f(xraw[(size_t)j * xstride + c])));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) xmax[w][j] = m;
+    }
+    __syncthreads();
+    if (tid < nt) {
+      float m = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kLinWarps; ++ww) m = fmaxf(m, xmax[ww][tid]);
+      s_shift[tid] = f16_shift(m);
+    }
+    __syncthreads();
+    for (int i = tid; i < nt * (a.K / 2); i += kLinThreads) {  // in place: each pair read then written by one thread
+      const int j = i / (a.K / 2), c = (i % (a.K / 2)) * 2;
+      const float sc = ldexpf(1.0f, -s_shift[j]);
+      const __half2 hv = __floats2half2_rn(Act<TA>::to_f(xraw[(size_t)j * xstride + c]) * sc,
+                                           Act<TA>::to_f(xraw[(size_t)j * xstride + c + 1]) * sc);
+      *reinterpret_cast<__half2 *>(xs + (size_t)j * xstride + c) = hv;
+    }
+    __syncthreads();
+    if (first) {  // this warp's quarter of the weight tile
+      first = false;
+      const bool ok = mbar_wait_bounded(&bar[w], 0);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+          if (a.status) atomicOr(a.status, TM_STATUS_TIMEOUT);
+          for (int q = 0; q < kLinWarps; ++q) mbar_wait_bounded(&bar[q], 0);
+        }
+        return;
+      }
+    }
+    const __half *xrow = xs + (size_t)min(g, nt - 1) * xstride + 4 * t;  // B column n = g
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int blk = 0; blk < cpw / 8; ++blk) {
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};  // two independent MMA chains
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const int kc = kc0 + blk * 8 + i;
+        uint32_t r0, r1, r2, r3, a0, a1, a2, a3, c0, c1, c2, c3;
+        ldsm_x2(wsm + kc * 256, r0, r1);
+        ldsm_x2(wsm + (kc + 1) * 256, r2, r3);
+        const uint2 bx0 = *reinterpret_cast<const uint2 *>(xrow + kc * 16);
+        const uint2 bx1 = *reinterpret_cast<const uint2 *>(xrow + (kc + 1) * 16);
+        e4m3x4_to_f16x2x2(r0, a0, a2);
+        e4m3x4_to_f16x2x2(r1, a1, a3);
+        e4m3x4_to_f16x2x2(r2, c0, c2);
+        e4m3x4_to_f16x2x2(r3, c1, c3);
+        mma_16816(d0, a0, a1, a2, a3, bx0.x, bx0.y);
+        mma_16816(d1, c0, c1, c2, c3, bx1.x, bx1.y);
+      }
+      const float sblk = ssc[(kc0 + blk * 8) / 8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = fmaf(d0[q] + d1[q], sblk, acc[q]);
+    }
+    // D fragment: (row g, tokens 2t, 2t+1), (row g+8, tokens 2t, 2t+1)
+    red[w][g][2 * t] = acc[0];
+    red[w][g][2 * t + 1] = acc[1];
+    red[w][g + 8][2 * t] = acc[2];
+    red[w][g + 8][2 * t + 1] = acc[3];
+    __syncthreads();
+    if (tid < nt * kLinRows) {
+      const int j = tid / kLinRows, r = tid % kLinRows;
+      float y = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kLinWarps; ++ww) y += red[ww][r][j];
+      y *= ldexpf(1.0f, s_shift[j]);
+      const int64_t o = (int64_t)(tg + j) * a.N + rg * kLinRows + r;
+      if (a.residual) y += Act<TA>::to_f(Act<TA>::ld_cg(a.residual + o));
+      a.out[o] = Act<TA>::from_f(y);
+    }
+  }
+}
+
+static size_t linear_smem(int K) {
+  return (size_t)kLinRows * K + (size_t)kLinNT * (K + 8) * 2 + (size_t)(K / 128) * sizeof(float);
+}
+
+struct LinearLaunch {
+  const void *x; int64_t T; int K, N;
+  const uint8_t *w; const float *s; const void *residual; void *out; uint32_t *status; cudaStream_t st;
+  template <typename TA> int run() {
+    if constexpr (sizeof(TA) != 2) {
+      return fail(TM_ERR_UNSUPPORTED, "tm_fp8_linear: act dtype must be bf16 or fp16");
+    } else {
+      LinArgs<TA> a;
+      a.x = (const TA *)x; a.w = w; a.s = s; a.residual = (const TA *)residual; a.out = (TA *)out;
+      a.status = status; a.T = (int)T; a.K = K; a.N = N;
+      const size_t smem = linear_smem(K);
+      int rc = ensure_smem(reinterpret_cast<const void *>(k6_linear<TA>), smem);
+      if (rc) return rc;
+      return launch_pdl(k6_linear<TA>, dim3(N / kLinRows), dim3(kLinThreads), smem, st, "k6_linear launch", a);
+    }
+  }
+};
+
+}  // namespace tmoe
+
+using namespace tmoe;
+
+extern "C" int tm_fp8_linear(const void *x, int64_t tokens, int in_features, int out_features, int act_dtype,
+                             const uint8_t *w_packed, const float *scale_inv, const void *residual, void *out,
+                             uint32_t *status, void *stream) {
+  TM_REQUIRE(x && w_packed && scale_inv && out, "null pointer");
+  TM_REQUIRE(tokens >= 1 && tokens <= (1 << 20), "tokens %lld out of range", (long long)tokens);
+  TM_REQUIRE(in_features % 512 == 0 && in_features > 0 && in_features <= 6144,
+             "in_features %d must be a positive multiple of 512, at most 6144", in_features);
+  TM_REQUIRE(out_features % 128 == 0 && out_features > 0, "out_features %d must be a positive multiple of 128",
+             out_features);
+  TM_REQUIRE(aligned(x, 16) && aligned(w_packed, 16) && aligned(out, 16) && (!residual || aligned(residual, 2)),
+             "x, w_packed and out must be 16-byte aligned");
+  LinearLaunch f{x, tokens, in_features, out_features, w_packed, scale_inv, residual, out, status,
+                 as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}

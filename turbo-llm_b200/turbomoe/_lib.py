@@ -49,6 +49,8 @@ SIGNATURES = {
     "tm_combine_slots": (_i, [_p, _p, _p, _i64, _i, _i, _i, _p, _p, _p]),
     "tm_moe_decode_layer_noalloc": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                          _i, _p, _p, _p, _p, _p, _p, _p]),
+    "tm_pack_linear": (_i, [_p, _i, _i, _p, _p]),
+    "tm_fp8_linear": (_i, [_p, _i64, _i, _i, _i, _p, _p, _p, _p, _p, _p]),
     "tm_ep_buffer_bytes": (_i64, [_i, _i64, _i, _i, _i, _i]),
     "tm_ep_create": (_i, [_i, _i, _i, _i, _i, _i, _i, _i64, _p, C.POINTER(_p)]),
     "tm_ep_connect": (_i, [_p, _p]),

@@ -361,3 +361,41 @@ def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: Pac
     moe_gateup(x, k, packed, ws, shared, shared_gate_w)
     moe_down_combine(w, packed, ws, out, shared, residual.contiguous() if residual is not None else None)
     return out
+
+
+# ------------------------------------------------ dense FP8 linear (K6) ----
+@dataclass
+class PackedLinear:
+    """One FP8 block-scaled dense weight [out_features, in_features], packed for
+    tm_fp8_linear (scales kept in the checkpoint layout)."""
+    w: torch.Tensor       # uint8 [N * K], packed
+    s: torch.Tensor       # fp32 [N/128, K/128]
+    out_features: int
+    in_features: int
+
+
+def pack_linear(w_fp8: torch.Tensor, scale_inv: torch.Tensor) -> PackedLinear:
+    """Pack a checkpoint's e4m3 ``weight`` [N, K] + ``weight_scale_inv`` [N/128, K/128]."""
+    _need_cuda(w_fp8, scale_inv)
+    N, K = w_fp8.shape
+    w = _u8(w_fp8).contiguous()
+    out = torch.empty(N * K, dtype=torch.uint8, device=w.device)
+    check(lib().tm_pack_linear(w.data_ptr(), N, K, out.data_ptr(), _stream(w)), "tm_pack_linear")
+    return PackedLinear(out, scale_inv.float().contiguous(), N, K)
+
+
+def fp8_linear(x: torch.Tensor, pl: PackedLinear, residual: torch.Tensor | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear(x, dequantize(W))`` (+ residual) on the packed FP8 weight;
+    x [T, K] bf16/fp16 -> [T, N] in x's dtype."""
+    _need_cuda(x)
+    x = x.contiguous()
+    T, K = x.shape
+    if K != pl.in_features:
+        raise TurboMoEError(f"x has {K} features, the weight expects {pl.in_features}")
+    if out is None:
+        out = torch.empty(T, pl.out_features, dtype=x.dtype, device=x.device)
+    res = residual.contiguous() if residual is not None else None
+    check(lib().tm_fp8_linear(x.data_ptr(), T, K, pl.out_features, _code(x.dtype), pl.w.data_ptr(),
+                              pl.s.data_ptr(), _ptr(res), out.data_ptr(), None, _stream(x)), "tm_fp8_linear")
+    return out
