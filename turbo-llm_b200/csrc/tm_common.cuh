@@ -176,6 +176,25 @@ __device__ __forceinline__ void tma_bulk_g2s(void *dst, const void *src, uint32_
       : "memory");
 }
 
+// L2 policy for weight streams read once per step: their lines are the first
+// to be evicted, so the code, router weights, activations and workspace stay
+// in L2 while gigabytes of expert weights pass through it.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// tma_bulk_g2s with an L2 cache policy (l2_evict_first for weight streams).
+__device__ __forceinline__ void tma_bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                                  uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Order this thread's earlier generic-proxy shared-memory accesses (after a
 // CTA barrier: everyone's) before a following TMA write into the same bytes.
 __device__ __forceinline__ void fence_proxy_async() {
@@ -192,6 +211,43 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+// ------------------------------------------ cluster-scope mbarrier use ----
+// Shared::cluster address of `p` (this CTA's shared variable) in the CTA of
+// cluster rank `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier of any CTA of the cluster; release at cluster scope
+// orders this thread's earlier stores (shared::cluster included) before it.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence_cluster() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Bounded wait with acquire at cluster scope: stores that other CTAs made
+// before their release-arrive are visible after it returns true.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity, uint64_t max_ns) {
+  uint64_t t0 = 0;
+  for (bool first = true;; first = false) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (first) t0 = t;
+    else if (t - t0 > max_ns) return false;
+  }
 }
 
 // Wait for phase `parity` of `bar` for at most ~`max_ns` nanoseconds of
@@ -270,17 +326,30 @@ __device__ __forceinline__ int f16_shift(float maxabs) {
 // a workspace region, to reconstruct kernel timelines inside CUDA graphs.
 // Product builds compile every hook to nothing and reserve no space.
 #ifdef TM_TRACE
-constexpr int64_t kTraceCap = 1 << 18;
+constexpr int64_t kTraceCap = 1 << 20;
 constexpr int64_t kTraceBytes = 16 + kTraceCap * 16;
+constexpr int kTraceSlots = 8;  // events a CTA may record per launch (ids 0..7)
+// The CTA's first event (kTrEnter) reserves 2 * kTraceSlots entries with one
+// atomic; later events are plain stores into them (no round trip), so the
+// marks do not delay the code they time.  Event ev fills entry 2*ev with
+// (header, globaltimer) and entry 2*ev+1 with (header | 0x80 << 48, clock64).
+// Slots a CTA never writes keep the zeros the host cleared them to.
 __device__ __forceinline__ void trace_event(uint32_t *tr, int kid, int ev) {
+  __shared__ uint64_t *slot;
   if (tr && threadIdx.x == 0) {
-    const unsigned i = atomicAdd(tr, 1u);
-    if (i < kTraceCap) {
-      uint64_t t;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      uint64_t *e = reinterpret_cast<uint64_t *>(tr + 4) + 2 * i;
-      e[0] = ((uint64_t)kid << 56) | ((uint64_t)ev << 48) | (uint64_t)(blockIdx.x + blockIdx.y * gridDim.x);
-      e[1] = t;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const uint64_t c = clock64();
+    if (ev == 0) {
+      const unsigned i = atomicAdd(tr, (unsigned)(2 * kTraceSlots));
+      slot = i + 2 * kTraceSlots <= kTraceCap ? reinterpret_cast<uint64_t *>(tr + 4) + 2 * i : nullptr;
+    }
+    if (slot != nullptr && ev < kTraceSlots) {
+      const uint64_t h = ((uint64_t)kid << 56) | ((uint64_t)ev << 48) | (uint64_t)(blockIdx.x + blockIdx.y * gridDim.x);
+      slot[4 * ev] = h;
+      slot[4 * ev + 1] = t;
+      slot[4 * ev + 2] = h | (0x80ull << 48);
+      slot[4 * ev + 3] = c;
     }
   }
 }

@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(kLinThreads) k6_linear(LinArgs<TA> a) {
     const uint8_t *src = a.w + (int64_t)rg * tile_bytes;
     for (int q = 0; q < kLinWarps; ++q) {
       mbar_arrive_expect_tx(&bar[q], quarter);
-      tma_bulk_g2s(wtile + q * quarter, src + q * quarter, quarter, &bar[q]);
+      tma_bulk_g2s_hint(wtile + q * quarter, src + q * quarter, quarter, &bar[q], l2_evict_first());
     }
   }
   for (int i = tid; i < KB; i += kLinThreads) ssc[i] = __ldg(a.s + (int64_t)((rg * kLinRows) / 128) * KB + i);

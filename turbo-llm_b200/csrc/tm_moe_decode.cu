@@ -32,6 +32,7 @@ constexpr int kK3Threads = kK3Warps * 32;
 constexpr int kK3T1Warps = 8;              // K3 one token: one warp per routed expert
 constexpr int kK3T1Threads = kK3T1Warps * 32;
 constexpr int kK3T1MaxExperts = 16;        // routed + shared experts the one-token path holds
+constexpr int kK3T1MaxKB = 32;             // 128-column scale blocks per expert row it holds (K <= 4096)
 constexpr int kCombineInKernelMaxT = 64;
 
 struct PlanView {
@@ -141,7 +142,7 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup(GateUpArgs<TA> a) {
   }
   if (tid == 0) {
     mbar_arrive_expect_tx(&bar, tile_bytes);
-    tma_bulk_g2s(wtile, wbase + (int64_t)rg * tile_bytes, tile_bytes, &bar);
+    tma_bulk_g2s_hint(wtile, wbase + (int64_t)rg * tile_bytes, tile_bytes, &bar, l2_evict_first());
   }
   pdl_trigger();
   const int HB = a.H / 128, KC = a.H / 16;
@@ -300,9 +301,10 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
   }
   if (tid == 0) {
     const uint8_t *src = wbase + (int64_t)rg * tile_bytes;
+    const uint64_t pol = l2_evict_first();
     for (int q = 0; q < kK2Warps; ++q) {
       mbar_arrive_expect_tx(&bar[q], quarter);
-      tma_bulk_g2s(wtile + q * quarter, src + q * quarter, quarter, &bar[q]);
+      tma_bulk_g2s_hint(wtile + q * quarter, src + q * quarter, quarter, &bar[q], pol);
     }
   }
   pdl_trigger();
@@ -413,6 +415,7 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
     }
     // D fragment: (row g, tokens 2t, 2t+1), (row g+8, tokens 2t, 2t+1); the
     // partial sums reuse the x staging bytes once every warp is past its MMAs
+    TM_TRACE_EVENT(a.pl.trace, kTrGateUp, 4);  // warp 0's MMAs done
     __syncthreads();
     red[w][0][g][2 * t] = accg[0];
     red[w][0][g][2 * t + 1] = accg[1];
@@ -572,7 +575,7 @@ __global__ void __launch_bounds__(kK3Threads) k3_down(DownArgs<TA> a) {
   const int tile = kRows * K;
   if (!idle && tid == 0) {
     mbar_arrive_expect_tx(&bar, tile);
-    tma_bulk_g2s(wtile, wbase + (int64_t)rgo * tile, tile, &bar);
+    tma_bulk_g2s_hint(wtile, wbase + (int64_t)rgo * tile, tile, &bar, l2_evict_first());
   }
   pdl_trigger();
   pdl_wait();  // K2 (h) has completed
@@ -660,10 +663,12 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1(DownArgs<TA> a) {
   if (tid == 0) {
     mbar_arrive_expect_tx(&bar, n_active * tile_r + (a.has_shared ? tile_s : 0));
     for (int e = 0; e < n_active; ++e)
-      tma_bulk_g2s(k3_smem + (size_t)e * tile_r,
-                   a.w2 + (int64_t)s_rec[e].x * a.H * a.I + (int64_t)rgo * tile_r, tile_r, &bar);
+      tma_bulk_g2s_hint(k3_smem + (size_t)e * tile_r,
+                        a.w2 + (int64_t)s_rec[e].x * a.H * a.I + (int64_t)rgo * tile_r, tile_r, &bar,
+                        l2_evict_first());
     if (a.has_shared)
-      tma_bulk_g2s(k3_smem + (size_t)n_active * tile_r, a.sh_w2 + (int64_t)rgo * tile_s, tile_s, &bar);
+      tma_bulk_g2s_hint(k3_smem + (size_t)n_active * tile_r, a.sh_w2 + (int64_t)rgo * tile_s, tile_s, &bar,
+                        l2_evict_first());
   }
   pdl_trigger();
   pdl_wait();  // K2 (h) has completed
@@ -726,6 +731,8 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
   static_assert(sizeof(TA) == 2, "16-bit activations");
   extern __shared__ __align__(128) uint8_t k3_smem[];
   __shared__ float ysm[kK3T1MaxExperts][kRows];
+  __shared__ float s_sc[kK3T1MaxExperts][kK3T1MaxKB];  // block scales of this CTA's 16 rows
+  __shared__ float s_back[kK3T1MaxExperts];            // 2^shift that undoes h's f16 scaling
   __shared__ int4 s_rec[kK3T1MaxExperts];
   __shared__ int s_slot[32], s_map[32];   // pair -> slot, slot -> active expert
   __shared__ float s_w[32];
@@ -758,13 +765,33 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
   if (tid == 0) {
     mbar_arrive_expect_tx(&bar, n_active * tile_r + (a.has_shared ? tile_s : 0));
     for (int e = 0; e < n_active; ++e)
-      tma_bulk_g2s(k3_smem + (size_t)e * tile_r,
-                   a.w2 + (int64_t)s_rec[e].x * a.H * a.I + (int64_t)rgo * tile_r, tile_r, &bar);
+      tma_bulk_g2s_hint(k3_smem + (size_t)e * tile_r,
+                        a.w2 + (int64_t)s_rec[e].x * a.H * a.I + (int64_t)rgo * tile_r, tile_r, &bar,
+                        l2_evict_first());
     if (a.has_shared)
-      tma_bulk_g2s(k3_smem + (size_t)n_active * tile_r, a.sh_w2 + (int64_t)rgo * tile_s, tile_s, &bar);
+      tma_bulk_g2s_hint(k3_smem + (size_t)n_active * tile_r, a.sh_w2 + (int64_t)rgo * tile_s, tile_s, &bar,
+                        l2_evict_first());
   }
+  // block scales into shared memory now (weights: independent of K2), not
+  // one dependent global load per 128 columns inside the MMA loop
+  {
+    const int KB = a.I / 128, KBs = a.Is / 128, rb = (rgo * kRows) / 128;
+    for (int i = tid; i < n_exp * kK3T1MaxKB; i += kK3T1Threads) {
+      const int e = i / kK3T1MaxKB, b = i % kK3T1MaxKB;
+      if (e == n_active) {
+        if (b < KBs) s_sc[e][b] = __ldg(a.sh_s2 + (int64_t)rb * KBs + b);
+      } else if (b < KB) {
+        s_sc[e][b] = __ldg(a.s2 + ((int64_t)s_rec[e].x * (a.H / 128) + rb) * KB + b);
+      }
+    }
+  }
+  // the residual (this layer's input, complete before the router that
+  // preceded K2 could pass its own wait) is loaded now, off the tail
+  float res_pre = 0.f;
+  if (tid < kRows && a.residual) res_pre = Act<TA>::to_f(Act<TA>::ld_cg(a.residual + rgo * kRows + tid));
   pdl_trigger();
   pdl_wait();  // K2 (h) has completed
+  const float shw = (a.has_shared && tid < kRows) ? ld_cg(a.sh_w) : 0.f;  // gate score from K2
   TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrWaited);
   if (tid == 0) {
     const uint32_t hb = (uint32_t)a.k * a.I * sizeof(float), hsb = (uint32_t)a.Is * sizeof(float);
@@ -794,6 +821,7 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const int sh_exp = f16_shift(m);
     const float sc = ldexpf(1.0f, -sh_exp);
+    if (lane == 0) s_back[e] = ldexpf(1.0f, sh_exp);
     for (int c = lane * 2; c < K; c += 64)
       *reinterpret_cast<__half2 *>(hh + c) = __floats2half2_rn(hf[c] * sc, hf[c + 1] * sc);
     __syncwarp();
@@ -810,16 +838,10 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
   for (int e = w; e < n_exp; e += kK3T1Warps) {
     const bool sh = e == n_active;
     const int K = sh ? a.Is : a.I;
-    const float *hf = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
-    float m = 0.f;  // recompute the shift (cheap; keeps the conversion loop register-light)
-    for (int c = lane; c < K; c += 32) m = fmaxf(m, fabsf(hf[c]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float back = ldexpf(1.0f, f16_shift(m));
+    const float back = s_back[e];  // written by this warp in the conversion pass
     const __half *hrow = h16 + (size_t)e * hstride + 4 * t;
     const uint32_t wsm = smem_u32(k3_smem + (size_t)e * tile_r) + (lane & 15) * 16;
-    const float *srow = (sh ? a.sh_s2 : a.s2 + (int64_t)s_rec[e].x * (a.H / 128) * (a.I / 128)) +
-                        (int64_t)((rgo * kRows) / 128) * (K / 128);
+    const float *srow = s_sc[e];
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int blk = 0; blk < K / 128; ++blk) {
       float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};  // two independent MMA chains
@@ -838,7 +860,7 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
         mma_16816(d0, a0, a1, a2, a3, bx0.x, bx0.y);
         mma_16816(d1, c0, c1, c2, c3, bx1.x, bx1.y);
       }
-      const float s = __ldg(srow + blk);
+      const float s = srow[blk];
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[q] = fmaf(d0[q] + d1[q], s, acc[q]);
     }
@@ -848,14 +870,15 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
       ysm[e][g + 8] = acc[2] * back;
     }
   }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, 4);  // warp 0's MMAs done
   __syncthreads();
   if (tid < kRows) {
     float y = 0.f;
     for (int kk = 0; kk < a.k; ++kk)
       if (s_slot[kk] >= 0) y = fmaf(s_w[kk], ysm[s_map[s_slot[kk]]][tid], y);
-    if (a.has_shared) y = fmaf(ld_cg(a.sh_w), ysm[n_active][tid], y);
+    if (a.has_shared) y = fmaf(shw, ysm[n_active][tid], y);
     const int nn = rgo * kRows + tid;
-    if (a.residual) y += Act<TA>::to_f(Act<TA>::ld_cg(a.residual + nn));
+    if (a.residual) y += res_pre;
     a.out[nn] = Act<TA>::from_f(y);
   }
   TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrExit);
@@ -948,7 +971,8 @@ struct DownLaunch {
     const int max_active = (int)std::min<int64_t>(E, T * k);
     a.combine_in_kernel = T <= kCombineInKernelMaxT ? 1 : 0;
     a.tile_bytes = kRows * std::max(I, a.Is);
-    if (T == 1 && max_active + a.has_shared <= kK3T1MaxExperts && k <= 32) {
+    if (T == 1 && max_active + a.has_shared <= kK3T1MaxExperts && k <= 32 &&
+        std::max(I, a.Is) <= 128 * kK3T1MaxKB) {
       size_t smem = (size_t)max_active * kRows * I + (size_t)kRows * a.Is + ((size_t)k * I + a.Is) * sizeof(float);
       if constexpr (sizeof(TA) == 2) {
         smem += (size_t)(max_active + a.has_shared) * (std::max(I, a.Is) + 8) * 2;

@@ -552,6 +552,7 @@ __device__ void topk_redux_token(const RouterArgs<TA> &a, const float *lg, int t
     if (s_idx) s_idx[lane] = my_e;
   }
   if (!plan) return;
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 5);  // top-k done, plan starts
   // single token: the k distinct experts each get one slot, in ascending id order
   int asc = 0;
   for (int q = 0; q < a.k; ++q) asc += __shfl_sync(0xffffffffu, my_e, q) < my_e;
@@ -671,6 +672,7 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<T
       }
     }
   }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 4);  // dot products done
   cluster.sync();  // every CTA's logits are in CTA 0
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrExit);
   if (crank != 0 || !ok) return;
@@ -695,6 +697,228 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<T
     return;
   }
   plan_build(src, nt, a.k, a.E, a.pp, reinterpret_cast<int *>(r_smem));
+}
+
+// One-token decode router (k <= 8, E <= 128): the latency-critical link of
+// every decode layer, so each stage is a short dependency chain.
+//  * Two expert rows per warp, held in registers before the dependency wait;
+//    the dot products run as 8 independent partial sums (two rows x four
+//    chains) and both rows' warp reductions are interleaved.
+//  * Each warp stores its two logits into CTA 0's shared memory and arrives on
+//    CTA 0's mbarrier (release, cluster scope); only CTA 0's warp 0 waits, no
+//    cluster-wide barrier.
+//  * Top-k: each lane sorts its 4 (logit, expert) keys, then k rounds of one
+//    redux.sync.max over the lanes' heads, the winner advancing; the softmax
+//    denominator's reduction runs between those rounds.
+//  * The plan comes from a 128-bit mask of the selected experts (popcounts),
+//    not from shuffles.
+// Same results as k1_router_cluster: the same keys and tie rule (value
+// descending, then lower expert id), the same softmax and renormalisation
+// arithmetic in the same order; the logits' fp32 partial sums are added in a
+// different order (within the rounding the tests allow for F.linear).
+constexpr int kT1MaxK = 8;
+template <typename TA>
+__global__ void __launch_bounds__(kRouterThreads) k1_router_t1(RouterArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t r_smem[];  // x row
+  TA *xs = reinterpret_cast<TA *>(r_smem);
+  __shared__ float s_logit[kClusterMaxE];
+  __shared__ __align__(8) uint64_t bar;   // x copy
+  __shared__ __align__(8) uint64_t lbar;  // CTA 0: one arrival per warp of the cluster
+  constexpr int V = 8;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int vpl = a.H / (V * 32);  // 16-byte vectors per lane and row (<= 8: host checks)
+  const int e0 = crank * (kRouterWarps * 2) + w * 2;
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrEnter);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_init(&lbar, kClusterCTAs * kRouterWarps);
+    mbar_init_fence_cluster();
+  }
+  uint4 row[2][8];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int e = min(e0 + r, a.E - 1);  // rows past E compute a discarded copy of row E-1
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.w + (int64_t)e * a.H);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < vpl) row[r][i] = ldg_stream(src + i * 32 + lane);
+  }
+#ifdef TM_TRACE
+  {  // trace builds: when have this warp's rows arrived?
+    uint32_t d = 0u;
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < vpl) d ^= row[r][i].x ^ row[r][i].y ^ row[r][i].z ^ row[r][i].w;
+    if (d == 0x9e3779b9u) s_logit[lane] = 0.f;
+    TM_TRACE_EVENT(a.pp.trace, kTrRouter, 5);
+  }
+#endif
+  cluster.sync();  // every CTA runs and CTA 0's lbar is initialised (off the critical path)
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrWaited);
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)a.H * sizeof(TA);
+    mbar_arrive_expect_tx(&bar, bytes);
+    tma_bulk_g2s(xs, a.x, bytes, &bar);
+  }
+  const bool ok = mbar_wait_bounded(&bar, 0);
+  if (!ok && lane == 0) atomicOr(a.pp.status, TM_STATUS_TIMEOUT);
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
+  float acc[2][4];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i < vpl) {
+      const uint4 xq = *reinterpret_cast<const uint4 *>(xs + (i * 32 + lane) * V);
+      const TA *xe = reinterpret_cast<const TA *>(&xq);
+      float xf[V];
+#pragma unroll
+      for (int u = 0; u < V; ++u) xf[u] = Act<TA>::to_f(xe[u]);
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const TA *qe = reinterpret_cast<const TA *>(&row[r][i]);
+#pragma unroll
+        for (int u = 0; u < V; ++u) acc[r][u & 3] = fmaf(Act<TA>::to_f(qe[u]), xf[u], acc[r][u & 3]);
+      }
+    }
+  }
+  float s0 = (acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3]);
+  float s1 = (acc[1][0] + acc[1][1]) + (acc[1][2] + acc[1][3]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+  }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 7);  // dot products reduced
+  if (lane == 0) {
+    float *logit0 = cluster.map_shared_rank(&s_logit[0], 0);
+    const float r0 = Act<TA>::round(s0), r1 = Act<TA>::round(s1);  // F.linear outputs in act dtype
+    if (e0 < a.E) logit0[e0] = r0;
+    if (e0 + 1 < a.E) logit0[e0 + 1] = r1;
+    if (a.logits_out) {
+      if (e0 < a.E) a.logits_out[e0] = Act<TA>::from_f(r0);
+      if (e0 + 1 < a.E) a.logits_out[e0 + 1] = Act<TA>::from_f(r1);
+    }
+    mbar_arrive_cluster(cluster_addr(&lbar, 0));
+  }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 4);  // dot products done
+  if (crank != 0) return;
+  if (w != 0) {
+    for (int i = tid - 32; i < a.pp.k3_cnt_n; i += kRouterThreads - 32) a.pp.k3_cnt[i] = 0;
+    return;
+  }
+  // CTA 0, warp 0.  Its limit is above every peer's own x wait (1 s), so a
+  // peer always arrives (and has made its stores) before this gives up.
+  if (!mbar_wait_cluster_bounded(&lbar, 0, 2000000000ull)) {
+    if (lane == 0) atomicOr(a.pp.status, TM_STATUS_TIMEOUT);
+    return;
+  }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrExit);
+  // ---- top-k over 4 keys per lane (expert i * 32 + lane)
+  float v[4];
+  uint32_t key[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < a.E ? s_logit[e] : -INFINITY;
+    key[i] = e < a.E ? (order16(LogitKey<TA>::bits(v[i])) << 16) | (0xFFFFu - e) : 0u;
+  }
+  uint32_t h0 = max(key[0], key[1]), h1 = min(key[0], key[1]);  // sort descending
+  uint32_t h2 = max(key[2], key[3]), h3 = min(key[2], key[3]);
+  {
+    const uint32_t a0 = max(h0, h2), a2 = min(h0, h2), a1 = max(h1, h3), a3 = min(h1, h3);
+    h0 = a0;
+    h1 = max(a1, a2);
+    h2 = min(a1, a2);
+    h3 = a3;
+  }
+  uint32_t win[kT1MaxK];
+  float m = 0.f, ls = 0.f;
+#pragma unroll
+  for (int r = 0; r < kT1MaxK; ++r) {
+    if (r < a.k) {
+      win[r] = __reduce_max_sync(0xffffffffu, h0);
+      if (h0 == win[r]) {  // keys are distinct: exactly one lane advances
+        h0 = h1;
+        h1 = h2;
+        h2 = h3;
+        h3 = 0u;
+      }
+    } else {
+      win[r] = 0u;
+    }
+    if (r == 0) {  // softmax denominator: exp(v - max) summed in expert-slot order, then over lanes
+      m = LogitKey<TA>::value(unorder16(win[0] >> 16));
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (i * 32 + lane < a.E) ls += __expf(v[i] - m);
+    } else if (r <= 5) {
+      ls += __shfl_xor_sync(0xffffffffu, ls, 32 >> r);
+    }
+  }
+  // rank `lane` (< k): its expert and logit
+  int my_e = 0;
+  float my_v = 0.f;
+#pragma unroll
+  for (int r = 0; r < kT1MaxK; ++r)
+    if (lane == r) {
+      my_e = 0xFFFF - (int)(win[r] & 0xFFFFu);
+      my_v = LogitKey<TA>::value(unorder16(win[r] >> 16));
+    }
+  const float p = lane < a.k ? __expf(my_v - m) / ls : 0.f;  // softmax probability of rank `lane`
+  const float psum = warp_sum(p);
+  // ---- plan: mask of the selected experts
+  uint32_t msk[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int r = 0; r < kT1MaxK; ++r) {
+    if (r < a.k) {
+      const int e = 0xFFFF - (int)(win[r] & 0xFFFFu);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) msk[i] |= (e >> 5) == i ? 1u << (e & 31) : 0u;
+    }
+  }
+  const PlanPtrs &pp = a.pp;
+  int below = 0;  // selected experts with an id below i * 32 + lane
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int x = i * 32 + lane;
+    const int here = below + __popc(msk[i] & ((1u << lane) - 1u));
+    if (x < a.E) {
+      pp.counts[x] = (msk[i] >> lane) & 1u;
+      pp.offsets[x] = here;
+    }
+    below += __popc(msk[i]);
+  }
+  if (lane < a.k) {
+    const int ew = my_e >> 5, eb = my_e & 31;
+    int asc = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)  // (selects, not a dynamically indexed register array)
+      asc += i < ew ? __popc(msk[i]) : i == ew ? __popc(msk[i] & ((1u << eb) - 1u)) : 0;
+    a.idx_out[lane] = my_e;
+    a.w_out[lane] = Act<TA>::from_f(p / psum);
+    pp.slot_pair[asc] = lane;
+    pp.slot_token[asc] = 0;
+    pp.pair_slot[lane] = asc;
+    pp.act_list[asc] = my_e;
+    pp.act_rec[asc] = make_int4(my_e, 1, asc, 0);
+  }
+  if (lane == 0) {
+    pp.offsets[a.E] = a.k;
+    pp.meta[kMetaNActive] = a.k;
+    pp.meta[kMetaPairs] = a.k;
+    pp.meta[kMetaTokens] = 1;
+  }
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 6);
 }
 
 // ------------------------------------- multi-token router (tensor cores) ----
@@ -1115,8 +1339,11 @@ struct RouterLaunch {
         a.TB = T;
         a.n_ttiles = 1;
         a.n_etiles = kClusterCTAs;
-        const size_t smem = std::max((size_t)T * H * sizeof(TA), plan_smem(kRouterWarps, E));
         const dim3 grid(kClusterCTAs), block(kRouterThreads);
+        if (T == 1 && k <= kT1MaxK)
+          return launch_cluster_pdl(k1_router_t1<TA>, grid, block, (size_t)H * sizeof(TA), kClusterCTAs, s,
+                                    "k1_router launch", a);
+        const size_t smem = std::max((size_t)T * H * sizeof(TA), plan_smem(kRouterWarps, E));
         switch (T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8) {
           case 1: return launch_cluster_pdl(k1_router_cluster<TA, 1>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
           case 2: return launch_cluster_pdl(k1_router_cluster<TA, 2>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
