@@ -261,7 +261,7 @@ def run_ours(args, rank, world, local):
             idx, w = routes[l]
             ops.route_plan(idx, 128, ws)
             if with_k2:
-                ops.moe_gateup(xs[l], 8, pls[l].experts, ws)
+                ops.moe_gateup(xs[l], 8, pls[l].experts, ws, prefetch_down=True)
             if with_k3:
                 ops.moe_down_combine(w, pls[l].experts, ws, out, residual=xs[l])
 

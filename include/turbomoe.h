@@ -156,6 +156,19 @@ int tm_moe_decode_gateup(const void *x, int64_t tokens, int hidden, int inter,
                          int shared_inter, const void *sh_gate_w, void *ws,
                          int64_t ws_bytes, void *stream);
 
+/* K2 as tm_moe_decode_gateup; in addition each CTA, once its own weight
+ * tile has landed, pulls its share of the packed down projections of the
+ * same experts (w2 of the routed experts; sh_w2 when sh_w13 is set) from HBM
+ * into L2, so that the tm_moe_decode_down_combine call that follows reads
+ * them from L2.  Same arguments as tm_moe_decode_gateup plus w2 / sh_w2 (the
+ * arrays later passed to tm_moe_decode_down_combine); same results bit for
+ * bit. */
+int tm_moe_decode_gateup_prefetch(const void *x, int64_t tokens, int hidden, int inter,
+                                  int n_experts, int top_k, int act_dtype, const uint8_t *w13,
+                                  const float *s13, const uint8_t *sh_w13, const float *sh_s13,
+                                  int shared_inter, const void *sh_gate_w, const uint8_t *w2,
+                                  const uint8_t *sh_w2, void *ws, int64_t ws_bytes, void *stream);
+
 /* K3: down dequant-GEMV with the routing-weighted combine (+ the
  * sigmoid-gated shared expert, + an optional residual).  Replaces moe_seq's
  * down projection and weighted sum (execution/moe.py:18-19), the weighted

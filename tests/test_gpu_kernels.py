@@ -327,3 +327,28 @@ def test_route_plan_many_pairs_flags_bad_ids():
     assert torch.equal(plan["slot_token"].long(), grp["tokens"])
     assert torch.equal((plan["slot_pair"] % 4).long(), grp["kpos"])
     assert ws.status() == 0
+
+
+@pytest.mark.parametrize("T,shared_inter", [(1, 0), (5, 0), (1, 512), (3, 512)])
+def test_gateup_prefetch_matches_plain_gateup(T, shared_inter):
+    """tm_moe_decode_gateup_prefetch (K2 that also pulls the down projections
+    into L2) gives bit for bit the output of tm_moe_decode_gateup + K3."""
+    from turbomoe import ops, synth
+    shape = synth.MoEShape(2048, 768, 128, 8, shared_inter)
+    lw = synth.make_layer(shape, 31 + T, 0, device="cuda")
+    experts, shared, gate = packed_from_layer(lw)
+    ws = workspace_for(shape)
+    x = synth.make_hidden(T, shape.hidden, 4, dtype=torch.bfloat16, device="cuda")
+    idx, w = ops.router_topk(x, lw.router.cuda(), 8, ws)
+    g = gate.to(x.dtype) if gate is not None else None
+    outs = []
+    for pf in (False, True, False, True):
+        ops.route_plan(idx, 128, ws)
+        ops.moe_gateup(x, 8, experts, ws, shared, g, prefetch_down=pf)
+        out = torch.empty_like(x)
+        ops.moe_down_combine(w, experts, ws, out, shared, residual=x)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])

@@ -221,10 +221,13 @@ __device__ __forceinline__ uint32_t cluster_addr(const void *p, int rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
   return r;
 }
-// Arrive on an mbarrier of any CTA of the cluster; release at cluster scope
-// orders this thread's earlier stores (shared::cluster included) before it.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+// Asynchronous 4-byte store into shared memory of a CTA of the cluster; when
+// it lands it completes 4 transaction bytes on that CTA's mbarrier, so the
+// writer needs no fence and may exit right after issuing it.
+__device__ __forceinline__ void st_async_u32(uint32_t dst_cluster_addr, uint32_t v, uint32_t bar_cluster_addr) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.u32 [%0], %1, [%2];" ::"r"(dst_cluster_addr),
+               "r"(v), "r"(bar_cluster_addr)
+               : "memory");
 }
 __device__ __forceinline__ void mbar_init_fence_cluster() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");

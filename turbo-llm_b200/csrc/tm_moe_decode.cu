@@ -91,9 +91,25 @@ template <typename TA> struct GateUpArgs {
   const TA *sh_gate_w;
   PlanView pl;
   float *sh_w, *h, *sh_h;
+  // optional (NULL: none): the packed down projections of the same experts.
+  // Once its own tile has landed, CTA (expert, row group rg) pulls bytes
+  // [rg*16*H, (rg+1)*16*H) of that expert's w2 into L2; the RG = I/16 CTAs of
+  // an expert cover its whole H x I down projection, so the K3 call that
+  // follows reads it from L2 while HBM would otherwise idle through K2's
+  // arithmetic and the kernel boundary.
+  const uint8_t *pf_w2, *pf_sh_w2;
   int T, H, I, Is, E, P, RG, RGs;
   int routed_ctas;  // max_active * RG
 };
+
+// L2 prefetch of one 16-row slice of an expert's packed down projection
+// (16 * H bytes, 16-byte aligned since H % 512 == 0); fire and forget.
+__device__ __forceinline__ void k2_prefetch_down(const uint8_t *w2, int64_t expert_bytes, int expert, int rg,
+                                                 int H) {
+  if (w2 == nullptr) return;
+  const uint8_t *p = w2 + (int64_t)expert * expert_bytes + (int64_t)rg * 16 * H;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"((uint32_t)(16 * H)) : "memory");
+}
 
 template <typename TA, int kNT>
 __global__ void __launch_bounds__(kK2Threads) k2_gateup(GateUpArgs<TA> a) {
@@ -116,7 +132,7 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup(GateUpArgs<TA> a) {
   TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrWaited);
   int b = blockIdx.x;
   bool shared_expert;
-  int rg, n, slot0, I;
+  int rg, n, slot0, I, eid = 0;
   const uint8_t *wbase;
   const float *sbase;
   if (b < a.routed_ctas) {
@@ -129,6 +145,7 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup(GateUpArgs<TA> a) {
     n = rec.y;
     slot0 = rec.z;
     I = a.I;
+    eid = rec.x;
     wbase = a.w13 + (int64_t)rec.x * 2 * a.I * a.H;
     sbase = a.s13 + (int64_t)rec.x * 2 * (a.I / 128) * (a.H / 128);
   } else {
@@ -181,6 +198,10 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup(GateUpArgs<TA> a) {
     if (tg == 0) {
       if (!tile_ready(&bar, a.pl.status)) return;
       TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrData);
+      if (tid == 0) {  // this CTA's tile is in: HBM can carry K3's weights now
+        if (shared_expert) k2_prefetch_down(a.pf_sh_w2, (int64_t)a.H * a.Is, 0, rg, a.H);
+        else k2_prefetch_down(a.pf_w2, (int64_t)a.H * a.I, eid, rg, a.H);
+      }
     } else {
       __syncthreads();
     }
@@ -275,7 +296,7 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
   TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrWaited);
   int b = blockIdx.x;
   bool shared_expert;
-  int rg, n, slot0, I;
+  int rg, n, slot0, I, eid = 0;
   const uint8_t *wbase;
   const float *sbase;
   if (b < a.routed_ctas) {
@@ -288,6 +309,7 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
     n = rec.y;
     slot0 = rec.z;
     I = a.I;
+    eid = rec.x;
     wbase = a.w13 + (int64_t)rec.x * 2 * a.I * a.H;
     sbase = a.s13 + (int64_t)rec.x * 2 * (a.I / 128) * (a.H / 128);
   } else {
@@ -387,6 +409,10 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
         return;
       }
       TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrData);
+      if (tid == 0) {  // this CTA's tile is in: HBM can carry K3's weights now
+        if (shared_expert) k2_prefetch_down(a.pf_sh_w2, (int64_t)a.H * a.Is, 0, rg, a.H);
+        else k2_prefetch_down(a.pf_w2, (int64_t)a.H * a.I, eid, rg, a.H);
+      }
     }
     const __half *xrow = xs + (size_t)min(g, nt - 1) * xstride + 4 * t;  // B column n = g
     float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
@@ -903,6 +929,7 @@ struct GateUpLaunch {
   const void *x; int64_t T; int H, I, E, k, Is;
   const uint8_t *w13; const float *s13; const uint8_t *sh_w13; const float *sh_s13; const void *sh_gate_w;
   void *ws; const WsLayout *L; cudaStream_t s;
+  const uint8_t *pf_w2 = nullptr, *pf_sh_w2 = nullptr;  // down projections to pull into L2 (optional)
   template <typename TA, int kNT> int go(GateUpArgs<TA> &a, int grid) {
     if constexpr (sizeof(TA) == 2) {
       // tile + x rows (f16, padded; >= the 4 KB reduction area) + block scales
@@ -918,6 +945,7 @@ struct GateUpLaunch {
     GateUpArgs<TA> a;
     a.x = (const TA *)x;
     a.w13 = w13; a.s13 = s13; a.sh_w13 = sh_w13; a.sh_s13 = sh_s13; a.sh_gate_w = (const TA *)sh_gate_w;
+    a.pf_w2 = pf_w2; a.pf_sh_w2 = sh_w13 ? pf_sh_w2 : nullptr;
     a.pl = plan_view(ws, *L);
     a.sh_w = ws_ptr<float>(ws, L->sh_w);
     a.h = ws_ptr<float>(ws, L->h);
@@ -1016,6 +1044,27 @@ extern "C" int tm_moe_decode_gateup(const void *x, int64_t tokens, int hidden, i
   if (rc) return rc;
   GateUpLaunch f{x, tokens, hidden, inter, n_experts, top_k, shared_inter, w13, s13, sh_w13, sh_s13,
                  sh_gate_w, ws, &L, as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
+extern "C" int tm_moe_decode_gateup_prefetch(const void *x, int64_t tokens, int hidden, int inter,
+                                             int n_experts, int top_k, int act_dtype, const uint8_t *w13,
+                                             const float *s13, const uint8_t *sh_w13, const float *sh_s13,
+                                             int shared_inter, const void *sh_gate_w, const uint8_t *w2,
+                                             const uint8_t *sh_w2, void *ws, int64_t ws_bytes, void *stream) {
+  TM_REQUIRE(x && w13 && s13 && w2, "null pointer");
+  TM_REQUIRE(hidden % 512 == 0, "hidden (%d) must be a multiple of 512", hidden);
+  TM_REQUIRE(inter % 128 == 0 && inter > 0, "inter (%d) must be a positive multiple of 128", inter);
+  TM_REQUIRE(!sh_w13 || (sh_s13 && sh_gate_w && sh_w2 && shared_inter > 0 && shared_inter % 128 == 0),
+             "shared expert needs sh_s13, sh_gate_w, sh_w2 and shared_inter %% 128 == 0");
+  TM_REQUIRE(aligned(x, 16) && aligned(w13, 16) && aligned(w2, 16) &&
+                 (!sh_w13 || (aligned(sh_w13, 16) && aligned(sh_w2, 16))),
+             "x and weights must be 16-byte aligned");
+  WsLayout L;
+  int rc = ws_check(ws, ws_bytes, tokens, n_experts, top_k, hidden, inter, sh_w13 ? shared_inter : 0, &L);
+  if (rc) return rc;
+  GateUpLaunch f{x, tokens, hidden, inter, n_experts, top_k, shared_inter, w13, s13, sh_w13, sh_s13,
+                 sh_gate_w, ws, &L, as_stream(stream), w2, sh_w2};
   return dispatch_act(act_dtype, f);
 }
 

@@ -701,12 +701,12 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<T
 
 // One-token decode router (k <= 8, E <= 128): the latency-critical link of
 // every decode layer, so each stage is a short dependency chain.
-//  * Two expert rows per warp, held in registers before the dependency wait;
-//    the dot products run as 8 independent partial sums (two rows x four
-//    chains) and both rows' warp reductions are interleaved.
-//  * Each warp stores its two logits into CTA 0's shared memory and arrives on
-//    CTA 0's mbarrier (release, cluster scope); only CTA 0's warp 0 waits, no
-//    cluster-wide barrier.
+//  * One expert row per warp (16 warps per CTA, 8 CTAs), held in registers
+//    before the dependency wait; the dot product runs as 4 independent
+//    partial sums.
+//  * Each warp sends its logit into CTA 0's shared memory with st.async,
+//    which completes 4 bytes on CTA 0's mbarrier (CTA 0 expects 4 * E): no
+//    fence, no cluster-wide barrier; only CTA 0's warp 0 waits.
 //  * Top-k: each lane sorts its 4 (logit, expert) keys, then k rounds of one
 //    redux.sync.max over the lanes' heads, the winner advancing; the softmax
 //    denominator's reduction runs between those rounds.
@@ -717,47 +717,36 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<T
 // arithmetic in the same order; the logits' fp32 partial sums are added in a
 // different order (within the rounding the tests allow for F.linear).
 constexpr int kT1MaxK = 8;
+constexpr int kT1Warps = kClusterMaxE / kClusterCTAs;  // 16: one expert row per warp
+constexpr int kT1Threads = kT1Warps * 32;
 template <typename TA>
-__global__ void __launch_bounds__(kRouterThreads) k1_router_t1(RouterArgs<TA> a) {
+__global__ void __launch_bounds__(kT1Threads) k1_router_t1(RouterArgs<TA> a) {
   static_assert(sizeof(TA) == 2, "16-bit activations");
   extern __shared__ __align__(128) uint8_t r_smem[];  // x row
   TA *xs = reinterpret_cast<TA *>(r_smem);
-  __shared__ float s_logit[kClusterMaxE];
+  __shared__ __align__(16) float s_logit[kClusterMaxE];
   __shared__ __align__(8) uint64_t bar;   // x copy
-  __shared__ __align__(8) uint64_t lbar;  // CTA 0: one arrival per warp of the cluster
+  __shared__ __align__(8) uint64_t lbar;  // CTA 0: 4 * E bytes of logits from the cluster
   constexpr int V = 8;
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int vpl = a.H / (V * 32);  // 16-byte vectors per lane and row (<= 8: host checks)
-  const int e0 = crank * (kRouterWarps * 2) + w * 2;
+  const int vpl = a.H / (V * 32);  // 16-byte vectors per lane (<= 8: host checks)
+  const int e = crank * kT1Warps + w;
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrEnter);
   if (tid == 0) {
     mbar_init(&bar, 1);
-    mbar_init(&lbar, kClusterCTAs * kRouterWarps);
+    mbar_init(&lbar, 1);
     mbar_init_fence_cluster();
+    if (crank == 0) mbar_arrive_expect_tx(&lbar, (uint32_t)a.E * 4u);
   }
-  uint4 row[2][8];
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int e = min(e0 + r, a.E - 1);  // rows past E compute a discarded copy of row E-1
-    const uint4 *src = reinterpret_cast<const uint4 *>(a.w + (int64_t)e * a.H);
+  uint4 row[8];
+  {
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.w + (int64_t)min(e, a.E - 1) * a.H);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      if (i < vpl) row[r][i] = ldg_stream(src + i * 32 + lane);
+      if (i < vpl) row[i] = ldg_stream(src + i * 32 + lane);
   }
-#ifdef TM_TRACE
-  {  // trace builds: when have this warp's rows arrived?
-    uint32_t d = 0u;
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i < vpl) d ^= row[r][i].x ^ row[r][i].y ^ row[r][i].z ^ row[r][i].w;
-    if (d == 0x9e3779b9u) s_logit[lane] = 0.f;
-    TM_TRACE_EVENT(a.pp.trace, kTrRouter, 5);
-  }
-#endif
   cluster.sync();  // every CTA runs and CTA 0's lbar is initialised (off the critical path)
   pdl_trigger();
   pdl_wait();  // x comes from the previous kernel
@@ -770,54 +759,34 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_t1(RouterArgs<TA> a)
   const bool ok = mbar_wait_bounded(&bar, 0);
   if (!ok && lane == 0) atomicOr(a.pp.status, TM_STATUS_TIMEOUT);
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
-  float acc[2][4];
-#pragma unroll
-  for (int r = 0; r < 2; ++r)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) acc[r][q] = 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (i < vpl) {
       const uint4 xq = *reinterpret_cast<const uint4 *>(xs + (i * 32 + lane) * V);
       const TA *xe = reinterpret_cast<const TA *>(&xq);
-      float xf[V];
+      const TA *qe = reinterpret_cast<const TA *>(&row[i]);
 #pragma unroll
-      for (int u = 0; u < V; ++u) xf[u] = Act<TA>::to_f(xe[u]);
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const TA *qe = reinterpret_cast<const TA *>(&row[r][i]);
-#pragma unroll
-        for (int u = 0; u < V; ++u) acc[r][u & 3] = fmaf(Act<TA>::to_f(qe[u]), xf[u], acc[r][u & 3]);
-      }
+      for (int u = 0; u < V; ++u) acc[u & 3] = fmaf(Act<TA>::to_f(qe[u]), Act<TA>::to_f(xe[u]), acc[u & 3]);
     }
   }
-  float s0 = (acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3]);
-  float s1 = (acc[1][0] + acc[1][1]) + (acc[1][2] + acc[1][3]);
+  float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 7);  // dot product reduced
+  if (lane == 0 && e < a.E) {
+    const float r = Act<TA>::round(sum);  // F.linear output in act dtype
+    st_async_u32(cluster_addr(&s_logit[e], 0), __float_as_uint(r), cluster_addr(&lbar, 0));
+    if (a.logits_out) a.logits_out[e] = Act<TA>::from_f(r);
   }
-  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 7);  // dot products reduced
-  if (lane == 0) {
-    float *logit0 = cluster.map_shared_rank(&s_logit[0], 0);
-    const float r0 = Act<TA>::round(s0), r1 = Act<TA>::round(s1);  // F.linear outputs in act dtype
-    if (e0 < a.E) logit0[e0] = r0;
-    if (e0 + 1 < a.E) logit0[e0 + 1] = r1;
-    if (a.logits_out) {
-      if (e0 < a.E) a.logits_out[e0] = Act<TA>::from_f(r0);
-      if (e0 + 1 < a.E) a.logits_out[e0 + 1] = Act<TA>::from_f(r1);
-    }
-    mbar_arrive_cluster(cluster_addr(&lbar, 0));
-  }
-  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 4);  // dot products done
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, 4);  // logit sent
   if (crank != 0) return;
   if (w != 0) {
-    for (int i = tid - 32; i < a.pp.k3_cnt_n; i += kRouterThreads - 32) a.pp.k3_cnt[i] = 0;
+    for (int i = tid - 32; i < a.pp.k3_cnt_n; i += kT1Threads - 32) a.pp.k3_cnt[i] = 0;
     return;
   }
   // CTA 0, warp 0.  Its limit is above every peer's own x wait (1 s), so a
-  // peer always arrives (and has made its stores) before this gives up.
+  // peer always has sent its logit before this gives up.
   if (!mbar_wait_cluster_bounded(&lbar, 0, 2000000000ull)) {
     if (lane == 0) atomicOr(a.pp.status, TM_STATUS_TIMEOUT);
     return;
@@ -1341,8 +1310,8 @@ struct RouterLaunch {
         a.n_etiles = kClusterCTAs;
         const dim3 grid(kClusterCTAs), block(kRouterThreads);
         if (T == 1 && k <= kT1MaxK)
-          return launch_cluster_pdl(k1_router_t1<TA>, grid, block, (size_t)H * sizeof(TA), kClusterCTAs, s,
-                                    "k1_router launch", a);
+          return launch_cluster_pdl(k1_router_t1<TA>, grid, dim3(kT1Threads), (size_t)H * sizeof(TA), kClusterCTAs,
+                                    s, "k1_router launch", a);
         const size_t smem = std::max((size_t)T * H * sizeof(TA), plan_smem(kRouterWarps, E));
         switch (T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8) {
           case 1: return launch_cluster_pdl(k1_router_cluster<TA, 1>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);

@@ -42,6 +42,8 @@ SIGNATURES = {
     "tm_router_topk": (_i, [_p, _i64, _i, _i, _p, _i, _i, _p, _p, _p, _p, _i64, _p]),
     "tm_route_plan": (_i, [_p, _i64, _i, _i, _p, _i64, _p]),
     "tm_moe_decode_gateup": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p, _p, _i64, _p]),
+    "tm_moe_decode_gateup_prefetch": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p, _p, _p, _p,
+                                           _i64, _p]),
     "tm_moe_decode_down_combine": (_i, [_i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _i, _p, _p, _p,
                                         _i64, _p]),
     "tm_moe_prefill_grouped": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p,

@@ -268,19 +268,26 @@ def route_plan(idx: torch.Tensor, n_experts: int, ws: Workspace):
 
 # --------------------------------------------------------------- K2/K3 ----
 def moe_gateup(x: torch.Tensor, top_k: int, packed: PackedExperts, ws: Workspace,
-               shared: PackedExperts | None = None, shared_gate_w: torch.Tensor | None = None):
-    """K2 alone: gate+up + SwiGLU for the plan already in ``ws`` (h stays in ``ws``)."""
+               shared: PackedExperts | None = None, shared_gate_w: torch.Tensor | None = None,
+               prefetch_down: bool = False):
+    """K2 alone: gate+up + SwiGLU for the plan already in ``ws`` (h stays in ``ws``).
+    ``prefetch_down``: also pull the down projections of the same experts into
+    L2 for the K3 call that follows (tm_moe_decode_gateup_prefetch)."""
     T, H = x.shape
     Is = shared.inter if shared is not None else 0
     if shared is not None and shared_gate_w is None:
         raise TurboMoEError("shared expert needs its gate weight")
     sgw = shared_gate_w.reshape(-1).to(x.dtype).contiguous() if shared is not None else None
     buf = ws.buf
-    check(lib().tm_moe_decode_gateup(x.data_ptr(), T, H, packed.inter, packed.n_experts, top_k, _code(x.dtype),
-                                     packed.w13.data_ptr(), packed.s13.data_ptr(),
-                                     _ptr(shared.w13) if shared else None, _ptr(shared.s13) if shared else None,
-                                     Is, _ptr(sgw), buf.data_ptr(), buf.numel(), _stream(x)),
-          "tm_moe_decode_gateup")
+    head = (x.data_ptr(), T, H, packed.inter, packed.n_experts, top_k, _code(x.dtype),
+            packed.w13.data_ptr(), packed.s13.data_ptr(),
+            _ptr(shared.w13) if shared else None, _ptr(shared.s13) if shared else None, Is, _ptr(sgw))
+    if prefetch_down:
+        check(lib().tm_moe_decode_gateup_prefetch(*head, packed.w2.data_ptr(), _ptr(shared.w2) if shared else None,
+                                                  buf.data_ptr(), buf.numel(), _stream(x)),
+              "tm_moe_decode_gateup_prefetch")
+    else:
+        check(lib().tm_moe_decode_gateup(*head, buf.data_ptr(), buf.numel(), _stream(x)), "tm_moe_decode_gateup")
 
 
 def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out: torch.Tensor,
@@ -358,7 +365,7 @@ def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: Pac
         moe_prefill(x, w, packed, ws, out, residual.contiguous() if residual is not None else None, shared,
                     shared_gate_w)
         return out
-    moe_gateup(x, k, packed, ws, shared, shared_gate_w)
+    moe_gateup(x, k, packed, ws, shared, shared_gate_w, prefetch_down=True)
     moe_down_combine(w, packed, ws, out, shared, residual.contiguous() if residual is not None else None)
     return out
 
