@@ -840,16 +840,27 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
     const int K = sh ? a.Is : a.I;
     const float *hf = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
     __half *hh = h16 + (size_t)e * hstride;
-    // this expert's h -> f16 with an exact power-of-2 shift (warp-local)
-    float m = 0.f;
-    for (int c = lane; c < K; c += 32) m = fmaxf(m, fabsf(hf[c]));
+    // this expert's h -> f16 with an exact power-of-2 shift (warp-local);
+    // K % 128 == 0, so each lane's loads come in groups of 4 (issued together)
+    float m4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+    for (int c = lane; c < K; c += 128) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) m4[u] = fmaxf(m4[u], fabsf(hf[c + 32 * u]));
+    }
+    float m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const int sh_exp = f16_shift(m);
     const float sc = ldexpf(1.0f, -sh_exp);
     if (lane == 0) s_back[e] = ldexpf(1.0f, sh_exp);
-    for (int c = lane * 2; c < K; c += 64)
-      *reinterpret_cast<__half2 *>(hh + c) = __floats2half2_rn(hf[c] * sc, hf[c + 1] * sc);
+#pragma unroll 2
+    for (int c = lane * 2; c < K; c += 128) {
+      const float2 v0 = *reinterpret_cast<const float2 *>(hf + c);
+      const float2 v1 = *reinterpret_cast<const float2 *>(hf + c + 64);
+      *reinterpret_cast<__half2 *>(hh + c) = __floats2half2_rn(v0.x * sc, v0.y * sc);
+      *reinterpret_cast<__half2 *>(hh + c + 64) = __floats2half2_rn(v1.x * sc, v1.y * sc);
+    }
     __syncwarp();
   }
   const bool ok = mbar_wait_bounded(&bar, 0);
@@ -869,26 +880,27 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
     const uint32_t wsm = smem_u32(k3_smem + (size_t)e * tile_r) + (lane & 15) * 16;
     const float *srow = s_sc[e];
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
     for (int blk = 0; blk < K / 128; ++blk) {
-      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};  // two independent MMA chains
+      // four independent MMA chains of two 16-column chunks each
+      float d[4][4];
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d[c][q] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
         const int kc = blk * 8 + i;
-        uint32_t r0, r1, r2, r3, a0, a1, a2, a3, c0, c1, c2, c3;
+        uint32_t r0, r1, a0, a1, a2, a3;
         ldsm_x2(wsm + kc * 256, r0, r1);
-        ldsm_x2(wsm + (kc + 1) * 256, r2, r3);
-        const uint2 bx0 = *reinterpret_cast<const uint2 *>(hrow + kc * 16);
-        const uint2 bx1 = *reinterpret_cast<const uint2 *>(hrow + (kc + 1) * 16);
+        const uint2 bx = *reinterpret_cast<const uint2 *>(hrow + kc * 16);
         e4m3x4_to_f16x2x2(r0, a0, a2);
         e4m3x4_to_f16x2x2(r1, a1, a3);
-        e4m3x4_to_f16x2x2(r2, c0, c2);
-        e4m3x4_to_f16x2x2(r3, c1, c3);
-        mma_16816(d0, a0, a1, a2, a3, bx0.x, bx0.y);
-        mma_16816(d1, c0, c1, c2, c3, bx1.x, bx1.y);
+        mma_16816(d[i & 3], a0, a1, a2, a3, bx.x, bx.y);
       }
       const float s = srow[blk];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[q] = fmaf(d0[q] + d1[q], s, acc[q]);
+      for (int q = 0; q < 4; ++q) acc[q] = fmaf((d[0][q] + d[1][q]) + (d[2][q] + d[3][q]), s, acc[q]);
     }
     // column 0 of D lives in lanes with t == 0: rows g (acc[0]) and g + 8 (acc[2])
     if (t == 0) {
