@@ -46,11 +46,14 @@ LAYERS = 48
 SEED = 1234
 # algorithmic bytes, one layer-token (T=1, E=128, k=8, H=2048, I=768)
 EXPERT_BYTES = 3 * 768 * 2048                      # 4,718,592 B FP8 per expert
-K2_BYTES = 8 * 2 * 768 * 2048 + 8 * 2 * 6 * 16 * 4 + 2048 * 2 + 8 * 768 * 4   # gate/up + scales + x + h
+# K2 (tm_moe_decode_gateup_prefetch) reads its own operands (gate/up weights +
+# scales + x, writes h) and pulls the 8 experts' down projections into L2 for K3
+K2_OWN_BYTES = 8 * 2 * 768 * 2048 + 8 * 2 * 6 * 16 * 4 + 2048 * 2 + 8 * 768 * 4   # 25,200,640
+K2_BYTES = K2_OWN_BYTES + 8 * 2048 * 768                                         # + 12,582,912 down
 LAYER_BYTES = 8 * EXPERT_BYTES + 8 * 288 * 4 + 128 * 2048 * 2 + 2 * 2048 * 2  # 38.29 MB
 # dram__bytes_read.sum + dram__bytes_write.sum of one K2 launch, from an ncu
-# capture of this workload (profiles/k2_gateup_decode_qwen3.md); None until measured
-K2_TRAFFIC = 25211648
+# capture of this workload (profiles/decode_kernels_qwen3_bs1.md)
+K2_TRAFFIC = 37795328
 
 
 def _peaks():
@@ -448,7 +451,8 @@ def run_ours(args, rank, world, local):
                 "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
                 "path": "RouterExecutor.compute_routing + MoEExecutor.execute_layer x48 captured in a CUDA graph",
                 "eager_value": round(world * args.tokens * args.steps / eager_s, 2)},
-        "roofline": {"bound": "hbm", "kernel": "k2_gateup (gate+up dequant-GEMV + SwiGLU)",
+        "roofline": {"bound": "hbm", "kernel": "k2_gateup (gate+up dequant-GEMV + SwiGLU; pulls the experts' down "
+                                                     "projections into L2 for K3)",
                      "achieved": round(k2_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(k2_gbs / peak, 4), "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": K2_BYTES, "launch_us": round(k2 * 1000, 3),
