@@ -304,6 +304,63 @@ __device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t v, uint32_t &lo, uint
       : "r"(v));
 }
 
+// d += A(16x32 e4m3) * B(32x8 e4m3), fp32 accumulators (products of two
+// e4m3 values are exact in fp32).
+__device__ __forceinline__ void mma_16832_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Power-of-2 exponent s that maps maxabs into [128, 256): v * 2^s then fits
+// e4m3 (max 448) with its top bits in the normal range; 0 for maxabs 0.
+__device__ __forceinline__ int e4m3_shift(float maxabs) {
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 0;
+  int e;
+  frexpf(maxabs, &e);
+  return max(-100, min(100, 8 - e));
+}
+
+// Two fp32 -> two e4m3 bytes (a -> low byte, b -> high byte), and back.
+__device__ __forceinline__ uint32_t e4m3x2_from(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+__device__ __forceinline__ float2 e4m3x2_value(uint32_t v) {
+  uint32_t h;
+  asm("{\n\t.reg .b16 p;\n\tcvt.u16.u32 p, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, p;\n\t}" : "=r"(h) : "r"(v));
+  return __half22float2(*reinterpret_cast<__half2 *>(&h));
+}
+
+// Four scaled activations v (already multiplied by 2^s, |v| < 256) as three
+// e4m3 terms, v ~= hi + mid / 16 + lo / 256, each term rounded to nearest:
+// 12 significant bits, so a bf16 or fp16 value is kept to within 2^-12 of
+// itself.  Bytes in element order, one u32 per term.
+__device__ __forceinline__ void e4m3_split3(const float (&v)[4], uint32_t &hi, uint32_t &mid, uint32_t &lo) {
+  float r[4];
+  hi = e4m3x2_from(v[0], v[1]) | (e4m3x2_from(v[2], v[3]) << 16);
+  {
+    const float2 p = e4m3x2_value(hi & 0xFFFFu), q = e4m3x2_value(hi >> 16);
+    r[0] = (v[0] - p.x) * 16.f;
+    r[1] = (v[1] - p.y) * 16.f;
+    r[2] = (v[2] - q.x) * 16.f;
+    r[3] = (v[3] - q.y) * 16.f;
+  }
+  mid = e4m3x2_from(r[0], r[1]) | (e4m3x2_from(r[2], r[3]) << 16);
+  {
+    const float2 p = e4m3x2_value(mid & 0xFFFFu), q = e4m3x2_value(mid >> 16);
+    r[0] = (r[0] - p.x) * 16.f;
+    r[1] = (r[1] - p.y) * 16.f;
+    r[2] = (r[2] - q.x) * 16.f;
+    r[3] = (r[3] - q.y) * 16.f;
+  }
+  lo = e4m3x2_from(r[0], r[1]) | (e4m3x2_from(r[2], r[3]) << 16);
+}
+
 // d += A(16x16 f16) * B(16x8 f16), fp32 accumulators.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {

@@ -468,6 +468,214 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
   TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrExit);
 }
 
+// One-token K2 on FP8 tensor cores: mma.sync m16n8k32 e4m3 x e4m3 reads the
+// packed weight tile as it is (no e4m3 -> f16 conversion), and the token
+// enters as three e4m3 terms x * 2^s ~= hi + mid/16 + lo/256 (12 significant
+// bits: within 2^-12 of each bf16/fp16 value), one per MMA column, so one MMA
+// of 32 weight columns serves all three.  Half the MMAs of k2_gateup_mma and
+// none of its conversions; fp32 accumulation, block scale per 128 columns.
+// Shared memory: tile, the three e4m3 rows of x (the raw row lands over mid and
+// lo first), block scales.
+template <typename TA>
+__global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t k2_smem[];
+  const int tile_bytes = 32 * a.H;
+  const int quarter = tile_bytes / kK2Warps;
+  uint8_t *wtile = k2_smem;
+  uint8_t *xb = k2_smem + tile_bytes;                          // [3][H] e4m3: hi, mid, lo
+  const TA *xraw = reinterpret_cast<const TA *>(xb + a.H);     // [H] act (before the split)
+  float *ssc = reinterpret_cast<float *>(xb + 3 * a.H);        // [2][H/128]
+  __shared__ float red[kK2Warps][2][kRows];
+  __shared__ float xmax[kK2Warps], s_gl[kK2Warps];
+  __shared__ int s_shift;
+  __shared__ __align__(8) uint64_t bar[kK2Warps];
+  __shared__ __align__(8) uint64_t xbar;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrEnter);
+  if (tid == 0) {
+    for (int q = 0; q < kK2Warps; ++q) mbar_init(&bar[q], 1);
+    mbar_init(&xbar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();  // the routing plan and x come from earlier kernels
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrWaited);
+  int b = blockIdx.x;
+  bool shared_expert;
+  int rg, slot0, I, eid = 0;
+  const uint8_t *wbase;
+  const float *sbase;
+  if (b < a.routed_ctas) {
+    shared_expert = false;
+    const int aidx = b / a.RG;
+    rg = b % a.RG;
+    const int n_active = ld_cg(a.pl.meta + kMetaNActive);
+    const int4 rec = ld_cg4(a.pl.act_rec + aidx);  // issued together with n_active
+    if (aidx >= n_active) return;
+    slot0 = rec.z;
+    I = a.I;
+    eid = rec.x;
+    wbase = a.w13 + (int64_t)rec.x * 2 * a.I * a.H;
+    sbase = a.s13 + (int64_t)rec.x * 2 * (a.I / 128) * (a.H / 128);
+  } else {
+    shared_expert = true;
+    rg = b - a.routed_ctas;
+    slot0 = 0;
+    I = a.Is;
+    wbase = a.sh_w13;
+    sbase = a.sh_s13;
+  }
+  if (tid == 0) {
+    const uint8_t *src = wbase + (int64_t)rg * tile_bytes;
+    const uint64_t pol = l2_evict_first();
+    for (int q = 0; q < kK2Warps; ++q) {
+      mbar_arrive_expect_tx(&bar[q], quarter);
+      tma_bulk_g2s_hint(wtile + q * quarter, src + q * quarter, quarter, &bar[q], pol);
+    }
+    const uint32_t rowb = (uint32_t)a.H * sizeof(TA);
+    mbar_arrive_expect_tx(&xbar, rowb);
+    tma_bulk_g2s(const_cast<TA *>(xraw), a.x, rowb, &xbar);  // the single token
+  }
+  pdl_trigger();
+  const int HB = a.H / 128, KC = a.H / 16;
+  const int ib = (rg * kRows) / 128;
+  for (int i = tid; i < 2 * HB; i += kK2Threads) ssc[i] = __ldg(sbase + ib * 2 * HB + i);
+  const bool gate_logit = shared_expert && rg == 0;
+  if (!tile_ready(&xbar, a.pl.status, 0)) {
+    if (tid == 0)
+      for (int q = 0; q < kK2Warps; ++q) mbar_wait_bounded(&bar[q], 0);
+    return;
+  }
+  // max |x| -> power-of-2 scale; optional shared-gate logit (fp32), same order
+  // as k2_gateup_mma
+  {
+    float m = 0.f, gl = 0.f;
+    const int c_lo = w * (a.H / kK2Warps), c_hi = c_lo + a.H / kK2Warps;
+    for (int c = c_lo + lane; c < c_hi; c += 32) {
+      const float v = Act<TA>::to_f(xraw[c]);
+      m = fmaxf(m, fabsf(v));
+      if (gate_logit) gl = fmaf(v, Act<TA>::to_f(__ldg(a.sh_gate_w + c)), gl);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (gate_logit) gl = warp_sum(gl);
+    if (lane == 0) {
+      xmax[w] = m;
+      s_gl[w] = gl;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float m = 0.f, gl = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kK2Warps; ++ww) {
+      m = fmaxf(m, xmax[ww]);
+      gl += s_gl[ww];
+    }
+    s_shift = e4m3_shift(m);
+    if (gate_logit) {
+      // F.linear output and torch.sigmoid both produce the act dtype (moe.py:81-83)
+      const float logit = Act<TA>::round(gl);
+      a.sh_w[0] = Act<TA>::round(1.0f / (1.0f + __expf(-logit)));
+    }
+  }
+  __syncthreads();
+  {  // split: every thread first reads its elements (the raw row overlaps mid/lo)
+    constexpr int kMaxSteps = 8;  // H <= 4096 (host checks)
+    const int steps = a.H / (4 * kK2Threads);
+    const float sc = ldexpf(1.0f, s_shift);
+    float v[kMaxSteps][4];
+#pragma unroll
+    for (int k = 0; k < kMaxSteps; ++k)
+      if (k < steps) {
+        const int c = 4 * (tid + k * kK2Threads);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[k][u] = Act<TA>::to_f(xraw[c + u]) * sc;
+      }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kMaxSteps; ++k)
+      if (k < steps) {
+        const int c = 4 * (tid + k * kK2Threads);
+        uint32_t h, md, l;
+        e4m3_split3(v[k], h, md, l);
+        *reinterpret_cast<uint32_t *>(xb + c) = h;
+        *reinterpret_cast<uint32_t *>(xb + a.H + c) = md;
+        *reinterpret_cast<uint32_t *>(xb + 2 * a.H + c) = l;
+      }
+  }
+  __syncthreads();
+  // this warp's quarter of the weight tile
+  if (!tile_ready(&bar[w], a.pl.status, 0)) {
+    if (tid == 0)
+      for (int q = 0; q < kK2Warps; ++q) mbar_wait_bounded(&bar[q], 0);
+    return;
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrData);
+  if (tid == 0) {  // this CTA's tile is in: HBM can carry K3's weights now
+    if (shared_expert) k2_prefetch_down(a.pf_sh_w2, (int64_t)a.H * a.Is, 0, rg, a.H);
+    else k2_prefetch_down(a.pf_w2, (int64_t)a.H * a.I, eid, rg, a.H);
+  }
+  const int cpw = KC / kK2Warps;  // 16-column chunks per warp
+  const int kc0 = w * cpw;
+  const int g = lane >> 2, t = lane & 3;
+  // A (ldmatrix.x4): lanes 0-15 rows 0-15 of chunk kc, lanes 16-31 of chunk kc+1
+  const uint32_t wsm = smem_u32(wtile) + (kc0 + (lane >> 4)) * 512 + (lane & 15) * 16;
+  // B column n = g: 0 hi, 1 mid, 2 lo (columns 3-7 repeat lo and are not read)
+  const uint8_t *xsel = xb + min(g, 2) * a.H + kc0 * 16 + 4 * t;
+  float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+  for (int blk = 0; blk < cpw / 8; ++blk) {
+    float dg[2][4], du[2][4];  // four independent MMA chains (two per operand)
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dg[c][q] = du[c][q] = 0.f;
+#pragma unroll
+    for (int st = 0; st < 4; ++st) {
+      const int kc = blk * 8 + 2 * st;
+      uint32_t g0, g1, g2, g3, u0, u1, u2, u3;
+      ldsm_x4(wsm + kc * 512, g0, g1, g2, g3);
+      ldsm_x4(wsm + kc * 512 + 256, u0, u1, u2, u3);
+      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xsel + kc * 16);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xsel + kc * 16 + 16);
+      mma_16832_e4m3(dg[st & 1], g0, g1, g2, g3, b0, b1);
+      mma_16832_e4m3(du[st & 1], u0, u1, u2, u3, b0, b1);
+    }
+    const int cb = (kc0 + blk * 8) / 8;
+    const float sg = ssc[cb], su = ssc[HB + cb];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      accg[q] = fmaf(dg[0][q] + dg[1][q], sg, accg[q]);
+      accu[q] = fmaf(du[0][q] + du[1][q], su, accu[q]);
+    }
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, 4);  // warp 0's MMAs done
+  // D: lane (g, t=0) holds columns hi, mid of rows g, g+8; lane (g, t=1) lo
+  const float lg0 = __shfl_down_sync(0xffffffffu, accg[0], 1), lg8 = __shfl_down_sync(0xffffffffu, accg[2], 1);
+  const float lu0 = __shfl_down_sync(0xffffffffu, accu[0], 1), lu8 = __shfl_down_sync(0xffffffffu, accu[2], 1);
+  if (t == 0) {
+    red[w][0][g] = accg[0] + (accg[1] + lg0 * 0.0625f) * 0.0625f;
+    red[w][0][g + 8] = accg[2] + (accg[3] + lg8 * 0.0625f) * 0.0625f;
+    red[w][1][g] = accu[0] + (accu[1] + lu0 * 0.0625f) * 0.0625f;
+    red[w][1][g + 8] = accu[2] + (accu[3] + lu8 * 0.0625f) * 0.0625f;
+  }
+  __syncthreads();
+  if (tid < kRows) {
+    float gs = 0.f, us = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kK2Warps; ++ww) {
+      gs += red[ww][0][tid];
+      us += red[ww][1][tid];
+    }
+    const float back = ldexpf(1.0f, -s_shift);
+    float *hout = shared_expert ? a.sh_h : a.h;
+    hout[(int64_t)slot0 * I + rg * kRows + tid] = silu(gs * back) * (us * back);
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrExit);
+}
+
 // =================================================================== K3 ====
 template <typename TA> struct DownArgs {
   const TA *topk_w;
@@ -922,6 +1130,186 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
   TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrExit);
 }
 
+// One-token K3 on FP8 tensor cores: as k3_down_t1_mma, but each expert's h
+// (fp32 from K2) enters as three e4m3 terms h * 2^s ~= hi + mid/16 + lo/256
+// (12 significant bits; the per-expert power-of-2 s from max |h|), one per MMA
+// column, and the packed e4m3 down tile is multiplied as it is by
+// mma.sync m16n8k32: half the MMAs, no weight conversion.
+template <typename TA>
+__global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t k3_smem[];
+  __shared__ float ysm[kK3T1MaxExperts][kRows];
+  __shared__ float s_sc[kK3T1MaxExperts][kK3T1MaxKB];  // block scales of this CTA's 16 rows
+  __shared__ float s_back[kK3T1MaxExperts];            // 2^-shift that undoes h's scaling
+  __shared__ int4 s_rec[kK3T1MaxExperts];
+  __shared__ int s_slot[32], s_map[32];   // pair -> slot, slot -> active expert
+  __shared__ float s_w[32];
+  __shared__ __align__(8) uint64_t bar;   // weight tiles
+  __shared__ __align__(8) uint64_t hbar;  // h of every slot
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int rgo = blockIdx.x;
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrEnter);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    mbar_init(&hbar, 1);
+    mbar_fence_init();
+  }
+  // plan (the router completed before this grid could start, see k3_down)
+  const int n_active = ld_cg(a.pl.meta + kMetaNActive);
+  const int n_exp = n_active + a.has_shared;  // <= kK3T1MaxExperts (host checks the bound)
+  if (tid < n_active) s_rec[tid] = ld_cg4(a.pl.act_rec + tid);
+  if (tid < a.k) {
+    s_slot[tid] = ld_cg(a.pl.pair_slot + tid);
+    s_w[tid] = Act<TA>::to_f(Act<TA>::ld_cg(a.topk_w + tid));
+  }
+  __syncthreads();
+  const int tile_r = kRows * a.I, tile_s = kRows * a.Is;
+  const int Kmax = max(a.I, a.Is);
+  // [routed tiles][shared tile][h fp32: k slots x I, then Is][h e4m3: 3 x Kmax per expert]
+  float *hs = reinterpret_cast<float *>(k3_smem + (size_t)n_active * tile_r + tile_s);
+  uint8_t *h8 = reinterpret_cast<uint8_t *>(hs + (size_t)a.k * a.I + a.Is);
+  if (tid < n_active)
+    for (int c = 0; c < s_rec[tid].y; ++c) s_map[s_rec[tid].z + c] = tid;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar, n_active * tile_r + (a.has_shared ? tile_s : 0));
+    for (int e = 0; e < n_active; ++e)
+      tma_bulk_g2s_hint(k3_smem + (size_t)e * tile_r,
+                        a.w2 + (int64_t)s_rec[e].x * a.H * a.I + (int64_t)rgo * tile_r, tile_r, &bar,
+                        l2_evict_first());
+    if (a.has_shared)
+      tma_bulk_g2s_hint(k3_smem + (size_t)n_active * tile_r, a.sh_w2 + (int64_t)rgo * tile_s, tile_s, &bar,
+                        l2_evict_first());
+  }
+  // block scales into shared memory now (weights: independent of K2), not
+  // one dependent global load per 128 columns inside the MMA loop
+  {
+    const int KB = a.I / 128, KBs = a.Is / 128, rb = (rgo * kRows) / 128;
+    for (int i = tid; i < n_exp * kK3T1MaxKB; i += kK3T1Threads) {
+      const int e = i / kK3T1MaxKB, b = i % kK3T1MaxKB;
+      if (e == n_active) {
+        if (b < KBs) s_sc[e][b] = __ldg(a.sh_s2 + (int64_t)rb * KBs + b);
+      } else if (b < KB) {
+        s_sc[e][b] = __ldg(a.s2 + ((int64_t)s_rec[e].x * (a.H / 128) + rb) * KB + b);
+      }
+    }
+  }
+  // the residual (this layer's input, complete before the router that
+  // preceded K2 could pass its own wait) is loaded now, off the tail
+  float res_pre = 0.f;
+  if (tid < kRows && a.residual) res_pre = Act<TA>::to_f(Act<TA>::ld_cg(a.residual + rgo * kRows + tid));
+  pdl_trigger();
+  pdl_wait();  // K2 (h) has completed
+  const float shw = (a.has_shared && tid < kRows) ? ld_cg(a.sh_w) : 0.f;  // gate score from K2
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrWaited);
+  if (tid == 0) {
+    const uint32_t hb = (uint32_t)a.k * a.I * sizeof(float), hsb = (uint32_t)a.Is * sizeof(float);
+    mbar_arrive_expect_tx(&hbar, hb + (a.has_shared ? hsb : 0));
+    tma_bulk_g2s(hs, a.h, hb, &hbar);  // slots 0..k-1 of the single token
+    if (a.has_shared) tma_bulk_g2s(hs + (size_t)a.k * a.I, a.sh_h, hsb, &hbar);
+  }
+  const bool hok = mbar_wait_bounded(&hbar, 0);
+  if (__syncthreads_or(!hok)) {
+    if (tid == 0) {
+      atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(&bar, 0);
+      mbar_wait_bounded(&hbar, 0);
+    }
+    return;
+  }
+  const int g = lane >> 2, t = lane & 3;
+  for (int e = w; e < n_exp; e += kK3T1Warps) {
+    const bool sh = e == n_active;
+    const int K = sh ? a.Is : a.I;
+    const float *hf = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
+    uint8_t *he = h8 + (size_t)e * 3 * Kmax;
+    // this expert's h -> three e4m3 terms with a power-of-2 scale (warp-local);
+    // K % 128 == 0, so each lane's loads come in groups of 4 (issued together)
+    float m4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+    for (int c = lane; c < K; c += 128) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) m4[u] = fmaxf(m4[u], fabsf(hf[c + 32 * u]));
+    }
+    float m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int sh_exp = e4m3_shift(m);
+    const float sc = ldexpf(1.0f, sh_exp);
+    if (lane == 0) s_back[e] = ldexpf(1.0f, -sh_exp);
+#pragma unroll 2
+    for (int c = 4 * lane; c < K; c += 128) {
+      const float4 q = *reinterpret_cast<const float4 *>(hf + c);
+      float v[4] = {q.x * sc, q.y * sc, q.z * sc, q.w * sc};
+      uint32_t th, tm, tl;
+      e4m3_split3(v, th, tm, tl);
+      *reinterpret_cast<uint32_t *>(he + c) = th;
+      *reinterpret_cast<uint32_t *>(he + Kmax + c) = tm;
+      *reinterpret_cast<uint32_t *>(he + 2 * Kmax + c) = tl;
+    }
+    __syncwarp();
+  }
+  const bool ok = mbar_wait_bounded(&bar, 0);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) {
+      atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(&bar, 0);
+    }
+    return;
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrData);
+  for (int e = w; e < n_exp; e += kK3T1Warps) {
+    const bool sh = e == n_active;
+    const int K = sh ? a.Is : a.I;
+    const float back = s_back[e];  // written by this warp in the conversion pass
+    // A (ldmatrix.x4): lanes 0-15 rows 0-15 of chunk kc, lanes 16-31 of chunk kc+1
+    const uint32_t wsm = smem_u32(k3_smem + (size_t)e * tile_r) + (lane >> 4) * 256 + (lane & 15) * 16;
+    // B column n = g: 0 hi, 1 mid, 2 lo (columns 3-7 repeat lo and are not read)
+    const uint8_t *hsel = h8 + (size_t)e * 3 * Kmax + min(g, 2) * Kmax + 4 * t;
+    const float *srow = s_sc[e];
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+    for (int blk = 0; blk < K / 128; ++blk) {
+      float d[4][4];  // four independent MMA chains, one 32-column step each
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d[c][q] = 0.f;
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        const int kc = blk * 8 + 2 * st;
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(wsm + kc * 256, a0, a1, a2, a3);
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(hsel + kc * 16);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(hsel + kc * 16 + 16);
+        mma_16832_e4m3(d[st], a0, a1, a2, a3, b0, b1);
+      }
+      const float s = srow[blk];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = fmaf((d[0][q] + d[1][q]) + (d[2][q] + d[3][q]), s, acc[q]);
+    }
+    // D: lane (g, t=0) holds columns hi, mid of rows g (acc[0], acc[1]) and
+    // g + 8 (acc[2], acc[3]); lane (g, t=1) holds lo in acc[0], acc[2]
+    const float lo0 = __shfl_down_sync(0xffffffffu, acc[0], 1), lo8 = __shfl_down_sync(0xffffffffu, acc[2], 1);
+    if (t == 0) {
+      ysm[e][g] = (acc[0] + (acc[1] + lo0 * 0.0625f) * 0.0625f) * back;
+      ysm[e][g + 8] = (acc[2] + (acc[3] + lo8 * 0.0625f) * 0.0625f) * back;
+    }
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, 4);  // warp 0's MMAs done
+  __syncthreads();
+  if (tid < kRows) {
+    float y = 0.f;
+    for (int kk = 0; kk < a.k; ++kk)
+      if (s_slot[kk] >= 0) y = fmaf(s_w[kk], ysm[s_map[s_slot[kk]]][tid], y);
+    if (a.has_shared) y = fmaf(shw, ysm[n_active][tid], y);
+    const int nn = rgo * kRows + tid;
+    if (a.residual) y += res_pre;
+    a.out[nn] = Act<TA>::from_f(y);
+  }
+  TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrExit);
+}
+
 template <typename TA>
 __global__ void __launch_bounds__(256) k3_combine(DownArgs<TA> a) {
   // grid: (H / 16, ceil(T / 16)); 16 tokens x 16 rows per CTA
@@ -944,6 +1332,10 @@ struct GateUpLaunch {
   const uint8_t *pf_w2 = nullptr, *pf_sh_w2 = nullptr;  // down projections to pull into L2 (optional)
   template <typename TA, int kNT> int go(GateUpArgs<TA> &a, int grid) {
     if constexpr (sizeof(TA) == 2) {
+      if (kNT == 1 && T == 1 && H <= 4096) {  // one token: FP8 MMAs on the split activation
+        const size_t smem = (size_t)32 * H + (size_t)3 * H + 2 * (H / 128) * sizeof(float);
+        return launch_pdl(k2_gateup_f8<TA>, dim3(grid), dim3(kK2Threads), smem, s, "k2_gateup launch", a);
+      }
       // tile + x rows (f16, padded; >= the 4 KB reduction area) + block scales
       const size_t smem = (size_t)32 * H + std::max<size_t>((size_t)kNT * (H + 8) * 2, 4096) +
                           2 * (H / 128) * sizeof(float);
@@ -1015,6 +1407,10 @@ struct DownLaunch {
         std::max(I, a.Is) <= 128 * kK3T1MaxKB) {
       size_t smem = (size_t)max_active * kRows * I + (size_t)kRows * a.Is + ((size_t)k * I + a.Is) * sizeof(float);
       if constexpr (sizeof(TA) == 2) {
+        const size_t smem8 = smem + (size_t)(max_active + a.has_shared) * 3 * std::max(I, a.Is);
+        if (smem8 <= 200 * 1024)
+          return launch_pdl(k3_down_t1_f8<TA>, dim3(a.RGo), dim3(kK3T1Threads), smem8, s,
+                            "k3_down_t1 launch", a);
         smem += (size_t)(max_active + a.has_shared) * (std::max(I, a.Is) + 8) * 2;
         if (smem <= 200 * 1024)
           return launch_pdl(k3_down_t1_mma<TA>, dim3(a.RGo), dim3(kK3T1Threads), smem, s,
