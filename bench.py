@@ -53,7 +53,7 @@ K2_BYTES = K2_OWN_BYTES + 8 * 2048 * 768                                        
 LAYER_BYTES = 8 * EXPERT_BYTES + 8 * 288 * 4 + 128 * 2048 * 2 + 2 * 2048 * 2  # 38.29 MB
 # dram__bytes_read.sum + dram__bytes_write.sum of one K2 launch, from an ncu
 # capture of this workload (profiles/decode_kernels_qwen3_bs1.md)
-K2_TRAFFIC = 37795328
+K2_TRAFFIC = 37772800
 
 
 def _peaks():
