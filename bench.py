@@ -503,6 +503,10 @@ def run_ep(args, rank, world, local):
         local_experts = ops.pack_experts(lw.gate[sl], lw.gate_s[sl], lw.up[sl], lw.up_s[sl], lw.down[sl],
                                          lw.down_s[sl])
         router_w = lw.router.to(torch.bfloat16).contiguous()
+        if args.ep_zipf > 0:  # skewed routing: logit bias log p_e carried by the last coordinate
+            router_w = synth.router_with_bias(router_w, synth.zipf_expert_bias(E, SEED + l, args.ep_zipf)).contiguous()
+        if l == 0:
+            router_w0 = router_w
         del lw
         if peer:
             layers.append(PeerExpertParallelMoE(router_w, local_experts, k, max_tokens=T))
@@ -510,7 +514,17 @@ def run_ep(args, rank, world, local):
             layers.append(ExpertParallelMoE(E, k, *cuda_functions(router_w, local_experts, k, E, H, I)))
     torch.cuda.empty_cache()
     x0 = synth.make_hidden(T, H, SEED + 100 + rank, rms_normalise=True, device=dev)
+    if args.ep_zipf > 0:
+        x0 = synth.tokens_for_bias(x0)
     bufs = [torch.empty_like(x0) for _ in range(2)]
+    # load balance of the first layer: routed pairs per owner rank, all ranks' tokens
+    ws0 = ops.Workspace(dev, E, k, H, I)
+    idx0, _ = ops.router_topk(x0, router_w0, k, ws0)
+    owner_pairs = torch.bincount(idx0.reshape(-1) // E_loc, minlength=world).to(torch.float64)
+    if world > 1:
+        dist.all_reduce(owner_pairs)
+    owner_imbalance = float(owner_pairs.max() / owner_pairs.mean())
+    del ws0, idx0
 
     def step(x):
         for i, ep in enumerate(layers):
@@ -563,7 +577,11 @@ def run_ep(args, rank, world, local):
            "value": round(T * world * args.steps / (ms / 1000.0), 1), "unit": "tokens/s", "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-           "dtype": "e4m3 weights, bf16 act, fp32 math", "data": "synthetic (seeded weights, uniform routing)",
+           "dtype": "e4m3 weights, bf16 act, fp32 math",
+           "data": "synthetic (seeded weights, " + (f"Zipf routing s={args.ep_zipf}: logit bias log p_e, p_e ~ "
+                                                    "rank^-s over a seeded expert permutation)"
+                                                    if args.ep_zipf > 0 else "uniform routing)"),
+           "owner_load_max_over_mean": round(owner_imbalance, 3),
            "config": {"workload": f"{args.ep_tokens} sequences x 1 token through {args.layers} MoE layers, "
                                   f"experts sharded {E_loc} per GPU, " +
                                   ("dispatch/return by NVLink peer stores (tm_ep_*), step in one CUDA graph"
@@ -657,6 +675,8 @@ def main():
     ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
                     help="decode: batch-1 decode (replicas for N>1); ep: expert-parallel batched decode")
     ap.add_argument("--ep-tokens", type=int, default=256, help="ep workload: sequences over all ranks")
+    ap.add_argument("--ep-zipf", type=float, default=0.0,
+                    help="ep workload: Zipf exponent of the expert popularity (0: uniform routing)")
     ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",
                     help="ep workload: NVLink peer-memory kernels (tm_ep_*) or NCCL all-to-all")
     args = ap.parse_args()

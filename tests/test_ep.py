@@ -111,3 +111,34 @@ def test_ep_skewed_routing_and_idle_ranks():
     # every row goes to rank 0; rank 1 receives none
     assert sum(res[1][2][1]) == 0
     assert sum(res[0][2][1]) == sum(sum(r[2][0]) for r in res)
+
+
+def test_zipf_routing_bias_skews_owner_load():
+    """The skewed-routing workload (bench.py --workload ep --ep-zipf 1.2): the
+    bias is log p_e with p_e ~ rank^-1.2 over a seeded permutation (hottest 0),
+    carried exactly by one coordinate, and it concentrates the routed pairs on
+    few experts; s = 0 keeps the routing balanced."""
+    import torch
+    from turbomoe import synth
+    from oracle import moe_oracle as O
+    E, H, k, G = 64, 512, 8, 8
+    b = synth.zipf_expert_bias(E, 3, 1.2)
+    assert b.max().item() == 0.0
+    ranks = torch.exp(-b / 1.2).round()
+    assert sorted(ranks.tolist()) == list(range(1, E + 1))
+    assert torch.equal(b, synth.zipf_expert_bias(E, 3, 1.2))      # seeded
+    shape = synth.MoEShape(H, 256, E, k, 0)
+    lw = synth.make_layer(shape, 11, 0)
+    x = synth.make_hidden(512, H, 4, rms_normalise=True)
+    w = synth.router_with_bias(lw.router, b)
+    xb = synth.tokens_for_bias(x)
+    # the bias is carried exactly: logits = W x (coordinate H-1 excluded) + bias
+    ref = x.float()[:, :-1] @ lw.router.float()[:, :-1].T + b.to(torch.bfloat16).float()
+    assert torch.allclose(xb.float() @ w.float().T, ref, atol=1e-4)
+    loads = {}
+    for s in (0.0, 1.2):
+        wb = synth.router_with_bias(lw.router, synth.zipf_expert_bias(E, 3, s))
+        idx, _ = O.compute_routing(xb, wb, k)
+        per_owner = torch.bincount(idx.reshape(-1) // (E // G), minlength=G).float()
+        loads[s] = (per_owner.max() / per_owner.mean()).item()
+    assert loads[0.0] < 1.25 and loads[1.2] > 1.5

@@ -126,6 +126,39 @@ def make_hidden(tokens: int, hidden: int, seed: int, rms_normalise=False,
     return x.to(dtype)
 
 
+def zipf_expert_bias(experts: int, seed: int, s: float = 1.2) -> torch.Tensor:
+    """Per-expert logit bias log p_e with p_e proportional to rank_e^-s over a
+    seeded permutation of the experts (rank 1 = the hottest), shifted so the
+    hottest expert's bias is 0: the skewed-routing workload of batched decode
+    (a few experts receive most tokens)."""
+    g = torch.Generator()
+    g.manual_seed(int(seed) * 131 + 17)
+    perm = torch.randperm(experts, generator=g)
+    rank = torch.empty(experts)
+    rank[perm] = torch.arange(1, experts + 1, dtype=torch.float32)
+    return -float(s) * torch.log(rank)
+
+
+def router_with_bias(router_w: torch.Tensor, bias: torch.Tensor, dim: int | None = None) -> torch.Tensor:
+    """Carry a per-expert logit bias through an unchanged router: router
+    column ``dim`` (default the last) is replaced by the bias, so for tokens
+    whose coordinate ``dim`` is 1 (``tokens_for_bias``) the logits are
+    sum_{j != dim} W[e, j] x[j] + bias[e].  Returns a new tensor."""
+    d = router_w.shape[1] - 1 if dim is None else dim
+    w = router_w.clone()
+    w[:, d] = bias.to(device=w.device, dtype=w.dtype)
+    return w
+
+
+def tokens_for_bias(x: torch.Tensor, dim: int | None = None) -> torch.Tensor:
+    """Copy of the tokens ``x`` [T, H] with coordinate ``dim`` (default the
+    last) set to 1, the carrier of ``router_with_bias``'s bias."""
+    d = x.shape[1] - 1 if dim is None else dim
+    xb = x.clone()
+    xb[:, d] = 1
+    return xb
+
+
 def tensor_names(layer: int, expert: int, prefix="model.layers"):
     p = f"{prefix}.{layer}.mlp.experts.{expert}"
     return {m: f"{p}.{m}.weight" for m in ("gate_proj", "up_proj", "down_proj")}
