@@ -83,3 +83,19 @@ def test_ops_refuse_cpu_tensors():
     from turbomoe import ops
     with pytest.raises(_lib.TurboMoEError):
         ops.dequant_fp8_block(torch.zeros(128, 128, dtype=torch.uint8), torch.ones(1, 1))
+
+
+def test_gateup_prefetch_argument_errors_without_launch():
+    """tm_moe_decode_gateup_prefetch rejects missing down projections, bad
+    shapes and unaligned pointers on the host, before any CUDA call."""
+    L = _lib.lib()
+    f = L.tm_moe_decode_gateup_prefetch
+    # x, T, H, I, E, k, dtype, w13, s13, sh_w13, sh_s13, Is, sh_gate, w2, sh_w2, ws, ws_bytes, stream
+    rc = f(16, 1, 2048, 768, 128, 8, 2, 16, 16, None, None, 0, None, None, None, 256, 1 << 30, None)
+    assert rc == _lib.TM_ERR_INVALID and b"null" in L.tm_last_error()          # no w2
+    rc = f(16, 1, 2000, 768, 128, 8, 2, 16, 16, None, None, 0, None, 16, None, 256, 1 << 30, None)
+    assert rc == _lib.TM_ERR_INVALID and b"hidden" in L.tm_last_error()
+    rc = f(16, 1, 2048, 768, 128, 8, 2, 16, 16, 16, 16, 512, 16, 16, None, 256, 1 << 30, None)
+    assert rc == _lib.TM_ERR_INVALID and b"shared expert" in L.tm_last_error()  # shared w13 without sh_w2
+    rc = f(16, 1, 2048, 768, 128, 8, 2, 24, 16, None, None, 0, None, 16, None, 256, 1 << 30, None)
+    assert rc == _lib.TM_ERR_INVALID and b"aligned" in L.tm_last_error()
