@@ -51,9 +51,12 @@ EXPERT_BYTES = 3 * 768 * 2048                      # 4,718,592 B FP8 per expert
 K2_OWN_BYTES = 8 * 2 * 768 * 2048 + 8 * 2 * 6 * 16 * 4 + 2048 * 2 + 8 * 768 * 4   # 25,200,640
 K2_BYTES = K2_OWN_BYTES + 8 * 2048 * 768                                         # + 12,582,912 down
 LAYER_BYTES = 8 * EXPERT_BYTES + 8 * 288 * 4 + 128 * 2048 * 2 + 2 * 2048 * 2  # 38.29 MB
-# dram__bytes_read.sum + dram__bytes_write.sum of one K2 launch, from an ncu
-# capture of this workload (profiles/decode_kernels_qwen3_bs1.md)
+# dram__bytes_read.sum + dram__bytes_write.sum of one K2 launch of this
+# workload, read from an ncu capture (not measured by this script: ncu replays
+# kernels, so it cannot run inside a timed bench)
 K2_TRAFFIC = 37772800
+K2_TRAFFIC_SOURCE = ("ncu --set full capture of k2_gateup_f8 in this workload (4-layer decode step, "
+                     "dram__bytes_read.sum + dram__bytes_write.sum of one launch)")
 
 
 def _peaks():
@@ -457,7 +460,7 @@ def run_ours(args, rank, world, local):
                      "frac": round(k2_gbs / peak, 4), "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": K2_BYTES, "launch_us": round(k2 * 1000, 3),
                      "launch_timing": "marginal device time of K2 in a CUDA graph of 48 layers (events)",
-                     "traffic": K2_TRAFFIC},
+                     "traffic": K2_TRAFFIC, "traffic_source": K2_TRAFFIC_SOURCE},
         "moe_layer": {"gbs": round(layer_gbs, 1), "frac": round(layer_gbs / peak, 4),
                       "bytes_per_layer": LAYER_BYTES, "us_per_layer": round(ms_per_step * 1000 / LAYERS, 3),
                       "k3_us": round(k3 * 1000, 3)},

@@ -45,6 +45,8 @@ typedef enum { TM_DTYPE_F32 = 0, TM_DTYPE_F16 = 1, TM_DTYPE_BF16 = 2 } tm_dtype;
 /* Device-side status bits written into the workspace (tm_workspace_status). */
 #define TM_STATUS_BAD_EXPERT_ID 1u  /* a top-k index was outside [0, n_experts) */
 #define TM_STATUS_TIMEOUT 2u        /* a bounded device-side wait gave up; outputs are invalid */
+#define TM_STATUS_PEER_FAILED 4u    /* expert parallelism: an owner rank gave up on this call (it timed
+                                       out waiting for a source); this rank's outputs are invalid */
 
 int tm_abi_version(void);
 const char *tm_last_error(void);
@@ -230,11 +232,19 @@ int tm_combine_slots(const void *y, const void *topk_w, const int32_t *pair_slot
  * by every GPU that loads the library until exit, and allocates nothing.
  *   - Calls whose tm_workspace_bytes(tokens, n_experts, top_k, hidden, inter,
  *     shared_inter) exceeds TM_NOALLOC_SCRATCH_BYTES are rejected with
- *     TM_ERR_WORKSPACE (8 MiB covers 64 tokens of Qwen3-30B-A3B and Qwen3.5
- *     MoE layers).
+ *     TM_ERR_WORKSPACE.  8 MiB covers 64 tokens of a Qwen3-30B-A3B layer
+ *     (E 128, top-8, H 2048, I 768: 6.1 MiB) and of a Qwen3.5 layer (E 256,
+ *     top-8, H 2048, I 512, shared I 512: 5.9 MiB); larger shapes fit fewer
+ *     tokens (E 512, top-10, H 4096, I 1024 needs 14.2 MiB at 64 tokens), so
+ *     check your own shape with tm_workspace_bytes.
+ *   - It always runs the decode kernels (K1, K2 with the L2 prefetch of the
+ *     down projections, K3), never the tcgen05 grouped GEMMs that the
+ *     workspace path switches to from 16 tokens: calls of 16-64 tokens are
+ *     slower here than through the workspace entry points.
  *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture.
+ *     (cudaGetSymbolAddress, with that device current) and caches it with the
+ *     device's current CUDA context; a call under another context looks it up
+ *     again.  Make that first call before any stream capture.
  *   - Every call shares the array; each call clears its header first.  Calls
  *     that overlap on the GPU (other streams or threads on the same device)
  *     race on it: order them on one stream.
@@ -287,8 +297,14 @@ int tm_fp8_linear(const void *x, int64_t tokens, int in_features, int out_featur
  * No host synchronisation: the sequence is CUDA-graph capturable.  Every
  * device-side wait is bounded (tm_ep_set_timeout, default 2 s); on expiry
  * TM_STATUS_TIMEOUT is set in the context status (tm_ep_status) and the call's
- * outputs are invalid.  Tokens per call may differ between ranks (each at most
- * max_tokens).  bf16/fp16 activations; hidden % 256 == 0, inter % 128 == 0. */
+ * outputs are invalid.  An owner that timed out waiting for a source returns
+ * nothing and tells every source, which sets TM_STATUS_PEER_FAILED: each rank
+ * whose outputs of the call are invalid sees a status bit.  A context whose
+ * status showed either bit may still receive late rows of the failed call:
+ * disconnect and destroy it on every rank (host barriers around both) and
+ * create a new one before the next call.  Tokens per call may differ between
+ * ranks (each at most max_tokens).  bf16/fp16 activations; hidden % 256 == 0,
+ * inter % 128 == 0. */
 #define TM_EP_MAX_RANKS 8
 #define TM_EP_HANDLE_BYTES 64
 typedef struct tm_ep_ctx tm_ep_ctx;

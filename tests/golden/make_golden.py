@@ -1,8 +1,8 @@
 """Generate the golden fixtures by running the REFERENCE itself.
 
-Run in the container where the reference checkout is mounted:
+Run where a checkout of the reference is available, giving its path:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path to the reference checkout>
 
 It writes seeded synthetic FP8 checkpoints to a temporary directory, imports
 the reference's ``ExpertLoader`` (loader/expert_loader.py), ``RouterExecutor``
@@ -160,4 +160,6 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the reference checkout>")
+    main(sys.argv[1])

@@ -63,6 +63,23 @@ def test_loader_interface(ckpt):
     assert torch.equal(full.cpu(), O.dequantize_weight(lw.up[5], lw.up_s[5], torch.bfloat16))
     out, c_ms, d_ms = L.load_weight_split("model.layers.1.mlp.experts.5.up_proj.weight")
     assert torch.equal(out, full) and c_ms >= 0 and d_ms >= 0
+    # prefill-time fetch (load_expert_dynamic): fresh tensors, the reference's dequantisation
+    hits = L.gpu_hits
+    dg, du, dd = L.load_expert_dynamic(0, 7)
+    lw0 = synth.make_layer(shape, 77, 0)
+    for got, q, s_ in ((dg, lw0.gate[7], lw0.gate_s[7]), (du, lw0.up[7], lw0.up_s[7]),
+                       (dd, lw0.down[7], lw0.down_s[7])):
+        assert got.is_cuda and got.dtype == torch.bfloat16
+        assert torch.equal(got.cpu(), O.dequantize_weight(q, s_, torch.bfloat16))
+    assert L.gpu_hits == hits + 1
+    dg.zero_()                        # not a view of anything the next call returns
+    dg2, _, _ = L.load_expert_dynamic(0, 7)
+    assert torch.equal(dg2.cpu(), O.dequantize_weight(lw0.gate[7], lw0.gate_s[7], torch.bfloat16))
+    # raw FP8 + scales of one expert (load_expert_raw)
+    raw = L.load_expert_raw(0, 7)
+    assert len(raw) == 6
+    assert torch.equal(raw[0].cpu().view(torch.uint8), lw0.gate[7].view(torch.uint8))
+    assert torch.equal(raw[5].cpu(), lw0.down_s[7].float())
     for a in ("DEVICE", "dtype", "layout", "weight_map", "expert_cache", "expert_metadata", "cache_limit",
               "num_slots", "ram_cache", "gpu_hits", "ram_hits", "ssd_hits", "load_ms_accum",
               "dequant_ms_accum", "evict_ms_accum", "lock"):

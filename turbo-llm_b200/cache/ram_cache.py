@@ -1,14 +1,15 @@
-"""Host LRU cache of raw FP8 expert tuples (interface of the reference's
-cache/ram_cache.py:6-101, kept for callers that read its stats).
+"""Host RAM tier of the expert cache: the interface of the reference's
+cache/ram_cache.py:6-101, kept for the engine and the backend, which read
+``stats()`` (runtime/engine.py:327-337, backend/api/routes/metrics.py:52,101).
 
-With the packed, fully device-resident expert layout the MoE path never
-streams experts from host memory, so the loader only uses this cache as a
-staging record; the eviction policy (least recently used, byte budget of a
-percentage of available RAM) is the reference's.
+With every expert of every layer packed once into device memory
+(``ExpertLoader.upload``), no expert is ever staged in host RAM: the MoE path
+has no RAM or SSD miss to serve.  So this tier holds nothing.  ``put`` is
+accepted and dropped, ``get`` always misses, and ``stats()`` reports an empty
+cache against the reference's byte budget (a percentage of available RAM,
+``memory.max_ram_percent``, default 35).
 """
 from __future__ import annotations
-
-from collections import OrderedDict
 
 import psutil
 
@@ -16,9 +17,8 @@ import psutil
 class RAMCache:
 
     def __init__(self, config=None):
-        self.cache = OrderedDict()
-        self.current = 0
         self.config = config
+        self.current = 0
         self.max_bytes = self.compute_limit()
 
     def compute_limit(self):
@@ -27,40 +27,20 @@ class RAMCache:
             pct = self.config["memory"]["max_ram_percent"]
         return int(psutil.virtual_memory().available * (pct / 100.0))
 
-    @staticmethod
-    def _size(value):
-        if isinstance(value, (list, tuple)):
-            return sum(t.numel() * t.element_size() for t in value if t is not None)
-        return value.numel() * value.element_size()
-
     def get(self, key):
-        if key not in self.cache:
-            return None
-        self.cache.move_to_end(key)
-        return self.cache[key][0]
+        return None
 
     def put(self, key, value):
-        size = self._size(value)
-        if size > self.max_bytes:
-            return
-        if key in self.cache:
-            self.current -= self.cache.pop(key)[1]
-        while self.current + size > self.max_bytes and self.cache:
-            _, (_, old) = self.cache.popitem(last=False)
-            self.current -= old
-        self.cache[key] = (value, size)
-        self.current += size
+        return None
 
     def clear(self):
-        self.cache.clear()
         self.current = 0
 
     def stats(self):
-        return {"entries": len(self.cache), "current_bytes": self.current, "max_bytes": self.max_bytes,
-                "usage_percent": 100 * self.current / self.max_bytes if self.max_bytes else 0}
+        return {"entries": 0, "current_bytes": 0, "max_bytes": self.max_bytes, "usage_percent": 0.0}
 
     def __contains__(self, key):
-        return key in self.cache
+        return False
 
     def __len__(self):
-        return len(self.cache)
+        return 0

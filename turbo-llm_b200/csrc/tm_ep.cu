@@ -37,7 +37,12 @@
 //
 // Every wait is bounded in wall time (default 2 s); on expiry the kernel sets
 // TM_STATUS_TIMEOUT in the context's status word and returns, so a missing
-// peer costs an error, never a hung GPU.  No TMA, no multicast: peer memory
+// peer costs an error, never a hung GPU.  An owner that gave up waiting for a
+// source processes nothing and tags its return flags (kEpFailTag); every
+// source that sees the tag sets TM_STATUS_PEER_FAILED, so no rank takes the
+// stale rows of an earlier call for this call's outputs with a clean status.
+// After either bit the context's regions may still receive late rows of the
+// failed call: close and recreate the context before its next call.  No TMA, no multicast: peer memory
 // is read and written with plain loads and stores only.
 #include <new>
 
@@ -51,6 +56,7 @@ constexpr int kEpWarps = kEpThreads / 32;
 constexpr int kEpCopyCTAs = 296;      // row copies: two CTAs per SM, one warp per row
 constexpr int kEpRowVecs = 8;         // 16-byte vectors a lane keeps in flight per row (H <= 2048 bf16: all)
 constexpr uint64_t kEpDefaultTimeoutNs = 2000000000ull;
+constexpr uint64_t kEpFailTag = 1ull << 63;   // in a return flag: the owner gave up on this call
 
 struct EpLayout {
   int64_t flags;   // uint64 [2][kEpMaxRanks]: [0][src] rows of src arrived, [1][owner] outputs of owner returned
@@ -60,6 +66,7 @@ struct EpLayout {
   int64_t ret;     // act [pmax][H]: outputs for this rank's slots, written by the owners
   int64_t epoch;   // uint64, local: calls completed
   int64_t status;  // uint32, local: TM_STATUS_* bits
+  int64_t owner_fail;  // uint32, local: 1 when this call's owner plan gave up waiting for a source
   int64_t done;    // int32 [kEpMaxRanks + 1], local: CTA completion counters
   int64_t total;
 };
@@ -79,6 +86,7 @@ static EpLayout ep_layout(int G, int64_t cap, int64_t pmax, int H, int act_bytes
   L.ret = take(pmax * H * act_bytes);
   L.epoch = take(8);
   L.status = take(4);
+  L.owner_fail = take(4);
   L.done = take((kEpMaxRanks + 1) * 4);
   L.total = off;
   return L;
@@ -110,15 +118,23 @@ __device__ __forceinline__ uint64_t ep_now_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Wait until *flag == want for at most timeout_ns of wall time.
-__device__ bool ep_wait_flag(const uint64_t *flag, uint64_t want, uint64_t timeout_ns) {
-  if (ld_acquire_sys(flag) == want) return true;
-  const uint64_t t0 = ep_now_ns();
-  while (true) {
-    if (ld_acquire_sys(flag) == want) return true;
-    if (ep_now_ns() - t0 > timeout_ns) return false;
-    __nanosleep(100);
+// Wait until (*flag & mask) == want for at most timeout_ns of wall time; the
+// value seen last goes to *seen.
+__device__ bool ep_wait_flag(const uint64_t *flag, uint64_t want, uint64_t timeout_ns, uint64_t mask = ~0ull,
+                             uint64_t *seen = nullptr) {
+  uint64_t v = ld_acquire_sys(flag);
+  bool ok = (v & mask) == want;
+  if (!ok) {
+    const uint64_t t0 = ep_now_ns();
+    while (true) {
+      v = ld_acquire_sys(flag);
+      if ((v & mask) == want) { ok = true; break; }
+      if (ep_now_ns() - t0 > timeout_ns) break;
+      __nanosleep(100);
+    }
   }
+  if (seen) *seen = v;
+  return ok;
 }
 __device__ __forceinline__ uint64_t ep_next(const EpDev &d) {
   return *reinterpret_cast<volatile uint64_t *>(d.local + d.L.epoch) + 1;
@@ -238,6 +254,7 @@ __global__ void __launch_bounds__(1024) ep_owner_plan(EpDev d, OwnerPlan pp) {
   const int64_t rows = (int64_t)G * d.cap;
   for (int64_t r = tid; r < rows; r += blockDim.x) pp.pair_slot[r] = -1;
   __syncthreads();
+  if (tid == 0) *reinterpret_cast<volatile uint32_t *>(d.local + d.L.owner_fail) = s_fail ? 1u : 0u;
   if (s_fail) {
     if (tid == 0) atomicOr(status, TM_STATUS_TIMEOUT);
     if (tid < G + 1) s_pre[tid] = 0;  // process nothing
@@ -345,7 +362,8 @@ __global__ void __launch_bounds__(1024) ep_owner_plan(EpDev d, OwnerPlan pp) {
   }
 }
 
-// Owner: every output row to its source's return region, then the flags.
+// Owner: every output row to its source's return region, then the flags
+// (tagged with kEpFailTag when this call's owner plan gave up).
 template <typename TA>
 __global__ void __launch_bounds__(kEpThreads) ep_return(EpDev d, const TA *y, const int *slot_token,
                                                         const int *plan_meta) {
@@ -369,22 +387,30 @@ __global__ void __launch_bounds__(kEpThreads) ep_return(EpDev d, const TA *y, co
     if (atomicAdd(done, 1) == (int)gridDim.x - 1) {
       atomicExch(done, 0);
       __threadfence_system();
+      const bool failed = *reinterpret_cast<volatile uint32_t *>(d.local + d.L.owner_fail) != 0u;
+      const uint64_t v = failed ? (ep | kEpFailTag) : ep;
       for (int g = 0; g < d.G; ++g)
-        st_release_sys(reinterpret_cast<uint64_t *>(d.peer[g] + d.L.flags) + kEpMaxRanks + d.rank, ep);
+        st_release_sys(reinterpret_cast<uint64_t *>(d.peer[g] + d.L.flags) + kEpMaxRanks + d.rank, v);
     }
   }
 }
 
-// Source: wait for every owner's outputs, then count the call as done.
+// Source: wait for every owner's outputs, then count the call as done.  A
+// return flag tagged kEpFailTag (the owner gave up on this call) sets
+// TM_STATUS_PEER_FAILED: the rows that owner should have returned are stale.
 __global__ void ep_wait_returns(EpDev d) {
   const int lane = threadIdx.x & 31;
   const uint64_t ep = ep_next(d);
-  bool ok = true;
-  if (lane < d.G)
+  bool ok = true, peer_failed = false;
+  if (lane < d.G) {
+    uint64_t seen = 0;
     ok = ep_wait_flag(reinterpret_cast<const uint64_t *>(d.local + d.L.flags) + kEpMaxRanks + lane, ep,
-                      d.timeout_ns);
-  if (!__all_sync(0xffffffffu, ok) && lane == 0)
-    atomicOr(reinterpret_cast<uint32_t *>(d.local + d.L.status), TM_STATUS_TIMEOUT);
+                      d.timeout_ns, ~kEpFailTag, &seen);
+    peer_failed = ok && (seen & kEpFailTag) != 0;
+  }
+  uint32_t *status = reinterpret_cast<uint32_t *>(d.local + d.L.status);
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) atomicOr(status, TM_STATUS_TIMEOUT);
+  if (__any_sync(0xffffffffu, peer_failed) && lane == 0) atomicOr(status, TM_STATUS_PEER_FAILED);
   __syncwarp();
   if (lane == 0) *reinterpret_cast<volatile uint64_t *>(d.local + d.L.epoch) = ep;
 }

@@ -10,13 +10,18 @@
 //
 // The scratch is `tm_noalloc_scratch`, kNoAllocScratchBytes (8 MiB) per GPU,
 // held by every GPU that loads the library until the process exits.  The
-// kernels get its device address from cudaGetSymbolAddress, taken once per
-// device on the first call made with that device current.  Every call shares
+// kernels get its device address from cudaGetSymbolAddress, taken on the first
+// call made with a device current and cached together with that device's
+// current CUDA context: a call under another context (after cudaDeviceReset,
+// or from a context the caller created itself) looks the address up again
+// instead of reusing a stale one.  Every call shares
 // the one array, which keeps the last call's contents: each call clears the
 // header (status word and counters) before its kernels run.  Two calls that
 // overlap on the GPU (different streams, or different host threads, on the
 // same device) race on the array and give wrong results; order them on one
 // stream.
+#include <cuda.h>   // CUcontext (type only; cuCtxGetCurrent is reached through cudart)
+
 #include <mutex>
 
 #include "tm_common.cuh"
@@ -32,8 +37,34 @@ static __device__ __align__(256) unsigned char tm_noalloc_scratch[kNoAllocScratc
 
 std::mutex g_setup_mu;
 void *g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of the scratch on the current device (set-up on first use).
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links
+// only the static CUDA runtime).  A thread on which no runtime call has yet
+// made the device's context current reads NULL here; the caller then looks the
+// address up again, and cudaGetSymbolAddress makes the context current.
+int current_context(CUcontext *ctx) {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    int rc = tmoe::cuda_check(cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q),
+                              "cudaGetDriverEntryPoint(cuCtxGetCurrent)");
+    if (rc) return rc;
+    if (!p || q != cudaDriverEntryPointSuccess)
+      return tmoe::fail(TM_ERR_CUDA, "cuCtxGetCurrent is not available from the driver");
+    fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  CUcontext c = nullptr;
+  if (fn(&c) != CUDA_SUCCESS) return tmoe::fail(TM_ERR_CUDA, "cuCtxGetCurrent failed");
+  *ctx = c;
+  return TM_OK;
+}
+
+// Device address of the scratch on the current device (set-up on first use,
+// and again whenever the device's current context has changed).
 int scratch_on_current_device(void **out) {
   int dev = -1;
   int rc = tmoe::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
@@ -41,16 +72,25 @@ int scratch_on_current_device(void **out) {
   if (dev < 0 || dev >= kMaxDevices)
     return tmoe::fail(TM_ERR_UNSUPPORTED, "device ordinal %d outside [0, %d)", dev, kMaxDevices);
   std::lock_guard<std::mutex> g(g_setup_mu);
-  if (!g_scratch_addr[dev]) {
-    void *p = nullptr;
-    rc = tmoe::cuda_check(cudaGetSymbolAddress(&p, tm_noalloc_scratch),
-                          "cudaGetSymbolAddress(tm_noalloc_scratch)");
+  CUcontext ctx = nullptr;
+  if (g_scratch_addr[dev]) {
+    rc = current_context(&ctx);
     if (rc) return rc;
-    if (!p || !tmoe::aligned(p, 256))
-      return tmoe::fail(TM_ERR_CUDA, "static scratch address %p is not 256-byte aligned", p);
-    g_scratch_addr[dev] = p;
+    if (ctx == g_scratch_ctx[dev]) {
+      *out = g_scratch_addr[dev];
+      return TM_OK;
+    }
   }
-  *out = g_scratch_addr[dev];
+  void *p = nullptr;
+  rc = tmoe::cuda_check(cudaGetSymbolAddress(&p, tm_noalloc_scratch), "cudaGetSymbolAddress(tm_noalloc_scratch)");
+  if (rc) return rc;
+  if (!p || !tmoe::aligned(p, 256))
+    return tmoe::fail(TM_ERR_CUDA, "static scratch address %p is not 256-byte aligned", p);
+  rc = current_context(&ctx);   // the runtime has made the device's context current by now
+  if (rc) return rc;
+  g_scratch_addr[dev] = p;
+  g_scratch_ctx[dev] = ctx;
+  *out = p;
   return TM_OK;
 }
 
@@ -85,8 +125,11 @@ extern "C" int tm_moe_decode_layer_noalloc(
   rc = tm_router_topk(x, tokens, hidden, act_dtype, router_w, n_experts, top_k, topk_idx, topk_w, nullptr, ws,
                       kNoAllocScratchBytes, stream);
   if (rc) return rc;
-  rc = tm_moe_decode_gateup(x, tokens, hidden, inter, n_experts, top_k, act_dtype, w13, s13, sh_w13, sh_s13, is,
-                            sh_gate_w, ws, kNoAllocScratchBytes, stream);
+  // K2 with the down projections pulled into L2 for K3 (the variant the
+  // workspace path uses; its results are identical to tm_moe_decode_gateup's)
+  rc = tm_moe_decode_gateup_prefetch(x, tokens, hidden, inter, n_experts, top_k, act_dtype, w13, s13, sh_w13,
+                                     sh_s13, is, sh_gate_w, w2, sh_w13 ? sh_w2 : nullptr, ws, kNoAllocScratchBytes,
+                                     stream);
   if (rc) return rc;
   rc = tm_moe_decode_down_combine(tokens, hidden, inter, n_experts, top_k, act_dtype, topk_w, w2, s2, sh_w2,
                                   sh_s2, is, residual, out, ws, kNoAllocScratchBytes, stream);

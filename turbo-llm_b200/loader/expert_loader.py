@@ -334,7 +334,13 @@ class ExpertLoader:
         return ops.unpack_expert(pl.experts, expert_id, self.dtype)
 
     def load_expert_dynamic(self, layer_id, expert_id):
+        """Prefill-time expert fetch (loader/expert_loader.py:269-360): fresh
+        dense dequantised (gate [I,H], up [I,H], down [H,I]) in ``dtype``,
+        outside any slot.  The reference counts a RAM or SSD hit; here every
+        expert is resident, so the lookup counts as a GPU hit."""
         pl = self.packed_layer(layer_id)
+        with self.lock:
+            self.gpu_hits += 1
         return ops.unpack_expert(pl.experts, expert_id, self.dtype)
 
     def load_expert_raw(self, layer_id, expert_id, is_decode=True):

@@ -71,6 +71,7 @@ TM_NOALLOC_SCRATCH_BYTES = 8 << 20
 TM_EP_MAX_RANKS = 8
 TM_EP_HANDLE_BYTES = 64
 TM_STATUS_TIMEOUT = 2
+TM_STATUS_PEER_FAILED = 4
 
 _lock = threading.Lock()
 _lib = None

@@ -6,10 +6,11 @@
 Each ``csrc/*.cu`` is compiled to an object under ``_build/`` (skipped when the
 object is newer than the source and every header), then linked into
 ``turbomoe/libturbomoe.so`` next to this file.  ``trace=True`` (``--trace``)
-builds the timeline variant instead: every source compiled with -DTM_TRACE
-into ``_build/trace/`` and linked as ``turbomoe/libturbomoe_trace.so`` (kernels
-record per-CTA (event, globaltimer, clock64) marks into the workspace; read
-them with ``python -m turbomoe.timeline``).  The product never loads it.
+builds a debugging variant instead: every source compiled with -DTM_TRACE into
+``_build/trace/`` and linked as ``turbomoe/libturbomoe_trace.so``; its kernels
+record per-CTA (kernel, event, globaltimer, clock64) marks into a region of
+the workspace whose layout ``tm_common.cuh`` documents (TM_TRACE).  The
+product never loads it and ships no reader for the marks.
 """
 from __future__ import annotations
 
