@@ -468,12 +468,285 @@ def run_ours(args, rank, world, local):
         "clocks": clk.summary(),
         "upload_s": round(upload_s, 1),
     }
+    if args.ep_tokens > 0:
+        res["ep"] = ep_measure(args, rank, world, local, loader, router)
+    if args.model_tokens > 0 and world == 1:
+        res["full_model"] = model_measure(args, local)
     if prefill is not None:
         res["prefill"] = prefill
     if c3 is not None:
         res["qwen35_layer"] = c3
     if attn is not None:
         res["attention_linears"] = attn
+    return res
+
+
+# ------------------------------------------ full-model greedy decode ----
+def model_measure(args, local):
+    """Batch-1 greedy decode of the whole random-init Qwen3-30B-A3B-FP8 model
+    (48 layers with attention, LM head and argmax; turbomoe.decoder, one CUDA
+    graph per step): the prompt of ``args.model_prompt`` tokens enters one
+    position per step, then ``args.model_tokens`` tokens are generated.
+    ``tokens_per_s`` = generated tokens / device time of their steps (CUDA
+    events); ``e2e`` = the public ``generate`` call with the prompt ids from
+    host memory and the generated ids read back, prefill included."""
+    from loader.expert_loader import ExpertLoader
+    from turbomoe import synth_model as S
+    from turbomoe.decoder import Qwen3MoeDecoder
+    dev = torch.device("cuda", local)
+    cfg = S.config()
+    P, N = args.model_prompt, args.model_tokens
+    t0 = time.time()
+    L = ExpertLoader(None, config={"execution": {"dtype": "bf16"}}, source=S.ModelSource(cfg, SEED, dev))
+    dec = Qwen3MoeDecoder(L, cfg, max_len=P + N + 8, device=dev)
+    dec.capture()
+    build_s = time.time() - t0
+    g = torch.Generator().manual_seed(SEED + 5)
+    prompt = torch.randint(0, cfg["vocab_size"], (P,), generator=g).tolist()
+    dec.teacher_forced(prompt)             # fills the cache of the prompt positions
+    for _ in range(3):                      # warm-up steps beyond the prompt (replaced below)
+        dec.step()
+    dec.pos.fill_(P)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(N):
+        dec.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    st = int(dec.status.item())
+    t = time.perf_counter()
+    toks = dec.generate(prompt, N)
+    e2e_s = time.perf_counter() - t
+    # per generated token: 8 experts, the router, the q/k/v/o weights and the
+    # KV rows of every layer (mean context P + N/2), plus the LM head
+    layer_bytes = (8 * 3 * 768 * 2048 + 128 * 2048 * 2 + 5120 * 2048 + 2048 * 4096
+                   + 2 * 4 * (P + N // 2) * 128 * 2)
+    step_bytes = 48 * layer_bytes + 151936 * 2048 * 2
+    hbm, _src = _peaks()
+    out = {"workload": f"Qwen3-30B-A3B-FP8 random-init, batch-1 greedy decode of {N} tokens after a {P}-token "
+                       "prompt (48 layers: FP8 q/k/v/o, GQA attention over the bf16 KV cache, MoE, bf16 LM head, "
+                       "device argmax); one CUDA graph per step",
+           "tokens_per_s": round(N / (ms / 1000.0), 1), "ms_per_token": round(ms / N, 4),
+           "algorithmic_bytes_per_token": step_bytes,
+           "hbm_gbs": round(step_bytes / (ms / N / 1000.0) / 1e9, 1),
+           "frac": round(step_bytes / (ms / N / 1000.0) / 1e9 / hbm, 4),
+           "e2e": {"tokens_per_s_incl_prefill": round(N / e2e_s, 1), "seconds": round(e2e_s, 3),
+                   "path": "Qwen3MoeDecoder.generate (prompt ids from host, one position per step, ids read back)"},
+           "kernel_launches_per_token": 2 + 48 * 9 + 1,
+           "build_s": round(build_s, 1), "status": st, "distinct_generated": len(set(toks))}
+    del dec, L
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------- expert parallelism on every line ----
+def _fp32_layer(x, idx, w, packed, tokens):
+    """fp32 evaluation of the routed experts for the first ``tokens`` tokens:
+    weights dequantised exactly (K0 in fp32, bit-exact to the reference's
+    dequantisation), then plain PyTorch fp32 matmuls in the order of
+    MoEExecutor.execute_layer (execution/moe.py:164-176).  A numerics
+    reference of the same op, used to check the expert-parallel output."""
+    from turbomoe import ops
+    xs = x[:tokens].float()
+    y = torch.zeros_like(xs)
+    cache = {}
+    for t in range(tokens):
+        for r in range(idx.shape[1]):
+            e = int(idx[t, r])
+            if e not in cache:
+                cache[e] = ops.unpack_expert(packed, e, torch.float32)
+            g, u, d = cache[e]
+            h = torch.nn.functional.silu(xs[t] @ g.T) * (xs[t] @ u.T)
+            y[t] += float(w[t, r]) * (h @ d.T)
+    return y
+
+
+def _cmp(a, b):
+    a, b = a.float(), b.float()
+    cos = torch.nn.functional.cosine_similarity(a.reshape(1, -1), b.reshape(1, -1)).item()
+    return float((a - b).abs().max()), cos
+
+
+def ep_measure(args, rank, world, local, loader, router):
+    """Expert-parallel batched decode of the Qwen3-30B-A3B MoE layers: the
+    ``args.ep_tokens`` sequences (one token each) split over the ranks, the
+    128 experts of every layer sharded E/N per GPU (views into the packed
+    layers the loader already holds), dispatch / experts / return over NVLink
+    peer memory (tm_ep_*), the whole step of ``args.layers`` layers in one CUDA
+    graph.  Uniform routing and, with ``args.ep_zipf`` > 0, Zipf-skewed routing.
+    Reports tokens/s (CUDA events, max over ranks), a per-phase split of an
+    eager pass, the single-GPU number of the same workload (rank 0 alone) for
+    the strong-scaling efficiency, and a parity block per rank."""
+    from turbomoe import ops, synth
+    from turbomoe._lib import lib
+    from turbomoe.ep import PeerExpertParallelMoE
+    shape = synth.QWEN3_30B_A3B
+    E, k, H, I = shape.experts, shape.top_k, shape.hidden, shape.inter
+    Lr = args.layers
+    E_loc = E // world
+    T = args.ep_tokens // world
+    dev = torch.device("cuda", local)
+    Lb = lib()
+    n13, ns13 = Lb.tm_packed_w13_bytes(H, I), Lb.tm_packed_s13_floats(H, I)
+    n2, ns2 = Lb.tm_packed_w2_bytes(H, I), Lb.tm_packed_s2_floats(H, I)
+
+    def shard(pe, a, b):
+        return ops.PackedExperts(pe.w13[a * n13:b * n13], pe.s13[a * ns13:b * ns13], pe.w2[a * n2:b * n2],
+                                 pe.s2[a * ns2:b * ns2], b - a, H, I)
+
+    full = [loader.packed_layer(l).experts for l in range(Lr)]
+    mine = [shard(pe, rank * E_loc, (rank + 1) * E_loc) for pe in full]
+    routers = {"uniform": [router.routers[l] for l in range(Lr)]}
+    if args.ep_zipf > 0:
+        routers["zipf"] = [synth.router_with_bias(router.routers[l], synth.zipf_expert_bias(E, SEED + l, args.ep_zipf))
+                           .contiguous() for l in range(Lr)]
+    x_u = synth.make_hidden(T, H, SEED + 100 + rank, rms_normalise=True, device=dev)
+    inputs = {"uniform": x_u, "zipf": synth.tokens_for_bias(x_u)}
+    bufs = [torch.empty_like(x_u) for _ in range(2)]
+
+    def build(shards, single=False, tokens=T):
+        chan = PeerExpertParallelMoE(routers["uniform"][0], shards[0], k, max_tokens=tokens, single=single)
+        out = {}
+        for name, rw in routers.items():
+            out[name] = [chan if (name == "uniform" and l == 0) else
+                         PeerExpertParallelMoE(rw[l], shards[l], k, tokens, channel=chan) for l in range(Lr)]
+        return chan, out
+
+    def step(eps, x, bb, marks=None):
+        for i, ep in enumerate(eps):
+            x = ep.forward(x, residual=x, out=bb[i % 2], marks=None if marks is None else marks[i])
+        return x
+
+    def capture(eps, x, bb):
+        for _ in range(args.warmup):
+            step(eps, x, bb)
+        torch.cuda.synchronize()
+        s_ = torch.cuda.Stream(device=dev)
+        s_.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_):
+            step(eps, x, bb)
+        torch.cuda.current_stream().wait_stream(s_)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(eps, x, bb)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        return g
+
+    def timed(g, n_steps, group_world):
+        barrier(group_world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n_steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(group_world)
+        return max_over_ranks(e0.elapsed_time(e1), group_world)
+
+    chan, layers = build(mine)
+    res = {"workload": f"{args.ep_tokens} sequences x 1 token through {Lr} Qwen3-30B-A3B MoE layers, experts "
+                       f"sharded {E_loc} per GPU over {world} GPU(s); dispatch / owner grouped GEMMs / return "
+                       "by NVLink peer stores (tm_ep_*), step in one CUDA graph",
+           "tokens_per_rank": T, "experts_per_rank": E_loc, "parallelism": f"ep{world}", "scaling": "strong",
+           "timing": "CUDA events around graph replays, max over ranks"}
+    with ClockSampler(local) as clk:
+        for name in routers:
+            g = capture(layers[name], inputs[name], bufs)
+            ms = timed(g, args.steps, world)
+            del g
+            res[name] = {"tokens_per_s": round(T * world * args.steps / (ms / 1000.0), 1),
+                         "us_per_layer": round(ms / args.steps / Lr * 1000, 1)}
+    res["clocks"] = clk.summary()
+    # per-phase split (eager pass; the experts phase includes the wait for the
+    # sources' rows, the combine phase the wait for the owners' outputs)
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(Lr)]
+    for name in routers:
+        torch.cuda.synchronize()
+        barrier(world)
+        step(layers[name], inputs[name], bufs, marks)
+        torch.cuda.synchronize()
+        ph = [sum(m[i].elapsed_time(m[i + 1]) for m in marks) / Lr * 1000 for i in range(4)]
+        ph = [max_over_ranks(v, world) for v in ph]
+        res[name]["phase_us_per_layer"] = {"router": round(ph[0], 1), "dispatch": round(ph[1], 1),
+                                           "experts_incl_wait": round(ph[2], 1),
+                                           "combine_incl_wait": round(ph[3], 1)}
+        lim = max(range(4), key=lambda i: ph[i])
+        res[name]["limiting_phase"] = ["router", "dispatch", "experts_incl_wait", "combine_incl_wait"][lim]
+    # load balance of the first layer: routed pairs per owner rank, all ranks' tokens
+    ws0 = ops.Workspace(dev, E, k, H, I)
+    for name in routers:
+        idx0, _ = ops.router_topk(inputs[name], routers[name][0], k, ws0)
+        pairs = torch.bincount(idx0.reshape(-1) // E_loc, minlength=world).to(torch.float64)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(pairs)
+        res[name]["owner_load_max_over_mean"] = round(float(pairs.max() / pairs.mean()), 3)
+        res[name]["distinct_experts_layer0_rank"] = int(torch.unique(idx0).numel())
+    # parity: layer 0 on this rank's tokens, EP vs the whole layer on this GPU
+    # (all 128 experts, same kernels: bit-exact expected) and vs fp32
+    par = {}
+    for name in routers:
+        xin = inputs[name]
+        y_ep = layers[name][0].forward(xin).clone()
+        idx, w = ops.router_topk(xin, routers[name][0], k, ws0)
+        y_1 = ops.moe_experts(xin, idx, w, full[0], ws0)
+        ns = min(T, 8)
+        y32 = _fp32_layer(xin, idx, w, full[0], ns)
+        torch.cuda.synchronize()
+        m1, c1 = _cmp(y_ep, y_1)
+        m32, c32 = _cmp(y_ep[:ns], y32)
+        ok = float(m32 <= 2e-2 and c32 >= 0.9995)
+        stats = torch.tensor([m1, -c1, m32, -c32, float(torch.equal(y_ep, y_1)), ok], dtype=torch.float64,
+                             device=dev)
+        if world > 1:
+            import torch.distributed as dist
+            lo = stats.clone()
+            lo[4:] *= -1
+            dist.all_reduce(lo, op=dist.ReduceOp.MAX)   # worst over ranks (min of the flags)
+            lo[4:] *= -1
+            stats = lo
+        st = stats.tolist()
+        par[name] = {"vs_single_gpu_layer": {"max_abs": st[0], "cos": -st[1], "bit_exact_all_ranks": bool(st[4])},
+                     "vs_fp32": {"max_abs": st[2], "cos": -st[3], "tokens_per_rank": ns,
+                                 "within_2e-2_0.9995_all_ranks": bool(st[5])}}
+    res["parity_layer0"] = par
+    status = max_over_ranks(float(layers["uniform"][0].status()), world)
+    res["status"] = int(status)
+    for name in routers:
+        for ep in layers[name]:
+            if ep is not chan:
+                ep.close()
+    chan.close()
+    # the same workload on one GPU (rank 0 alone, all experts local): the
+    # denominator of the strong-scaling efficiency
+    if world > 1:
+        if rank == 0:
+            chan1, layers1 = build(full, single=True, tokens=args.ep_tokens)
+            x1 = synth.make_hidden(args.ep_tokens, H, SEED + 100, rms_normalise=True, device=dev)
+            b1 = [torch.empty_like(x1) for _ in range(2)]
+            g = capture(layers1["uniform"], x1, b1)
+            ms1 = timed(g, args.steps, 1)
+            del g
+            for ep in layers1["uniform"] + layers1.get("zipf", []):
+                if ep is not chan1:
+                    ep.close()
+            chan1.close()
+            one = args.ep_tokens * args.steps / (ms1 / 1000.0)
+            res["single_gpu_tokens_per_s"] = round(one, 1)
+            res["strong_scaling_efficiency"] = round(res["uniform"]["tokens_per_s"] / (world * one), 3)
+        barrier(world)
+    else:
+        res["single_gpu_tokens_per_s"] = res["uniform"]["tokens_per_s"]
+        res["strong_scaling_efficiency"] = 1.0
+    if "zipf" in routers:
+        res["zipf"]["routing"] = (f"Zipf s={args.ep_zipf}: router column {H - 1} replaced by log p_e (p_e ~ rank^-s "
+                                  f"over a seeded expert permutation) and token coordinate {H - 1} set to 1, so the "
+                                  "experts also see that modified coordinate")
     return res
 
 
@@ -675,11 +948,15 @@ def main():
                     help="also time the FP8 q/k/v/o projections of this many layers, one token (0 = skip)")
     ap.add_argument("--c3-tokens", type=int, default=64,
                     help="also time one Qwen3.5-shaped layer call (shared expert) of this many tokens (0 = skip)")
+    ap.add_argument("--model-tokens", type=int, default=256,
+                    help="also time greedy decode of the whole model: tokens generated (0 = skip; 1 GPU only)")
+    ap.add_argument("--model-prompt", type=int, default=2048, help="prompt length of the whole-model decode")
     ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
                     help="decode: batch-1 decode (replicas for N>1); ep: expert-parallel batched decode")
-    ap.add_argument("--ep-tokens", type=int, default=256, help="ep workload: sequences over all ranks")
-    ap.add_argument("--ep-zipf", type=float, default=0.0,
-                    help="ep workload: Zipf exponent of the expert popularity (0: uniform routing)")
+    ap.add_argument("--ep-tokens", type=int, default=256,
+                    help="expert-parallel batched decode: sequences over all ranks (0 = skip the ep object)")
+    ap.add_argument("--ep-zipf", type=float, default=1.2,
+                    help="expert-parallel decode: also time Zipf-skewed routing with this exponent (0 = skip)")
     ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",
                     help="ep workload: NVLink peer-memory kernels (tm_ep_*) or NCCL all-to-all")
     args = ap.parse_args()

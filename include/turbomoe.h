@@ -45,6 +45,7 @@ typedef enum { TM_DTYPE_F32 = 0, TM_DTYPE_F16 = 1, TM_DTYPE_BF16 = 2 } tm_dtype;
 /* Device-side status bits written into the workspace (tm_workspace_status). */
 #define TM_STATUS_BAD_EXPERT_ID 1u  /* a top-k index was outside [0, n_experts) */
 #define TM_STATUS_TIMEOUT 2u        /* a bounded device-side wait gave up; outputs are invalid */
+#define TM_STATUS_BAD_TOKEN_ID 8u   /* a token id outside [0, vocab) or a position outside the KV cache */
 #define TM_STATUS_PEER_FAILED 4u    /* expert parallelism: an owner rank gave up on this call (it timed
                                        out waiting for a source); this rank's outputs are invalid */
 
@@ -270,13 +271,61 @@ int tm_moe_decode_layer_noalloc(const void *x, int64_t tokens, int hidden, int i
  * (tm_packed_w2_bytes(out_features, in_features) bytes, the layout of one
  * expert's down projection); scale_inv is the checkpoint's fp32
  * [out_features/128, in_features/128] as is.  x [tokens, in_features] and out
- * [tokens, out_features] act (bf16 or fp16); in_features % 512 == 0 (at most
+ * [tokens, out_features] act (bf16 or fp16 on the tensor-core kernel; fp32 on a
+ * CUDA-core kernel that dequantises each weight as the reference's fp32
+ * load_weight does); in_features % 512 == 0 (at most
  * 6144), out_features % 128 == 0.  One pass over W per call (decode-sized
  * calls are HBM-bound).  status: optional device uint32 for TM_STATUS_*. */
 int tm_pack_linear(const uint8_t *w, int out_features, int in_features, uint8_t *w_packed, void *stream);
 int tm_fp8_linear(const void *x, int64_t tokens, int in_features, int out_features, int act_dtype,
                   const uint8_t *w_packed, const float *scale_inv, const void *residual, void *out,
                   uint32_t *status, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* The rest of a Qwen3-MoE decode step (the full-model loop around the MoE
+ * path: runtime/engine.py:98-162, execution/layer_executor.py:137-170, over
+ * the Hugging Face Qwen3-MoE modules).  Every call reads its inputs from
+ * device memory (token ids and positions included), so a whole decode step
+ * can be captured in one CUDA graph and replayed with no host round trip.
+ * head_dim is 128.  Workspaces are caller-owned, zeroed once (their
+ * counters reset themselves) and must not be shared by overlapping calls. */
+
+/* out[t] = embed_tokens[ids[t]] (bf16 table [vocab][hidden] -> act).  An id
+ * outside [0, vocab) writes zeros and sets TM_STATUS_BAD_TOKEN_ID in *status
+ * (optional). */
+int tm_embed(const int64_t *ids, int64_t tokens, const void *table_bf16, int hidden, int64_t vocab,
+             int act_dtype, void *out, uint32_t *status, void *stream);
+/* RMSNorm of each token row (Qwen3MoeRMSNorm): fp32 mean of squares,
+ * round(x * rsqrt(mean + eps)) to act, times weight (act), rounded. */
+int tm_rmsnorm(const void *x, int64_t tokens, int hidden, int act_dtype, const void *weight, float eps,
+               void *out, void *stream);
+/* qkv [tokens][(n_heads + 2 n_kv_heads) * 128] (fused q/k/v projection output):
+ * q heads get RMSNorm (q_norm_w) and the rotary embedding at positions[t] ->
+ * q_out [tokens][n_heads][128]; k heads RMSNorm (k_norm_w) + rotary ->
+ * k_cache[kv][positions[t]]; v heads -> v_cache[kv][positions[t]].  Caches of
+ * one layer are [n_kv_heads][max_len][128] act; rope_table [max_len][2][128]
+ * act holds cos then sin per position (Qwen3MoeRotaryEmbedding's values).
+ * A position outside [0, max_len) skips the token and sets
+ * TM_STATUS_BAD_TOKEN_ID. */
+int tm_qk_rope_kv(const void *qkv, int64_t tokens, int n_heads, int n_kv_heads, int head_dim, int act_dtype,
+                  const void *q_norm_w, const void *k_norm_w, float eps, const void *rope_table,
+                  const int64_t *positions, int64_t max_len, void *q_out, void *k_cache, void *v_cache,
+                  uint32_t *status, void *stream);
+/* One query token's attention over cache positions [0, *position] (GQA, query
+ * head h reads KV head h / (n_heads / n_kv_heads)): softmax(scale q.k) v in
+ * fp32, out [n_heads * 128] act.  The positions are split over `splits` CTAs
+ * per KV head and merged by the last one. */
+int64_t tm_attn_decode_workspace_bytes(int n_heads, int n_kv_heads, int splits);
+int tm_attn_decode(const void *q, const void *k_cache, const void *v_cache, const int64_t *position,
+                   int64_t max_len, int n_heads, int n_kv_heads, int head_dim, int act_dtype, float scale,
+                   int splits, void *out, void *ws, int64_t ws_bytes, void *stream);
+/* LM head and greedy choice: logits = x . W^T (W bf16 [vocab][hidden], fp32
+ * accumulation, rounded to act for 16-bit act), optional logits output (act
+ * [vocab], NULL to skip), *token = index of the largest logit (lowest index
+ * among equal maxima, as torch.argmax). */
+int64_t tm_lm_head_workspace_bytes(void);
+int tm_lm_head_argmax(const void *x, int hidden, int act_dtype, const void *w_bf16, int64_t vocab, void *logits,
+                      int64_t *token, void *ws, int64_t ws_bytes, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Expert parallelism over NVLink peer memory (no counterpart in the reference,

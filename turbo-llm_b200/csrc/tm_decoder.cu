@@ -1,0 +1,574 @@
+// The rest of a Qwen3-MoE decode step around the MoE hot path: token
+// embedding, RMSNorm, per-head q/k RMSNorm + rotary embedding + KV-cache
+// append, one-token attention over the KV cache, and the LM head with the
+// greedy argmax.  With tm_fp8_linear (q/k/v/o projections) and the MoE
+// kernels they make one decode step that never leaves the device: the next
+// token id is written to device memory and read by the next step's
+// embedding, so a whole step can be replayed from one CUDA graph.
+//
+// Reference (the Hugging Face Qwen3-MoE modules the reference engine drives,
+// runtime/engine.py:98-162, execution/layer_executor.py:137-170):
+//   embed_tokens; input_layernorm / post_attention_layernorm / q_norm /
+//   k_norm / norm (RMSNorm: fp32 variance, x * rsqrt(var + eps) rounded to the
+//   act dtype, times the weight, rounded); apply_rotary_pos_emb
+//   (q * cos + rotate_half(q) * sin, every product and the sum rounded to the
+//   act dtype); scaled-dot-product attention over the cache (GQA); lm_head;
+//   torch.argmax of the last position's logits (first index among equal
+//   maxima).
+//
+// Layouts: KV cache of one layer [n_kv][max_len][head_dim] (act dtype), so the
+// rows one KV head reads are contiguous; rotary table [max_len][2][head_dim]
+// (cos, then sin) in the act dtype, computed by the host exactly as the
+// reference does (inv_freq in fp32, position * inv_freq, cos/sin in fp32,
+// rounded to the act dtype).
+#include "tm_common.cuh"
+
+namespace tmoe {
+
+constexpr int kHeadDim = 128;
+constexpr int kAttnTile = 32;   // positions per shared-memory tile
+constexpr int kHeadMaxAttnWarps = 16;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Four consecutive act values <-> floats.
+template <typename TA> struct Vec4;
+template <> struct Vec4<float> {
+  static __device__ __forceinline__ void load(const float *p, float (&v)[4]) {
+    const float4 r = *reinterpret_cast<const float4 *>(p);
+    v[0] = r.x; v[1] = r.y; v[2] = r.z; v[3] = r.w;
+  }
+  static __device__ __forceinline__ void load_cg(const float *p, float (&v)[4]) {
+    const float4 r = __ldcg(reinterpret_cast<const float4 *>(p));
+    v[0] = r.x; v[1] = r.y; v[2] = r.z; v[3] = r.w;
+  }
+  static __device__ __forceinline__ void store(float *p, const float (&v)[4]) {
+    *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+};
+template <typename TA> struct Vec4Half {
+  static __device__ __forceinline__ void unpack(uint2 r, float (&v)[4]) {
+    const TA *h = reinterpret_cast<const TA *>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = Act<TA>::to_f(h[i]);
+  }
+  static __device__ __forceinline__ void load(const TA *p, float (&v)[4]) {
+    unpack(*reinterpret_cast<const uint2 *>(p), v);
+  }
+  static __device__ __forceinline__ void load_cg(const TA *p, float (&v)[4]) {
+    unpack(__ldcg(reinterpret_cast<const uint2 *>(p)), v);
+  }
+  static __device__ __forceinline__ void store(TA *p, const float (&v)[4]) {
+    uint2 r;
+    TA *h = reinterpret_cast<TA *>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = Act<TA>::from_f(v[i]);
+    *reinterpret_cast<uint2 *>(p) = r;
+  }
+};
+template <> struct Vec4<__half> : Vec4Half<__half> {};
+template <> struct Vec4<__nv_bfloat16> : Vec4Half<__nv_bfloat16> {};
+
+// 16-byte asynchronous global -> shared copy (L2 only; the cache rows were
+// written by an earlier kernel of the step).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ------------------------------------------------------------------ embed ----
+// out[t] = table[ids[t]] (bf16 table -> act dtype, exact).  ids are read
+// through L2: the previous step's argmax wrote them.
+template <typename TO>
+__global__ void __launch_bounds__(256) k8_embed(const int64_t *ids, const __nv_bfloat16 *table, int hidden,
+                                                int64_t vocab, TO *out, uint32_t *status) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int64_t id = (int64_t)__ldcg(reinterpret_cast<const long long *>(ids) + t);
+  TO *o = out + (int64_t)t * hidden;
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0 && status) atomicOr(status, TM_STATUS_BAD_TOKEN_ID);
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) o[i] = Act<TO>::from_f(0.f);
+    return;
+  }
+  const __nv_bfloat16 *row = table + id * hidden;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) o[i] = Act<TO>::from_f(__bfloat162float(row[i]));
+}
+
+// ---------------------------------------------------------------- RMSNorm ----
+// One CTA per token: out = round(round(x * rsqrt(mean(x^2) + eps)) * w).
+template <typename TA>
+__global__ void __launch_bounds__(256) k8_rmsnorm(const TA *x, const TA *w, int hidden, float eps, TA *out) {
+  __shared__ float red[8];
+  pdl_wait();
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const TA *xr = x + (int64_t)t * hidden;
+  float ss = 0.f;
+  for (int i = tid; i < hidden; i += 256) {
+    const float v = Act<TA>::to_f(Act<TA>::ld_cg(xr + i));
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float r = rsqrtf(tot / (float)hidden + eps);
+  TA *o = out + (int64_t)t * hidden;
+  for (int i = tid; i < hidden; i += 256) {
+    const float v = Act<TA>::to_f(Act<TA>::ld_cg(xr + i));
+    const float nrm = Act<TA>::round(v * r);
+    o[i] = Act<TA>::from_f(nrm * Act<TA>::to_f(w[i]));
+  }
+}
+
+// ------------------------------------------- q/k norm, RoPE, KV append ----
+// qkv [T][(nh + 2 nkv) * 128]: q heads, then k heads, then v heads (the output
+// of the fused q/k/v projection).  One warp per (token, head); lane j holds
+// elements 4j..4j+3.  q heads: RMSNorm (q_norm) + rotary -> q_out [T][nh][128];
+// k heads: RMSNorm (k_norm) + rotary -> k_cache[kvh][pos]; v heads -> v_cache.
+template <typename TA>
+__global__ void __launch_bounds__(256) k8_qk_rope_kv(const TA *qkv, const TA *qn_w, const TA *kn_w, float eps,
+                                                     const TA *rope, const int64_t *positions, int nh, int nkv,
+                                                     int64_t max_len, TA *q_out, TA *k_cache, TA *v_cache,
+                                                     uint32_t *status) {
+  pdl_wait();
+  const int t = blockIdx.x, lane = threadIdx.x & 31;
+  const int hh = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int nheads = nh + 2 * nkv;
+  if (hh >= nheads) return;
+  const int64_t pos = (int64_t)__ldcg(reinterpret_cast<const long long *>(positions) + t);
+  if (pos < 0 || pos >= max_len) {
+    if (lane == 0 && status) atomicOr(status, TM_STATUS_BAD_TOKEN_ID);
+    return;
+  }
+  const int e0 = 4 * lane;
+  float v[4];
+  Vec4<TA>::load_cg(qkv + ((int64_t)t * nheads + hh) * kHeadDim + e0, v);
+  if (hh >= nh + nkv) {  // v head: copy into the cache
+    Vec4<TA>::store(v_cache + ((int64_t)(hh - nh - nkv) * max_len + pos) * kHeadDim + e0, v);
+    return;
+  }
+  const bool is_q = hh < nh;
+  const TA *nw = is_q ? qn_w : kn_w;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)kHeadDim + eps);
+  float n[4], out[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = Act<TA>::round(Act<TA>::round(v[i] * r) * Act<TA>::to_f(nw[e0 + i]));
+  float cs[4], sn[4];
+  Vec4<TA>::load(rope + (pos * 2) * kHeadDim + e0, cs);
+  Vec4<TA>::load(rope + (pos * 2 + 1) * kHeadDim + e0, sn);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // rotate_half: element e pairs with e + 64 (lane j with lane j + 16)
+    const float partner = __shfl_xor_sync(0xffffffffu, n[i], 16);
+    const float rot = lane < 16 ? -partner : partner;
+    out[i] = Act<TA>::round(Act<TA>::round(n[i] * cs[i]) + Act<TA>::round(rot * sn[i]));
+  }
+  if (is_q)
+    Vec4<TA>::store(q_out + ((int64_t)t * nh + hh) * kHeadDim + e0, out);
+  else
+    Vec4<TA>::store(k_cache + ((int64_t)(hh - nh) * max_len + pos) * kHeadDim + e0, out);
+}
+
+// ----------------------------------------------------- decode attention ----
+// One query token, GQA: q head h reads KV head h / (nh / nkv).  Context =
+// positions [0, pos] (pos from device memory, so a captured step replays at
+// any position).  Grid (nkv, splits): CTA (g, s) takes the group's nh/nkv q
+// heads (one warp each) over positions [s * chunk, min(n, (s + 1) * chunk))
+// with chunk = ceil(n / splits) rounded up to 32.  K/V rows arrive 32 at a
+// time by cp.async into a double-buffered shared tile.  Per tile a warp forms
+// its 32 scores (lane j holds q[4j..4j+3]; the 32 partial dot products are
+// summed across lanes by a 31-shuffle transposed reduction that leaves
+// position i's score in lane i), then updates its running max, sum and
+// output (fp32).  Each CTA writes (m, l, o[128]) per head; the last CTA of a
+// KV head (counter in the workspace, reset by that CTA) merges the splits:
+// out = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M), rounded to act.
+template <typename TA>
+__global__ void __launch_bounds__(kHeadMaxAttnWarps * 32) k8_attn_decode(
+    const TA *q, const TA *k_cache, const TA *v_cache, const int64_t *position, int64_t max_len, int nh, int nkv,
+    float scale, TA *out, float *part, unsigned *counters) {
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  TA *ks = reinterpret_cast<TA *>(attn_smem);                 // [2][32][128]
+  TA *vs = ks + 2 * kAttnTile * kHeadDim;                     // [2][32][128]
+  __shared__ unsigned s_last;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int G = nh / nkv;
+  const int g = blockIdx.x, s = blockIdx.y, S = gridDim.y;
+  const int h = g * G + w;
+  pdl_wait();
+  const int64_t n = (int64_t)__ldcg(reinterpret_cast<const long long *>(position)) + 1;
+  const int64_t per = ((n + S - 1) / S + kAttnTile - 1) / kAttnTile * kAttnTile;
+  const int64_t p_begin = (int64_t)s * per;
+  const int64_t p_end = min(n, p_begin + per);
+  const TA *kbase = k_cache + (int64_t)g * max_len * kHeadDim;
+  const TA *vbase = v_cache + (int64_t)g * max_len * kHeadDim;
+  constexpr int kVecPerRow = kHeadDim * (int)sizeof(TA) / 16;
+
+  auto issue = [&](int64_t p0, int buf) {
+    const int rows = (int)min((int64_t)kAttnTile, p_end - p0);
+    const int nvec = rows * kVecPerRow;
+    for (int i = tid; i < nvec; i += blockDim.x) {
+      const int r = i / kVecPerRow, c = i % kVecPerRow;
+      const int64_t off = (p0 + r) * kHeadDim + c * (16 / (int)sizeof(TA));
+      const int soff = (buf * kAttnTile + r) * kHeadDim + c * (16 / (int)sizeof(TA));
+      cp_async16(ks + soff, kbase + off);
+      cp_async16(vs + soff, vbase + off);
+    }
+    cp_async_commit();
+  };
+
+  float qv[4], o[4] = {0.f, 0.f, 0.f, 0.f};
+  float m = -INFINITY, l = 0.f;
+  Vec4<TA>::load_cg(q + (int64_t)h * kHeadDim + 4 * lane, qv);
+  if (p_begin < p_end) issue(p_begin, 0);
+  int buf = 0;
+  for (int64_t p0 = p_begin; p0 < p_end; p0 += kAttnTile, buf ^= 1) {
+    if (p0 + kAttnTile < p_end) {
+      issue(p0 + kAttnTile, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int cnt = (int)min((int64_t)kAttnTile, p_end - p0);
+    const TA *kt = ks + buf * kAttnTile * kHeadDim + 4 * lane;
+    const TA *vt = vs + buf * kAttnTile * kHeadDim + 4 * lane;
+    float sc[kAttnTile];
+#pragma unroll
+    for (int i = 0; i < kAttnTile; ++i) {
+      float kk[4];
+      Vec4<TA>::load(kt + i * kHeadDim, kk);
+      sc[i] = qv[0] * kk[0];
+#pragma unroll
+      for (int e = 1; e < 4; ++e) sc[i] = fmaf(qv[e], kk[e], sc[i]);
+    }
+    // transposed reduction: afterwards sc[0] of lane i is position p0 + i's dot product
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < off; ++i) {
+        const float send = upper ? sc[i] : sc[i + off];
+        const float keep = upper ? sc[i + off] : sc[i];
+        sc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    const float my = lane < cnt ? sc[0] * scale : -INFINITY;
+    const float m_new = fmaxf(m, warp_max(my));
+    const float p = lane < cnt ? expf(my - m_new) : 0.f;
+    const float corr = expf(m - m_new);   // 0 on the first tile (m = -inf)
+    l = l * corr + warp_sum(p);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] *= corr;
+    for (int i = 0; i < cnt; ++i) {
+      const float pi = __shfl_sync(0xffffffffu, p, i);
+      float vv[4];
+      Vec4<TA>::load(vt + i * kHeadDim, vv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = fmaf(pi, vv[e], o[e]);
+    }
+    m = m_new;
+    __syncthreads();  // the next issue() overwrites this buffer
+  }
+  // partial of (head h, split s): m, l, o[128]
+  float *pp = part + ((int64_t)h * S + s) * (kHeadDim + 4);
+  if (lane == 0) {
+    pp[0] = m;
+    pp[1] = l;
+  }
+  *reinterpret_cast<float4 *>(pp + 4 + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(counters + g, 1u) == (unsigned)(S - 1);
+  __syncthreads();
+  if (!s_last) return;
+  if (tid == 0) counters[g] = 0u;  // self-resetting for the next call
+  __threadfence();
+  float M = -INFINITY;
+  for (int j = 0; j < S; ++j) {
+    const float *pj = part + ((int64_t)h * S + j) * (kHeadDim + 4);
+    if (__ldcg(pj + 1) > 0.f) M = fmaxf(M, __ldcg(pj));
+  }
+  float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < S; ++j) {
+    const float *pj = part + ((int64_t)h * S + j) * (kHeadDim + 4);
+    const float lj = __ldcg(pj + 1);
+    if (!(lj > 0.f)) continue;
+    const float f = expf(__ldcg(pj) - M);
+    L = fmaf(lj, f, L);
+    const float4 oj = __ldcg(reinterpret_cast<const float4 *>(pj + 4 + 4 * lane));
+    acc[0] = fmaf(oj.x, f, acc[0]);
+    acc[1] = fmaf(oj.y, f, acc[1]);
+    acc[2] = fmaf(oj.z, f, acc[2]);
+    acc[3] = fmaf(oj.w, f, acc[3]);
+  }
+  float res[4];
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) res[e] = acc[e] * inv;
+  Vec4<TA>::store(out + (int64_t)h * kHeadDim + 4 * lane, res);
+}
+
+// ------------------------------------------------- LM head + greedy argmax ----
+// logits[r] = x . W[r] (W bf16 [vocab][hidden] as in the checkpoint, fp32
+// accumulation, rounded to the act dtype for 16-bit activations), then the
+// index of the largest logit, the lowest index among equal maxima (what
+// torch.argmax returns), written to *token (int64).  A warp takes one row at
+// a time (lane j: 16-byte chunks j, j + 32, ... of the row, x held in
+// registers); per-CTA winners go to the workspace and the last CTA (counter,
+// reset by that CTA) picks the overall one.
+template <typename TX, int NCH>
+__global__ void __launch_bounds__(256) k8_lm_head_argmax(const TX *x, const __nv_bfloat16 *w, int64_t vocab,
+                                                         TX *logits, float *part_val, int64_t *part_idx,
+                                                         unsigned *counter, int64_t *token) {
+  constexpr int H = NCH * 256;
+  __shared__ float s_val[8];
+  __shared__ int64_t s_idx[8];
+  __shared__ unsigned s_last;
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  float xr[NCH * 8];
+  pdl_wait();
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xr[c * 8 + e] = Act<TX>::to_f(Act<TX>::ld_cg(x + c * 256 + lane * 8 + e));
+  float best = -INFINITY;
+  int64_t best_i = INT64_MAX;
+  const int64_t nw = (int64_t)gridDim.x * 8;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + wp; r < vocab; r += nw) {
+    const __nv_bfloat16 *row = w + r * H + lane * 8;
+    uint4 raw[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) raw[c] = ldg_stream(row + c * 256);
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const __nv_bfloat16 *b = reinterpret_cast<const __nv_bfloat16 *>(&raw[c]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(xr[c * 8 + e], __bfloat162float(b[e]), acc);
+    }
+    acc = warp_sum(acc);
+    const float lg = Act<TX>::round(acc);
+    if (lane == 0 && logits) logits[r] = Act<TX>::from_f(lg);
+    if (lg > best) {  // rows ascend within a warp: strict > keeps the lowest index
+      best = lg;
+      best_i = r;
+    }
+  }
+  if (lane == 0) {
+    s_val[wp] = best;
+    s_idx[wp] = best_i;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float bv = s_val[0];
+    int64_t bi = s_idx[0];
+    for (int i = 1; i < 8; ++i)
+      if (s_val[i] > bv || (s_val[i] == bv && s_idx[i] < bi)) {
+        bv = s_val[i];
+        bi = s_idx[i];
+      }
+    part_val[blockIdx.x] = bv;
+    part_idx[blockIdx.x] = bi;
+    __threadfence();
+    s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  // last CTA: reduce the per-CTA winners
+  __threadfence();
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int i = tid; i < (int)gridDim.x; i += 256) {
+    const float v = __ldcg(part_val + i);
+    const int64_t ix = (int64_t)__ldcg(reinterpret_cast<const long long *>(part_idx) + i);
+    if (v > bv || (v == bv && ix < bi)) {
+      bv = v;
+      bi = ix;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    s_val[wp] = bv;
+    s_idx[wp] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int i = 1; i < 8; ++i)
+      if (s_val[i] > bv || (s_val[i] == bv && s_idx[i] < bi)) {
+        bv = s_val[i];
+        bi = s_idx[i];
+      }
+    *token = bi == INT64_MAX ? 0 : bi;
+    *counter = 0u;
+  }
+}
+
+constexpr int kLmHeadCTAs = 148 * 2;   // 2 CTAs of 256 threads per SM (96 registers a thread at hidden 2048)
+
+}  // namespace tmoe
+
+using namespace tmoe;
+
+// ------------------------------------------------------------------ C ABI ----
+namespace {
+struct EmbedLaunch {
+  const int64_t *ids; int64_t tokens; const void *table; int hidden; int64_t vocab; void *out; uint32_t *status;
+  cudaStream_t s;
+  template <typename TO> int run() {
+    return launch_pdl(k8_embed<TO>, dim3((unsigned)tokens), dim3(256), 0, s, "k8_embed launch", ids,
+                      (const __nv_bfloat16 *)table, hidden, vocab, (TO *)out, status);
+  }
+};
+struct NormLaunch {
+  const void *x; int64_t tokens; int hidden; const void *w; float eps; void *out; cudaStream_t s;
+  template <typename TA> int run() {
+    return launch_pdl(k8_rmsnorm<TA>, dim3((unsigned)tokens), dim3(256), 0, s, "k8_rmsnorm launch",
+                      (const TA *)x, (const TA *)w, hidden, eps, (TA *)out);
+  }
+};
+struct RopeLaunch {
+  const void *qkv; int64_t tokens; int nh, nkv; const void *qn, *kn; float eps; const void *rope;
+  const int64_t *pos; int64_t max_len; void *q_out, *k_cache, *v_cache; uint32_t *status; cudaStream_t s;
+  template <typename TA> int run() {
+    const dim3 grid((unsigned)tokens, (unsigned)((nh + 2 * nkv + 7) / 8));
+    return launch_pdl(k8_qk_rope_kv<TA>, grid, dim3(256), 0, s, "k8_qk_rope_kv launch", (const TA *)qkv,
+                      (const TA *)qn, (const TA *)kn, eps, (const TA *)rope, pos, nh, nkv, max_len, (TA *)q_out,
+                      (TA *)k_cache, (TA *)v_cache, status);
+  }
+};
+struct AttnLaunch {
+  const void *q, *kc, *vc; const int64_t *pos; int64_t max_len; int nh, nkv, splits; float scale; void *out;
+  float *part; unsigned *counters; cudaStream_t s;
+  template <typename TA> int run() {
+    const size_t smem = (size_t)4 * kAttnTile * kHeadDim * sizeof(TA);
+    return launch_pdl(k8_attn_decode<TA>, dim3(nkv, splits), dim3(32 * (nh / nkv)), smem, s,
+                      "k8_attn_decode launch", (const TA *)q, (const TA *)kc, (const TA *)vc, pos, max_len, nh,
+                      nkv, scale, (TA *)out, part, counters);
+  }
+};
+template <int NCH> struct LmHeadLaunch {
+  const void *x; const void *w; int64_t vocab; void *logits; float *pv; int64_t *pi; unsigned *cnt;
+  int64_t *token; cudaStream_t s;
+  template <typename TX> int run() {
+    return launch_pdl(k8_lm_head_argmax<TX, NCH>, dim3(kLmHeadCTAs), dim3(256), 0, s, "k8_lm_head_argmax launch",
+                      (const TX *)x, (const __nv_bfloat16 *)w, vocab, (TX *)logits, pv, pi, cnt, token);
+  }
+};
+
+int64_t attn_ws_bytes(int nh, int nkv, int splits) {
+  return (int64_t)nh * splits * (kHeadDim + 4) * 4 + 256;
+}
+}  // namespace
+
+extern "C" int tm_embed(const int64_t *ids, int64_t tokens, const void *table_bf16, int hidden, int64_t vocab,
+                        int act_dtype, void *out, uint32_t *status, void *stream) {
+  TM_REQUIRE(ids && table_bf16 && out, "null pointer");
+  TM_REQUIRE(tokens >= 1 && tokens <= (1 << 20) && hidden > 0 && vocab > 0, "bad shape");
+  EmbedLaunch f{ids, tokens, table_bf16, hidden, vocab, out, status, as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
+extern "C" int tm_rmsnorm(const void *x, int64_t tokens, int hidden, int act_dtype, const void *weight, float eps,
+                          void *out, void *stream) {
+  TM_REQUIRE(x && weight && out, "null pointer");
+  TM_REQUIRE(tokens >= 1 && tokens <= (1 << 20) && hidden > 0, "bad shape");
+  NormLaunch f{x, tokens, hidden, weight, eps, out, as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
+extern "C" int tm_qk_rope_kv(const void *qkv, int64_t tokens, int n_heads, int n_kv_heads, int head_dim,
+                             int act_dtype, const void *q_norm_w, const void *k_norm_w, float eps,
+                             const void *rope_table, const int64_t *positions, int64_t max_len, void *q_out,
+                             void *k_cache, void *v_cache, uint32_t *status, void *stream) {
+  TM_REQUIRE(qkv && q_norm_w && k_norm_w && rope_table && positions && q_out && k_cache && v_cache,
+             "null pointer");
+  TM_REQUIRE(head_dim == kHeadDim, "head_dim %d unsupported (128)", head_dim);
+  TM_REQUIRE(tokens >= 1 && tokens <= (1 << 20) && n_heads >= 1 && n_kv_heads >= 1 && max_len >= 1,
+             "bad shape");
+  TM_REQUIRE(aligned(qkv, 16) && aligned(q_out, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) &&
+                 aligned(rope_table, 16),
+             "buffers must be 16-byte aligned");
+  RopeLaunch f{qkv, tokens, n_heads, n_kv_heads, q_norm_w, k_norm_w, eps, rope_table, positions, max_len,
+               q_out, k_cache, v_cache, status, as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
+extern "C" int64_t tm_attn_decode_workspace_bytes(int n_heads, int n_kv_heads, int splits) {
+  if (n_heads < 1 || n_kv_heads < 1 || splits < 1) return fail(TM_ERR_INVALID, "bad shape");
+  return attn_ws_bytes(n_heads, n_kv_heads, splits);
+}
+
+extern "C" int tm_attn_decode(const void *q, const void *k_cache, const void *v_cache, const int64_t *position,
+                              int64_t max_len, int n_heads, int n_kv_heads, int head_dim, int act_dtype,
+                              float scale, int splits, void *out, void *ws, int64_t ws_bytes, void *stream) {
+  TM_REQUIRE(q && k_cache && v_cache && position && out && ws, "null pointer");
+  TM_REQUIRE(head_dim == kHeadDim, "head_dim %d unsupported (128)", head_dim);
+  TM_REQUIRE(n_kv_heads >= 1 && n_heads % n_kv_heads == 0 && n_heads / n_kv_heads <= kHeadMaxAttnWarps,
+             "%d query heads over %d KV heads unsupported (at most %d per KV head)", n_heads, n_kv_heads,
+             kHeadMaxAttnWarps);
+  TM_REQUIRE(splits >= 1 && splits <= 1024 && max_len >= 1, "bad splits %d / max_len %lld", splits,
+             (long long)max_len);
+  TM_REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(out, 16) && aligned(ws, 16),
+             "buffers must be 16-byte aligned");
+  const int64_t need = attn_ws_bytes(n_heads, n_kv_heads, splits);
+  if (ws_bytes < need) return fail(TM_ERR_WORKSPACE, "attention workspace %lld < %lld bytes", (long long)ws_bytes,
+                                   (long long)need);
+  float *part = static_cast<float *>(ws);
+  unsigned *counters = reinterpret_cast<unsigned *>(static_cast<char *>(ws) + need - 256);
+  TM_REQUIRE(n_kv_heads <= 64, "at most 64 KV heads");
+  AttnLaunch f{q, k_cache, v_cache, position, max_len, n_heads, n_kv_heads, splits, scale, out, part, counters,
+               as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
+extern "C" int64_t tm_lm_head_workspace_bytes(void) {
+  return (int64_t)kLmHeadCTAs * (4 + 8) + 256;
+}
+
+extern "C" int tm_lm_head_argmax(const void *x, int hidden, int act_dtype, const void *w_bf16, int64_t vocab,
+                                 void *logits, int64_t *token, void *ws, int64_t ws_bytes, void *stream) {
+  TM_REQUIRE(x && w_bf16 && token && ws, "null pointer");
+  TM_REQUIRE(vocab >= 1 && hidden % 256 == 0 && hidden >= 256 && hidden <= 4096,
+             "hidden %d must be a multiple of 256 in [256, 4096]", hidden);
+  TM_REQUIRE(aligned(w_bf16, 16) && aligned(x, 16) && aligned(ws, 16), "buffers must be 16-byte aligned");
+  if (ws_bytes < tm_lm_head_workspace_bytes())
+    return fail(TM_ERR_WORKSPACE, "LM-head workspace %lld < %lld bytes", (long long)ws_bytes,
+                (long long)tm_lm_head_workspace_bytes());
+  char *b = static_cast<char *>(ws);
+  int64_t *pi = reinterpret_cast<int64_t *>(b);
+  float *pv = reinterpret_cast<float *>(b + (int64_t)kLmHeadCTAs * 8);
+  unsigned *cnt = reinterpret_cast<unsigned *>(b + (int64_t)kLmHeadCTAs * 12 + 128 - ((int64_t)kLmHeadCTAs * 12) % 128);
+  cudaStream_t s = as_stream(stream);
+  switch (hidden / 256) {
+#define TM_LMH(N)                                                                   \
+  case N: {                                                                          \
+    LmHeadLaunch<N> f{x, w_bf16, vocab, logits, pv, pi, cnt, token, s};              \
+    return dispatch_act(act_dtype, f);                                               \
+  }
+    TM_LMH(1) TM_LMH(2) TM_LMH(4) TM_LMH(8) TM_LMH(16)
+#undef TM_LMH
+    default: return fail(TM_ERR_UNSUPPORTED, "hidden %d unsupported (256 * {1, 2, 4, 8, 16})", hidden);
+  }
+}

@@ -175,6 +175,47 @@ __global__ void __launch_bounds__(kLinThreads) k6_linear(LinArgs<TA> a) {
   }
 }
 
+// fp32 activations: a CUDA-core kernel on the same packed layout.  Every
+// weight is dequantised as the reference's fp32 load_weight does (e4m3 ->
+// fp32 exactly, times its block scale: one fp32 rounding) and accumulated in
+// fp32: the reference's fp32 F.linear up to the order of the sums.  CTA = one
+// packed 16-row group; warp w takes rows 4w..4w+3, lane j the 16-column
+// chunks j, j + 32, ... of a row; the lanes' sums are added by shuffles.
+__global__ void __launch_bounds__(kLinThreads) k6_linear_f32(LinArgs<float> a) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int rg = blockIdx.x;
+  const int KC = a.K / 16, KB = a.K / 128;
+  const uint8_t *tile = a.w + (int64_t)rg * kLinRows * a.K;   // [K/16][16 rows][16 B]
+  for (int rr = 0; rr < kLinRows / kLinWarps; ++rr) {
+    const int r = w * (kLinRows / kLinWarps) + rr;
+    const int n = rg * kLinRows + r;
+    const float *srow = a.s + (int64_t)(n / 128) * KB;
+    for (int t = 0; t < a.T; ++t) {
+      const float *xt = a.x + (int64_t)t * a.K;
+      float acc = 0.f;
+      for (int kc = lane; kc < KC; kc += 32) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(tile + ((int64_t)kc * kLinRows + r) * 16);
+        const float sc = srow[kc / 8];
+        const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float f[4];
+          e4m3x4_to_f32(wd[q], f[0], f[1], f[2], f[3]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc = fmaf(__ldcg(xt + kc * 16 + q * 4 + i), f[i] * sc, acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        const int64_t o = (int64_t)t * a.N + n;
+        a.out[o] = a.residual ? acc + __ldcg(a.residual + o) : acc;
+      }
+    }
+  }
+}
+
 static size_t linear_smem(int K) {
   return (size_t)kLinRows * K + (size_t)kLinNT * (K + 8) * 2 + (size_t)(K / 128) * sizeof(float);
 }
@@ -184,7 +225,10 @@ struct LinearLaunch {
   const uint8_t *w; const float *s; const void *residual; void *out; uint32_t *status; cudaStream_t st;
   template <typename TA> int run() {
     if constexpr (sizeof(TA) != 2) {
-      return fail(TM_ERR_UNSUPPORTED, "tm_fp8_linear: act dtype must be bf16 or fp16");
+      LinArgs<float> a;
+      a.x = (const float *)x; a.w = w; a.s = s; a.residual = (const float *)residual; a.out = (float *)out;
+      a.status = status; a.T = (int)T; a.K = K; a.N = N;
+      return launch_pdl(k6_linear_f32, dim3(N / kLinRows), dim3(kLinThreads), 0, st, "k6_linear_f32 launch", a);
     } else {
       LinArgs<TA> a;
       a.x = (const TA *)x; a.w = w; a.s = s; a.residual = (const TA *)residual; a.out = (TA *)out;

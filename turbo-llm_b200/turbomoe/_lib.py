@@ -53,6 +53,13 @@ SIGNATURES = {
                                          _i, _p, _p, _p, _p, _p, _p, _p]),
     "tm_pack_linear": (_i, [_p, _i, _i, _p, _p]),
     "tm_fp8_linear": (_i, [_p, _i64, _i, _i, _i, _p, _p, _p, _p, _p, _p]),
+    "tm_embed": (_i, [_p, _i64, _p, _i, _i64, _i, _p, _p, _p]),
+    "tm_rmsnorm": (_i, [_p, _i64, _i, _i, _p, C.c_float, _p, _p]),
+    "tm_qk_rope_kv": (_i, [_p, _i64, _i, _i, _i, _i, _p, _p, C.c_float, _p, _p, _i64, _p, _p, _p, _p, _p]),
+    "tm_attn_decode_workspace_bytes": (_i64, [_i, _i, _i]),
+    "tm_attn_decode": (_i, [_p, _p, _p, _p, _i64, _i, _i, _i, _i, C.c_float, _i, _p, _p, _i64, _p]),
+    "tm_lm_head_workspace_bytes": (_i64, []),
+    "tm_lm_head_argmax": (_i, [_p, _i, _i, _p, _i64, _p, _p, _p, _i64, _p]),
     "tm_ep_buffer_bytes": (_i64, [_i, _i64, _i, _i, _i, _i]),
     "tm_ep_create": (_i, [_i, _i, _i, _i, _i, _i, _i, _i64, _p, C.POINTER(_p)]),
     "tm_ep_connect": (_i, [_p, _p]),
@@ -72,6 +79,7 @@ TM_EP_MAX_RANKS = 8
 TM_EP_HANDLE_BYTES = 64
 TM_STATUS_TIMEOUT = 2
 TM_STATUS_PEER_FAILED = 4
+TM_STATUS_BAD_TOKEN_ID = 8
 
 _lock = threading.Lock()
 _lib = None

@@ -133,24 +133,44 @@ class PeerExpertParallelMoE:
     its own shard `local_experts` (PackedExperts of experts
     [rank * E/G, (rank + 1) * E/G)) - construction is collective (it exchanges
     the buffers' IPC handles) - and calls `forward` in the same order.  Without
-    an initialised process group it runs as a single rank."""
+    an initialised process group, or with ``single=True``, it runs as a single
+    rank owning every expert.
+
+    ``channel``: another PeerExpertParallelMoE of the same shape whose context
+    (peer buffers, workspaces) this layer reuses.  The layers of a model run
+    one after the other on one stream, and a source dispatches call n + 1 only
+    after every owner has returned call n, so one context can carry every
+    layer: construction is then local (no handle exchange) and only the
+    instance that created the context may ``close`` it."""
 
     def __init__(self, router_w: torch.Tensor, local_experts, top_k: int, max_tokens: int, group=None,
-                 timeout_s: float = 2.0):
+                 timeout_s: float = 2.0, channel: "PeerExpertParallelMoE | None" = None, single: bool = False):
         import ctypes as C
         from . import ops
         from ._lib import TM_EP_HANDLE_BYTES, check, lib
         self._C, self._ops, self._check, self._L = C, ops, check, lib()
-        single = not (dist.is_available() and dist.is_initialized())
+        E, H = router_w.shape
+        self.router_w = router_w.contiguous()
+        self.local = local_experts
+        if channel is not None:
+            if (channel.E, channel.k, channel.H, channel.I) != (E, top_k, H, local_experts.inter) or \
+                    channel.router_w.dtype != router_w.dtype or max_tokens > channel.max_tokens or \
+                    local_experts.n_experts != channel.local.n_experts:
+                raise ValueError("channel has another expert-parallel shape")
+            self.group, self.G, self.rank = channel.group, channel.G, channel.rank
+            self.E, self.k, self.H, self.I = E, top_k, H, local_experts.inter
+            self.max_tokens = channel.max_tokens
+            self.ctx, self.ws, self.owner_ws = channel.ctx, channel.ws, channel.owner_ws
+            self._owner = False
+            return
+        self._owner = True
+        single = single or not (dist.is_available() and dist.is_initialized())
         self.group = group
         self.G = 1 if single else dist.get_world_size(group)
         self.rank = 0 if single else dist.get_rank(group)
-        E, H = router_w.shape
         self.E, self.k, self.H, self.I = E, top_k, H, local_experts.inter
         if E % self.G or local_experts.n_experts != E // self.G:
             raise ValueError(f"{local_experts.n_experts} local experts do not match {E} over {self.G} ranks")
-        self.router_w = router_w.contiguous()
-        self.local = local_experts
         self.max_tokens = max_tokens
         dev = router_w.device
         code = ops._code(router_w.dtype)
@@ -175,25 +195,34 @@ class PeerExpertParallelMoE:
         check(self._L.tm_workspace_init(self.owner_ws.data_ptr(), n, ops._stream(self.owner_ws)), "tm_workspace_init")
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, marks=None) -> torch.Tensor:
+        """One layer call.  ``marks``: optional list of 5 CUDA events recorded
+        on the stream before the router, the dispatch, the experts, the combine
+        and after it (per-phase timing)."""
         ops, check, L = self._ops, self._check, self._L
         x = x.contiguous()
         T = x.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
+        mark = (lambda i: marks[i].record()) if marks is not None else (lambda i: None)
+        mark(0)
         idx, w = ops.router_topk(x, self.router_w, self.k, self.ws)
         s = ops._stream(x)
         buf = self.ws.buf
+        mark(1)
         check(L.tm_ep_dispatch(self.ctx, x.data_ptr(), T, idx.data_ptr(), buf.data_ptr(), buf.numel(), s),
               "tm_ep_dispatch")
         le = self.local
+        mark(2)
         check(L.tm_ep_experts(self.ctx, le.w13.data_ptr(), le.s13.data_ptr(), le.w2.data_ptr(), le.s2.data_ptr(),
                               self.owner_ws.data_ptr(), self.owner_ws.numel(), s), "tm_ep_experts")
         if out is None:
             out = torch.empty_like(x)
         res = residual.contiguous() if residual is not None else None
+        mark(3)
         check(L.tm_ep_combine(self.ctx, w.data_ptr(), T, buf.data_ptr(), buf.numel(),
                               res.data_ptr() if res is not None else None, out.data_ptr(), s), "tm_ep_combine")
+        mark(4)
         return out
 
     def status(self) -> int:
@@ -207,7 +236,11 @@ class PeerExpertParallelMoE:
         return int(v.value) | int(o.value) | self.ws.status()
 
     def close(self):
-        """Collective: every rank, after its last forward."""
+        """Collective: every rank, after its last forward (a no-op on a layer
+        that borrowed another one's context)."""
+        if not self._owner:
+            self.ctx = self._C.c_void_p()
+            return
         if self.ctx:
             torch.cuda.synchronize()
             if self.G > 1:
