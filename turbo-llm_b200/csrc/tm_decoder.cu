@@ -209,7 +209,8 @@ __global__ void __launch_bounds__(kHeadMaxAttnWarps * 32) k8_attn_decode(
   const int g = blockIdx.x, s = blockIdx.y, S = gridDim.y;
   const int h = g * G + w;
   pdl_wait();
-  const int64_t n = (int64_t)__ldcg(reinterpret_cast<const long long *>(position)) + 1;
+  // context length; a position past the cache (refused by tm_qk_rope_kv) is clamped
+  const int64_t n = min((int64_t)__ldcg(reinterpret_cast<const long long *>(position)) + 1, max_len);
   const int64_t per = ((n + S - 1) / S + kAttnTile - 1) / kAttnTile * kAttnTile;
   const int64_t p_begin = (int64_t)s * per;
   const int64_t p_end = min(n, p_begin + per);
