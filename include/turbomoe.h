@@ -211,6 +211,21 @@ int tm_moe_prefill_grouped(const void *x, int64_t tokens, int hidden, int inter,
                            const void *residual, void *out, void *ws, int64_t ws_bytes,
                            void *stream);
 
+/* The same layer call as tm_moe_prefill_grouped (same arguments, plan,
+ * workspace and results up to rounding) on FP8 tensor-core GEMMs
+ * (tcgen05.mma kind::f8f6f4) that multiply the packed e4m3 weights as they
+ * are stored: the tokens enter as two e4m3 terms (exact for bf16), each
+ * 128 x 128 weight block's scale is applied to its fp32 partial sum, g, u,
+ * silu(g) and h are rounded to bf16 as the reference rounds them
+ * (execution/moe.py:157-202).  Built for few tokens per expert (expert-parallel
+ * owners, batched decode); bf16 activations only; hidden and inter multiples
+ * of 128. */
+int tm_moe_grouped_f8(const void *x, int64_t tokens, int hidden, int inter, int n_experts, int top_k,
+                      int act_dtype, const void *topk_w, const uint8_t *w13, const float *s13,
+                      const uint8_t *w2, const float *s2, const uint8_t *sh_w13, const float *sh_s13,
+                      const uint8_t *sh_w2, const float *sh_s2, int shared_inter, const void *sh_gate_w,
+                      const void *residual, void *out, void *ws, int64_t ws_bytes, void *stream);
+
 /* Weighted combine of per-slot expert outputs in top-k order:
  * out[t] = residual[t] + sum_r topk_w[t,r] * y[pair_slot[t*top_k + r]]
  * (fp32 sums, slots < 0 skipped).  Replaces the weighted scatter-add of

@@ -495,6 +495,18 @@ int prefill_expert_outputs(const void *x, int64_t tokens, int hidden, int inter,
                            int act_dtype, const uint8_t *w13, const float *s13, const uint8_t *w2, const float *s2,
                            void *ws, const WsLayout &L, cudaStream_t stream);
 
+// The FP8 grouped GEMMs (tm_moe_f8.cu) for bf16 activations: per-slot expert
+// outputs (bf16, slot order) in the ypart region, like prefill_expert_outputs.
+int f8_expert_outputs(const void *x, int64_t T, int H, int I, int E, int k, const uint8_t *w13, const float *s13,
+                      const uint8_t *w2, const float *s2, const uint8_t *sh_w13, const float *sh_s13,
+                      const uint8_t *sh_w2, const float *sh_s2, const void *sh_gate_w, void *ws, const WsLayout &L,
+                      cudaStream_t s);
+
+// out[t] = sum_r topk_w[t,r] * y[pair_slot[t*k+r]] (top-k order, fp32) (+ sh_w[t] * y[sh_slot0 + t])
+// (+ residual[t]), rounded once to act (k4_combine).
+int combine_expert_outputs(const void *y, const void *topk_w, const int *pair_slot, const void *residual, void *out,
+                           int64_t T, int H, int k, int act_dtype, const float *sh_w, int sh_slot0, cudaStream_t s);
+
 constexpr int kMetaNActive = 0;
 constexpr int kMetaPairs = 1;
 constexpr int kMetaTokens = 2;

@@ -90,6 +90,7 @@ template <typename TO>
 __global__ void __launch_bounds__(256) k8_embed(const int64_t *ids, const __nv_bfloat16 *table, int hidden,
                                                 int64_t vocab, TO *out, uint32_t *status) {
   pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int64_t id = (int64_t)__ldcg(reinterpret_cast<const long long *>(ids) + t);
   TO *o = out + (int64_t)t * hidden;
@@ -104,17 +105,32 @@ __global__ void __launch_bounds__(256) k8_embed(const int64_t *ids, const __nv_b
 
 // ---------------------------------------------------------------- RMSNorm ----
 // One CTA per token: out = round(round(x * rsqrt(mean(x^2) + eps)) * w).
+// Threads hold 4 consecutive elements (one 8- or 16-byte load), the row
+// stays in registers between the sum of squares and the output (hidden <=
+// 4096 with 256 threads).
 template <typename TA>
 __global__ void __launch_bounds__(256) k8_rmsnorm(const TA *x, const TA *w, int hidden, float eps, TA *out) {
   __shared__ float red[8];
-  pdl_wait();
   const int t = blockIdx.x, tid = threadIdx.x;
-  const TA *xr = x + (int64_t)t * hidden;
-  float ss = 0.f;
-  for (int i = tid; i < hidden; i += 256) {
-    const float v = Act<TA>::to_f(Act<TA>::ld_cg(xr + i));
-    ss = fmaf(v, v, ss);
+  float wv[4][4];
+  for (int c = 0; c < 4; ++c) {   // the weights do not depend on the previous kernel
+    const int i = (c * 256 + tid) * 4;
+    if (i < hidden) Vec4<TA>::load(w + i, wv[c]);
   }
+  pdl_wait();
+  const TA *xr = x + (int64_t)t * hidden;
+  float v[4][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int i = (c * 256 + tid) * 4;
+    if (i < hidden) {
+      Vec4<TA>::load_cg(xr + i, v[c]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ss = fmaf(v[c][e], v[c][e], ss);
+    }
+  }
+  pdl_trigger();
   ss = warp_sum(ss);
   if ((tid & 31) == 0) red[tid >> 5] = ss;
   __syncthreads();
@@ -123,10 +139,15 @@ __global__ void __launch_bounds__(256) k8_rmsnorm(const TA *x, const TA *w, int 
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)hidden + eps);
   TA *o = out + (int64_t)t * hidden;
-  for (int i = tid; i < hidden; i += 256) {
-    const float v = Act<TA>::to_f(Act<TA>::ld_cg(xr + i));
-    const float nrm = Act<TA>::round(v * r);
-    o[i] = Act<TA>::from_f(nrm * Act<TA>::to_f(w[i]));
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int i = (c * 256 + tid) * 4;
+    if (i < hidden) {
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = Act<TA>::round(v[c][e] * r) * wv[c][e];
+      Vec4<TA>::store(o + i, y);
+    }
   }
 }
 
@@ -153,6 +174,7 @@ __global__ void __launch_bounds__(256) k8_qk_rope_kv(const TA *qkv, const TA *qn
   const int e0 = 4 * lane;
   float v[4];
   Vec4<TA>::load_cg(qkv + ((int64_t)t * nheads + hh) * kHeadDim + e0, v);
+  pdl_trigger();
   if (hh >= nh + nkv) {  // v head: copy into the cache
     Vec4<TA>::store(v_cache + ((int64_t)(hh - nh - nkv) * max_len + pos) * kHeadDim + e0, v);
     return;
@@ -235,6 +257,7 @@ __global__ void __launch_bounds__(kHeadMaxAttnWarps * 32) k8_attn_decode(
   float m = -INFINITY, l = 0.f;
   Vec4<TA>::load_cg(q + (int64_t)h * kHeadDim + 4 * lane, qv);
   if (p_begin < p_end) issue(p_begin, 0);
+  pdl_trigger();
   int buf = 0;
   for (int64_t p0 = p_begin; p0 < p_end; p0 += kAttnTile, buf ^= 1) {
     if (p0 + kAttnTile < p_end) {
@@ -298,23 +321,41 @@ __global__ void __launch_bounds__(kHeadMaxAttnWarps * 32) k8_attn_decode(
   if (!s_last) return;
   if (tid == 0) counters[g] = 0u;  // self-resetting for the next call
   __threadfence();
-  float M = -INFINITY;
-  for (int j = 0; j < S; ++j) {
-    const float *pj = part + ((int64_t)h * S + j) * (kHeadDim + 4);
-    if (__ldcg(pj + 1) > 0.f) M = fmaxf(M, __ldcg(pj));
+  // merge: lane j holds the (m, l) of splits j, j + 32, ... (loads in flight
+  // together), the weights e^(m_s - M) go to every lane by shuffles
+  const float *ph = part + (int64_t)h * S * (kHeadDim + 4);
+  float mj[2], lj[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int j = lane + 32 * u;
+    const bool v = j < S;
+    lj[u] = v ? __ldcg(ph + (int64_t)j * (kHeadDim + 4) + 1) : 0.f;
+    mj[u] = v ? __ldcg(ph + (int64_t)j * (kHeadDim + 4)) : -INFINITY;
+    if (!(lj[u] > 0.f)) mj[u] = -INFINITY;
   }
-  float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int j = 0; j < S; ++j) {
-    const float *pj = part + ((int64_t)h * S + j) * (kHeadDim + 4);
-    const float lj = __ldcg(pj + 1);
-    if (!(lj > 0.f)) continue;
-    const float f = expf(__ldcg(pj) - M);
-    L = fmaf(lj, f, L);
-    const float4 oj = __ldcg(reinterpret_cast<const float4 *>(pj + 4 + 4 * lane));
-    acc[0] = fmaf(oj.x, f, acc[0]);
-    acc[1] = fmaf(oj.y, f, acc[1]);
-    acc[2] = fmaf(oj.z, f, acc[2]);
-    acc[3] = fmaf(oj.w, f, acc[3]);
+  const float M = warp_max(fmaxf(mj[0], mj[1]));
+  float fj[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) fj[u] = lj[u] > 0.f ? expf(mj[u] - M) : 0.f;
+  const float L = warp_sum(fj[0] * lj[0] + fj[1] * lj[1]);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int j0 = 0; j0 < S; j0 += 8) {
+    float4 oj[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      oj[u] = j0 + u < S ? __ldcg(reinterpret_cast<const float4 *>(ph + (int64_t)(j0 + u) * (kHeadDim + 4) + 4 + 4 * lane))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      const float f = __shfl_sync(0xffffffffu, j < 32 ? fj[0] : fj[1], j & 31);
+      if (j < S && f > 0.f) {
+        acc[0] = fmaf(oj[u].x, f, acc[0]);
+        acc[1] = fmaf(oj[u].y, f, acc[1]);
+        acc[2] = fmaf(oj[u].z, f, acc[2]);
+        acc[3] = fmaf(oj[u].w, f, acc[3]);
+      }
+    }
   }
   float res[4];
   const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -346,6 +387,7 @@ __global__ void __launch_bounds__(256) k8_lm_head_argmax(const TX *x, const __nv
   for (int c = 0; c < NCH; ++c)
 #pragma unroll
     for (int e = 0; e < 8; ++e) xr[c * 8 + e] = Act<TX>::to_f(Act<TX>::ld_cg(x + c * 256 + lane * 8 + e));
+  pdl_trigger();
   float best = -INFINITY;
   int64_t best_i = INT64_MAX;
   const int64_t nw = (int64_t)gridDim.x * 8;
@@ -494,7 +536,9 @@ extern "C" int tm_embed(const int64_t *ids, int64_t tokens, const void *table_bf
 extern "C" int tm_rmsnorm(const void *x, int64_t tokens, int hidden, int act_dtype, const void *weight, float eps,
                           void *out, void *stream) {
   TM_REQUIRE(x && weight && out, "null pointer");
-  TM_REQUIRE(tokens >= 1 && tokens <= (1 << 20) && hidden > 0, "bad shape");
+  TM_REQUIRE(tokens >= 1 && tokens <= (1 << 20) && hidden > 0 && hidden % 4 == 0 && hidden <= 4096,
+             "bad shape (hidden %d: a multiple of 4, at most 4096)", hidden);
+  TM_REQUIRE(aligned(x, 16) && aligned(weight, 16) && aligned(out, 16), "buffers must be 16-byte aligned");
   NormLaunch f{x, tokens, hidden, weight, eps, out, as_stream(stream)};
   return dispatch_act(act_dtype, f);
 }
@@ -529,7 +573,7 @@ extern "C" int tm_attn_decode(const void *q, const void *k_cache, const void *v_
   TM_REQUIRE(n_kv_heads >= 1 && n_heads % n_kv_heads == 0 && n_heads / n_kv_heads <= kHeadMaxAttnWarps,
              "%d query heads over %d KV heads unsupported (at most %d per KV head)", n_heads, n_kv_heads,
              kHeadMaxAttnWarps);
-  TM_REQUIRE(splits >= 1 && splits <= 1024 && max_len >= 1, "bad splits %d / max_len %lld", splits,
+  TM_REQUIRE(splits >= 1 && splits <= 64 && max_len >= 1, "bad splits %d (1..64) / max_len %lld", splits,
              (long long)max_len);
   TM_REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(out, 16) && aligned(ws, 16),
              "buffers must be 16-byte aligned");

@@ -860,6 +860,29 @@ struct CombineLaunch {
 };
 }  // namespace tmoe
 
+namespace tmoe {
+struct CombineAllLaunch {
+  const void *y; const void *w; const int *pair_slot; const void *residual; void *out; int64_t T; int H, k;
+  const float *sh_w; int sh_slot0; cudaStream_t s;
+  template <typename TA> int run() {
+    if constexpr (sizeof(TA) != 2) {
+      return fail(TM_ERR_UNSUPPORTED, "combine: act dtype must be bf16 or fp16");
+    } else {
+      k4_combine<TA><<<(unsigned)T, 256, 0, s>>>((const TA *)y, (const TA *)w, pair_slot, (const TA *)residual,
+                                                   (TA *)out, H, k, sh_w, sh_slot0);
+      TM_LAUNCH_CHECK("k4_combine launch");
+      return TM_OK;
+    }
+  }
+};
+int combine_expert_outputs(const void *y, const void *topk_w, const int *pair_slot, const void *residual, void *out,
+                           int64_t T, int H, int k, int act_dtype, const float *sh_w, int sh_slot0, cudaStream_t s) {
+  TM_REQUIRE(k >= 1 && k <= kPfMaxTopK && H % 8 == 0, "combine: bad shape");
+  CombineAllLaunch f{y, topk_w, pair_slot, residual, out, T, H, k, sh_w, sh_slot0, s};
+  return dispatch_act(act_dtype, f);
+}
+}  // namespace tmoe
+
 extern "C" int tm_combine_slots(const void *y, const void *topk_w, const int32_t *pair_slot, int64_t tokens,
                                 int hidden, int top_k, int act_dtype, const void *residual, void *out,
                                 void *stream) {

@@ -48,6 +48,8 @@ SIGNATURES = {
                                         _i64, _p]),
     "tm_moe_prefill_grouped": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p,
                                     _p, _p, _p, _i64, _p]),
+    "tm_moe_grouped_f8": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p,
+                               _p, _p, _p, _i64, _p]),
     "tm_combine_slots": (_i, [_p, _p, _p, _i64, _i, _i, _i, _p, _p, _p]),
     "tm_moe_decode_layer_noalloc": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                          _i, _p, _p, _p, _p, _p, _p, _p]),

@@ -343,6 +343,28 @@ def moe_prefill(x: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Wor
           "tm_moe_prefill_grouped")
 
 
+def moe_grouped_f8(x: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Workspace, out: torch.Tensor,
+                   residual: torch.Tensor | None = None, shared: PackedExperts | None = None,
+                   shared_gate_w: torch.Tensor | None = None):
+    """K7: the same call as ``moe_prefill`` on the FP8 tensor-core GEMMs
+    (tm_moe_grouped_f8; bf16 activations) for the plan already in ``ws``."""
+    T, H = x.shape
+    k = w.shape[1]
+    if shared is not None and shared_gate_w is None:
+        raise TurboMoEError("shared expert needs its gate weight")
+    if shared is not None and ws.Is < shared.inter:
+        raise TurboMoEError("workspace was sized without the shared expert")
+    buf = ws.buf
+    gate = shared_gate_w.reshape(-1).to(x.dtype).contiguous() if shared is not None else None
+    sh = (shared.w13.data_ptr(), shared.s13.data_ptr(), shared.w2.data_ptr(), shared.s2.data_ptr(), shared.inter,
+          gate.data_ptr()) if shared is not None else (None, None, None, None, 0, None)
+    check(lib().tm_moe_grouped_f8(x.data_ptr(), T, H, packed.inter, packed.n_experts, k, _code(x.dtype),
+                                  w.data_ptr(), packed.w13.data_ptr(), packed.s13.data_ptr(),
+                                  packed.w2.data_ptr(), packed.s2.data_ptr(), *sh, _ptr(residual),
+                                  out.data_ptr(), buf.data_ptr(), buf.numel(), _stream(x)),
+          "tm_moe_grouped_f8")
+
+
 def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: PackedExperts, ws: Workspace,
                 shared: PackedExperts | None = None, shared_gate_w: torch.Tensor | None = None,
                 residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
