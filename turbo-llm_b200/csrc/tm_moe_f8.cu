@@ -25,7 +25,7 @@
 //     contiguous bulk copy;
 //   * the fp32 block scales (one per 128 x 128 weight block) cannot enter an
 //     FP8 MMA, so each 128-wide K chunk is its own MMA accumulation (D = A.B,
-//     fresh per chunk, double-buffered in TMEM) and the epilogue warps add
+//     fresh per chunk, four buffers in TMEM) and the epilogue warps add
 //     scale x chunk into fp32 registers: weights, scales and activations are
 //     all exact, only the fp32 sums round.
 // gate/up epilogue: g, u rounded to bf16, silu(g) rounded, h = silu * u
@@ -54,17 +54,23 @@ namespace tmoe {
 constexpr int kF8GateUp = 0, kF8Down = 1;
 constexpr int kF8Threads = 320;                 // 10 warps
 constexpr int kF8WTma = 0, kF8WMma = 1, kF8WEpi = 2, kF8NEpi = 8;
-constexpr int kF8GroupMax = 64;                 // tokens per unit (2 terms -> <= 128 MMA columns)
-constexpr int kF8Tile = 128 * 128;              // one A tile / the B stage: 16 KB
+constexpr int kF8GroupMax = 32;                 // tokens per unit (2 terms -> <= 64 MMA columns)
+constexpr int kF8Tile = 128 * 128;              // one A tile (128 rows x 128 K bytes): 16 KB
+constexpr int kF8BTile = 2 * kF8GroupMax * 128; // the B rows of one stage: 8 KB
+constexpr int kF8ExpStride = 16;                // bytes per slot of the h exponents (I <= 2048)
 constexpr int kF8MaxExperts = 1024;
 
 template <int kMode> struct F8Cfg {
-  static constexpr int kOps = kMode == kF8GateUp ? 2 : 1;         // A operands per unit (gate, up)
-  static constexpr int kStages = kMode == kF8GateUp ? 4 : 6;
-  static constexpr int kStageBytes = (kOps + 1) * kF8Tile;
+  // two A tiles per K chunk: gate and up of the same 128 rows, or two
+  // 128-row halves of a 256-row block of the down projection
+  static constexpr int kOps = 2;
+  static constexpr int kRowsPerUnit = kMode == kF8GateUp ? 128 : 256;
+  static constexpr int kStages = 5;
+  static constexpr int kStageBytes = kOps * kF8Tile + kF8BTile;
   static constexpr int kSmem = kStages * kStageBytes + 1024;
-  static constexpr int kBufCols = kOps * 128;                     // one accumulator buffer
-  static constexpr int kTmemCols = kMode == kF8GateUp ? 512 : 256;
+  static constexpr int kAccBufs = 4;                              // accumulator buffers (MMA runs ahead)
+  static constexpr int kBufCols = kOps * 2 * kF8GroupMax;         // one buffer: <= 64 columns per operand
+  static constexpr int kTmemCols = kAccBufs * kBufCols;            // 512 (gate/up) or 256 (down)
 };
 
 struct F8Args {
@@ -75,9 +81,9 @@ struct F8Args {
   const int *meta;
   const int4 *act_rec; // {expert, count, first slot, 0}
   const int *sexp;     // gate/up: per-slot power of 2 of the token terms
-  const int8_t *hexp;  // down: per-(slot, 128-row block of I) power of 2 of the h terms
+  const int8_t *hexp;  // down: per-(slot, 128-row block of I) power of 2 of the h terms, [slot][16]
   uint8_t *hq;         // gate/up output: h terms [I/16][R][16 B]
-  int8_t *hexp_out;    // gate/up output: [slot][I/128]
+  int8_t *hexp_out;    // gate/up output: [slot][16] (entry mt of slot)
   __nv_bfloat16 *y;    // down output: [slot][H]
   uint32_t *status;
   int H, I, E, P, T, has_shared;
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
   extern __shared__ __align__(1024) uint8_t f8_smem_raw[];
   uint8_t *stages = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(f8_smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[C::kStages], empty[C::kStages];
-  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar, epi_bar;
+  __shared__ __align__(8) uint64_t acc_full[C::kAccBufs], acc_empty[C::kAccBufs], drain_bar, epi_bar;
   __shared__ int prefix[kF8MaxExperts + 2];
   __shared__ float red[4][kF8GroupMax];  // gate/up: per-quadrant max |h| of each token of the unit
   __shared__ uint32_t tmem_slot;
@@ -195,7 +201,8 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int M = kGU ? a.I : a.H;     // weight rows per expert
   const int K = kGU ? a.H : a.I;     // reduction length
-  const int MT = M / 128, KC = K / 128;
+  const int MB = M / 128;            // 128-row blocks (of the block scales)
+  const int MT = M / C::kRowsPerUnit, KC = K / 128;
   const int4 shared_rec = make_int4(a.E, a.T, a.P, 0);
 
   if (warp == 0) {
@@ -237,12 +244,12 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kF8NEpi * 32);
+      mbar_init(&acc_empty[b], kF8NEpi);
     }
     mbar_init(&drain_bar, 1);
-    mbar_init(&epi_bar, kF8NEpi * 32);
+    mbar_init(&epi_bar, kF8NEpi);
     mbar_fence_init();
   }
   if (warp == kF8WMma) {
@@ -257,44 +264,48 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
 
   if (warp == kF8WTma) {
     // ------------------------------------------------------ TMA producer ----
-    if (lane == 0) {
-      const uint64_t pol = l2_evict_first();
-      uint32_t it = 0;
-      bool ok = true;
-      for (int j = 0; j < n_local && ok; ++j) {
-        const F8Tile t = tile_at(j);
-        const bool sh = t.e == a.E;
-        const CUtensorMap *map = sh ? &tm_sh : &tm_w;
-        const int g0 = (sh ? 0 : t.e * (M / 16)) + t.mt * 8;   // first 16-row group of the block
-        const uint32_t slab = (uint32_t)t.nvalid * 2 * 16;      // bytes of one 16-byte K slab of the rows
-        const uint8_t *bsrc = a.bq + (size_t)t.slot0 * 2 * 16;
-        for (int kc = 0; kc < KC; ++kc, ++it) {
-          const int st = it % C::kStages;
-          if (!f8_wait(&empty[st], ((it / C::kStages) & 1) ^ 1, &abort_flag, a.status)) { ok = false; break; }
-          uint8_t *sbase = stages + st * C::kStageBytes;
+    // lane 0 waits for the stage and issues the weight tiles; lanes 0-7 each
+    // copy one 16-byte K slab of the unit's token rows
+    const uint64_t pol = l2_evict_first();
+    uint32_t it = 0;
+    bool ok = true;
+    for (int j = 0; j < n_local && ok; ++j) {
+      const F8Tile t = tile_at(j);
+      const bool sh = t.e == a.E;
+      const CUtensorMap *map = sh ? &tm_sh : &tm_w;
+      const int g0 = (sh ? 0 : t.e * (M / 16)) + t.mt * (C::kRowsPerUnit / 16);   // first 16-row group
+      const uint32_t slab = (uint32_t)t.nvalid * 2 * 16;      // bytes of one 16-byte K slab of the rows
+      const uint32_t ncol = (uint32_t)((t.nvalid * 2 + 15) & ~15);
+      const uint8_t *bsrc = a.bq + (size_t)t.slot0 * 2 * 16;
+      for (int kc = 0; kc < KC; ++kc, ++it) {
+        const int st = it % C::kStages;
+        bool got = true;
+        if (lane == 0) got = f8_wait(&empty[st], ((it / C::kStages) & 1) ^ 1, &abort_flag, a.status);
+        if (!__shfl_sync(0xffffffffu, (int)got, 0)) { ok = false; break; }
+        uint8_t *sbase = stages + st * C::kStageBytes;
+        if (lane == 0) {
           mbar_arrive_expect_tx(&full[st], (uint32_t)(C::kOps * kF8Tile) + 8 * slab);
           if constexpr (kGU) {
             f8_tma4(sbase, map, 0, g0, kc * 8, 0, &full[st], pol);
             f8_tma4(sbase + kF8Tile, map, 0, g0, kc * 8, 1, &full[st], pol);
           } else {
             f8_tma3(sbase, map, 0, g0, kc * 8, &full[st], pol);
-          }
-          uint8_t *bdst = sbase + C::kOps * kF8Tile;
-          const uint32_t ncol = (uint32_t)((t.nvalid * 2 + 15) & ~15);
-          if (slab) {
-#pragma unroll 1
-            for (int kk = 0; kk < 8; ++kk)
-              tma_bulk_g2s(bdst + kk * ncol * 16, bsrc + (size_t)(kc * 8 + kk) * a.R * 16, slab, &full[st]);
+            f8_tma3(sbase + kF8Tile, map, 0, g0 + 8, kc * 8, &full[st], pol);
           }
         }
+        __syncwarp();   // the expected byte count is set before any slab copy can complete
+        if (slab && lane < 8)
+          tma_bulk_g2s(sbase + C::kOps * kF8Tile + lane * ncol * 16, bsrc + (size_t)(kc * 8 + lane) * a.R * 16, slab,
+                       &full[st]);
       }
-      // no copy may still be landing in shared memory when the CTA exits
-      // (after an abort the MMA warp stops consuming stages)
+    }
+    // no copy may still be landing in shared memory when the CTA exits
+    // (after an abort the MMA warp stops consuming stages)
+    if (lane == 0)
       for (uint32_t i = it > (uint32_t)C::kStages ? it - C::kStages : 0; i < it; ++i) {
         volatile int no_abort = 0;
         f8_wait(&full[i % C::kStages], (i / C::kStages) & 1, &no_abort, a.status);
       }
-    }
   } else if (warp == kF8WMma) {
     // ------------------------------------------------------- MMA issuer ----
     if (lane == 0) {
@@ -306,8 +317,8 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
         const uint32_t n_mma = ncol < 16 ? 16 : ncol;
         const uint32_t idesc = (1u << 4) | ((n_mma >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
         for (int kc = 0; kc < KC; ++kc, ++it, ++ch) {
-          const int buf = ch & 1, st = it % C::kStages;
-          if (!f8_wait(&acc_empty[buf], ((ch >> 1) & 1) ^ 1, &abort_flag, a.status) ||
+          const int buf = ch % C::kAccBufs, st = it % C::kStages;
+          if (!f8_wait(&acc_empty[buf], ((ch / C::kAccBufs) & 1) ^ 1, &abort_flag, a.status) ||
               !f8_wait(&full[st], (it / C::kStages) & 1, &abort_flag, a.status)) { ok = false; break; }
           f8_fence_after();
           const uint32_t sbase = smem_u32(stages + st * C::kStageBytes);
@@ -318,7 +329,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
 #pragma unroll
             for (int op = 0; op < C::kOps; ++op) {
               const uint64_t ad = f8_desc(sbase + op * kF8Tile + (uint32_t)(2 * s) * 2048, 2048, 128);
-              f8_mma(tmem + buf * C::kBufCols + op * 128, ad, bd, idesc, s > 0);
+              f8_mma(tmem + buf * C::kBufCols + op * (2 * kF8GroupMax), ad, bd, idesc, s > 0);
             }
           }
           issued = true;
@@ -335,13 +346,14 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
   } else {
     // --------------------------------------------------------- epilogue ----
     const int q = warp & 3;                    // TMEM lane quadrant
-    const int hf = (warp - kF8WEpi) >> 2;      // 16-column blocks hf, hf + 2, ...
+    const int hf = (warp - kF8WEpi) >> 2;      // 16-column block hf (tokens 8 hf .. 8 hf + 7) and hf + 2
     const int m = q * 32 + lane;               // weight row within the block
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t ch = 0, ep = 0;  // accumulator chunks consumed, epilogue-barrier phases passed
-    // all epilogue threads meet (bounded: a warp that aborted makes the others time out, never hang)
+    // the 8 epilogue warps meet (bounded: a warp that aborted makes the others time out, never hang)
     auto epi_sync = [&]() -> bool {
-      f8_arrive(&epi_bar);
+      __syncwarp();
+      if (lane == 0) f8_arrive(&epi_bar);
       const bool r = f8_wait(&epi_bar, ep & 1, &abort_flag, a.status);
       ++ep;
       return r;
@@ -350,68 +362,96 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
       const F8Tile t = tile_at(j);
       const bool sh = t.e == a.E;
       const int nblk = (t.nvalid * 2 + 15) >> 4;
-      float acc[C::kOps][4][16];
+      float acc[C::kOps][2][16];
 #pragma unroll
       for (int op = 0; op < C::kOps; ++op)
 #pragma unroll
-        for (int bi = 0; bi < 4; ++bi)
+        for (int bi = 0; bi < 2; ++bi)
 #pragma unroll
           for (int c = 0; c < 16; ++c) acc[op][bi][c] = 0.f;
-      // block scales of this unit: gate/up s13 [E][I/128][2][H/128]; down s2 [E][H/128][I/128]
-      const float *sc = kGU ? (sh ? a.sh_s : a.s + (size_t)t.e * MT * 2 * KC) + (size_t)t.mt * 2 * KC
-                            : (sh ? a.sh_s : a.s + (size_t)t.e * MT * KC) + (size_t)t.mt * KC;
+      // block scales of this unit, lane l holding chunks l, l + 32, ...:
+      // gate/up s13 [E][I/128][2][H/128]; down s2 [E][H/128][I/128]
+      const float *sc = kGU ? (sh ? a.sh_s : a.s + (size_t)t.e * MB * 2 * KC) + (size_t)t.mt * 2 * KC
+                            : (sh ? a.sh_s : a.s + (size_t)t.e * MB * KC) + (size_t)t.mt * 2 * KC;
+      float scr[C::kOps][4];
+#pragma unroll
+      for (int op = 0; op < C::kOps; ++op)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int kc = lane + 32 * u;
+          scr[op][u] = kc < KC ? __ldg(sc + op * KC + kc) : 0.f;
+        }
+      // down: h exponents of the tokens of this lane's columns (lanes 0-15: column l of each block)
+      uint4 hx[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+      if constexpr (!kGU) {
+#pragma unroll
+        for (int bi = 0; bi < 2; ++bi) {
+          const int tok = (hf + 2 * bi) * 8 + (lane >> 1);
+          if (lane < 16 && tok < t.nvalid)
+            hx[bi] = __ldcg(reinterpret_cast<const uint4 *>(a.hexp + (size_t)(t.slot0 + tok) * kF8ExpStride));
+        }
+      }
       bool ok = true;
       for (int kc = 0; kc < KC; ++kc, ++ch) {
-        const int buf = ch & 1;
-        if (!__all_sync(0xffffffffu, f8_wait(&acc_full[buf], (ch >> 1) & 1, &abort_flag, a.status))) {
+        const int buf = ch % C::kAccBufs;
+        if (!__all_sync(0xffffffffu, f8_wait(&acc_full[buf], (ch / C::kAccBufs) & 1, &abort_flag, a.status))) {
           ok = false;
           break;
         }
         f8_fence_after();
         float s_op[C::kOps];
 #pragma unroll
-        for (int op = 0; op < C::kOps; ++op) s_op[op] = __ldg(sc + (kGU ? op * KC : 0) + kc);
+        for (int op = 0; op < C::kOps; ++op) {
+          float sv = scr[op][0];
 #pragma unroll
-        for (int bi = 0; bi < 4; ++bi) {
+          for (int u = 1; u < 4; ++u)
+            if ((kc >> 5) == u) sv = scr[op][u];
+          s_op[op] = __shfl_sync(0xffffffffu, sv, kc & 31);
+        }
+#pragma unroll
+        for (int bi = 0; bi < 2; ++bi) {
           const int b = hf + 2 * bi;
           if (b < nblk) {
-            // down: each column's power of 2 of the h terms of this K chunk
-            float colf = 1.f;
+            float v[C::kOps][16];
+#pragma unroll
+            for (int op = 0; op < C::kOps; ++op)
+              f8_ld16(tq + buf * C::kBufCols + op * (2 * kF8GroupMax) + b * 16, v[op]);
+            f8_wait_ld();
+            float colf = 1.f;   // down: this lane's column power of 2 of the h terms of chunk kc
             if constexpr (!kGU) {
-              const int tok = b * 8 + (lane >> 1);
-              if (lane < 16 && tok < t.nvalid)
-                colf = ldexpf(1.f, -(int)__ldcg(a.hexp + (size_t)(t.slot0 + tok) * (a.I / 128) + kc));
+              const uint32_t wd = kc < 4 ? hx[bi].x : kc < 8 ? hx[bi].y : kc < 12 ? hx[bi].z : hx[bi].w;
+              colf = ldexpf(1.f, -(int)(int8_t)((wd >> (8 * (kc & 3))) & 0xFFu));
             }
 #pragma unroll
-            for (int op = 0; op < C::kOps; ++op) {
-              float v[16];
-              f8_ld16(tq + buf * C::kBufCols + op * 128 + b * 16, v);
-              f8_wait_ld();
+            for (int op = 0; op < C::kOps; ++op)
 #pragma unroll
               for (int c = 0; c < 16; ++c) {
                 const float f = kGU ? s_op[op] : s_op[op] * __shfl_sync(0xffffffffu, colf, c);
-                acc[op][bi][c] = fmaf(v[c], f, acc[op][bi][c]);
+                acc[op][bi][c] = fmaf(v[op][c], f, acc[op][bi][c]);
               }
-            }
           }
         }
         f8_fence_before();
-        f8_arrive(&acc_empty[buf]);
+        __syncwarp();
+        if (lane == 0) f8_arrive(&acc_empty[buf]);
       }
       if (!ok) break;
       // ---- finish the unit ----
       if constexpr (kGU) {
-        // h per (row m, token), the reference's bf16 roundings
-        float hv[4][8];
+        // h per (row m, token), the reference's bf16 roundings; lane l < nvalid
+        // holds token l's power of 2 of the x terms
+        const int my_sx = lane < t.nvalid ? __ldcg(a.sexp + t.slot0 + lane) : 0;
+        float hv[2][8];
 #pragma unroll
-        for (int bi = 0; bi < 4; ++bi) {
+        for (int bi = 0; bi < 2; ++bi) {
           const int b = hf + 2 * bi;
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
             const int tok = b * 8 + p;
+            const int sx = __shfl_sync(0xffffffffu, my_sx, tok & 31);
             float h = 0.f;
             if (b < nblk && tok < t.nvalid) {
-              const float f = ldexpf(1.f, -__ldcg(a.sexp + t.slot0 + tok));
+              const float f = ldexpf(1.f, -sx);
               const float g = Act<__nv_bfloat16>::round((acc[0][bi][2 * p] + acc[0][bi][2 * p + 1] * 0.0625f) * f);
               const float u = Act<__nv_bfloat16>::round((acc[1][bi][2 * p] + acc[1][bi][2 * p + 1] * 0.0625f) * f);
               const float sg = Act<__nv_bfloat16>::round(g / (1.0f + expf(-g)));
@@ -421,13 +461,12 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
             float mx = fabsf(h);
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            if (lane == 0 && b < nblk && tok < kF8GroupMax) red[q][tok] = mx;
+            if (lane == 0 && b < nblk) red[q][tok] = mx;
           }
         }
         if (!__all_sync(0xffffffffu, epi_sync())) break;
-        const int nI = a.I / 128;
 #pragma unroll
-        for (int bi = 0; bi < 4; ++bi) {
+        for (int bi = 0; bi < 2; ++bi) {
           const int b = hf + 2 * bi;
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
@@ -443,21 +482,24 @@ __global__ void __launch_bounds__(kF8Threads, 1) k7_gemm(const __grid_constant__
               uint8_t *dst = a.hq + ((size_t)(t.mt * 8 + (m >> 4)) * a.R + (size_t)slot * 2) * 16 + (m & 15);
               dst[0] = (uint8_t)hi;
               dst[16] = (uint8_t)lo;
-              if (m == 0) a.hexp_out[(size_t)slot * nI + t.mt] = (int8_t)e;
+              if (m == 0) a.hexp_out[(size_t)slot * kF8ExpStride + t.mt] = (int8_t)e;
             }
           }
         }
         if (!__all_sync(0xffffffffu, epi_sync())) break;  // red[] is reused by the next unit
       } else {
 #pragma unroll
-        for (int bi = 0; bi < 4; ++bi) {
+        for (int bi = 0; bi < 2; ++bi) {
           const int b = hf + 2 * bi;
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
             const int tok = b * 8 + p;
             if (b < nblk && tok < t.nvalid) {
-              const float y = acc[0][bi][2 * p] + acc[0][bi][2 * p + 1] * 0.0625f;
-              a.y[(size_t)(t.slot0 + tok) * a.H + t.mt * 128 + m] = __float2bfloat16_rn(y);
+#pragma unroll
+              for (int op = 0; op < C::kOps; ++op) {
+                const float y = acc[op][bi][2 * p] + acc[op][bi][2 * p + 1] * 0.0625f;
+                a.y[(size_t)(t.slot0 + tok) * a.H + t.mt * 256 + op * 128 + m] = __float2bfloat16_rn(y);
+              }
             }
           }
         }
@@ -608,25 +650,27 @@ static int f8_num_sms() {
 // Per-slot expert outputs (bf16, slot order) of the plan in `ws`, left in the
 // ypart region as [Rt][H]; Rt = P (+ T with a shared expert).  Workspace use:
 // ypart = y [Rt][H] bf16, then the token terms [H/16][2 Rt][16 B]; h region =
-// h terms [I/16][2 Rt][16 B], then their exponents [Rt][I/128]; logits region
+// h terms [I/16][2 Rt][16 B], then their exponents [Rt][16]; logits region
 // = per-slot token exponents [Rt]; sh_w = shared gate scores [T].
 int f8_expert_outputs(const void *x, int64_t T, int H, int I, int E, int k, const uint8_t *w13, const float *s13,
                       const uint8_t *w2, const float *s2, const uint8_t *sh_w13, const float *sh_s13,
                       const uint8_t *sh_w2, const float *sh_s2, const void *sh_gate_w, void *ws, const WsLayout &L,
                       cudaStream_t s) {
-  TM_REQUIRE(H % 128 == 0 && I % 128 == 0 && H >= 128 && I >= 128, "hidden %d / inter %d: multiples of 128", H, I);
+  TM_REQUIRE(H % 256 == 0 && I % 128 == 0 && H >= 256 && I >= 128, "hidden %d (multiple of 256) / inter %d "
+             "(multiple of 128) unsupported", H, I);
   TM_REQUIRE(E <= kF8MaxExperts, "n_experts %d > %d", E, kF8MaxExperts);
   const bool shared = sh_w13 != nullptr;
   const int64_t P = T * k, Rt = P + (shared ? T : 0), R = 2 * Rt;
   TM_REQUIRE(Rt < (1 << 30) && R * (int64_t)(H / 16) < ((int64_t)1 << 40), "call too large");
   // the regions (sized for K4's fp32 buffers) hold these
-  TM_REQUIRE(Rt * H * 2 + R * H <= L.total - L.ypart && R * I + Rt * (I / 128) <= L.ypart - L.h &&
+  TM_REQUIRE(I <= 128 * kF8ExpStride, "inter %d > %d", I, 128 * kF8ExpStride);
+  TM_REQUIRE(Rt * H * 2 + R * H <= L.total - L.ypart && R * I + Rt * kF8ExpStride <= L.ypart - L.h &&
                  Rt * 4 <= L.counts - L.logits,
              "workspace regions too small for the FP8 grouped GEMMs");
   __nv_bfloat16 *y = ws_ptr<__nv_bfloat16>(ws, L.ypart);
   uint8_t *xq = reinterpret_cast<uint8_t *>(y) + (size_t)Rt * H * 2;
   uint8_t *hq = ws_ptr<uint8_t>(ws, L.h);
-  int8_t *hexp = reinterpret_cast<int8_t *>(hq + (size_t)R * I);
+  int8_t *hexp = reinterpret_cast<int8_t *>(hq + (size_t)R * I);   // [Rt][16]
   int *sexp = ws_ptr<int>(ws, L.logits);
   float *sh_w = ws_ptr<float>(ws, L.sh_w);
   k7_prep<<<(unsigned)((Rt + 7) / 8), 256, 0, s>>>((const __nv_bfloat16 *)x, ws_ptr<int>(ws, L.slot_token),
@@ -683,8 +727,8 @@ extern "C" int tm_moe_grouped_f8(const void *x, int64_t tokens, int hidden, int 
     TM_REQUIRE(aligned(sh_w13, 16) && aligned(sh_w2, 16) && aligned(sh_gate_w, 16),
                "shared weights must be 16-byte aligned");
   }
-  TM_REQUIRE(hidden % 128 == 0 && hidden >= 128 && inter % 128 == 0 && inter >= 128,
-             "hidden (%d) and inter (%d) must be multiples of 128", hidden, inter);
+  TM_REQUIRE(hidden % 256 == 0 && hidden >= 256 && inter % 128 == 0 && inter >= 128,
+             "hidden (%d) must be a multiple of 256 and inter (%d) of 128", hidden, inter);
   TM_REQUIRE(top_k >= 1 && top_k <= 64, "top_k %d outside [1, 64]", top_k);
   TM_REQUIRE(aligned(x, 16) && aligned(w13, 16) && aligned(w2, 16) && aligned(out, 16) &&
                  (!residual || aligned(residual, 16)),
