@@ -43,3 +43,15 @@ def assert_close(out, ref, maxabs, cos, what=""):
     m, c = O.compare(out.cpu(), ref.cpu())
     assert m <= maxabs and c >= cos, f"{what}: max-abs {m:.3e} (<= {maxabs}), cos {c:.7f} (>= {cos})"
     return m, c
+
+
+def fp32_cos(T, dtype):
+    """Cosine bar against the fp32 evaluation of the reference's algorithm.
+    0.99999 where the kernels round only the outputs; 0.99995 for bf16 calls
+    of the FP8 grouped GEMMs (turbomoe.ops.F8_MAX_TOKENS), which also round g,
+    u, silu(g) and h to bf16 where the reference's bf16 F.linear / F.silu / *
+    round them (four roundings of up to 2^-9 relative each)."""
+    from turbomoe import ops
+    if dtype == torch.bfloat16 and ops.PREFILL_MIN_TOKENS <= T <= ops.F8_MAX_TOKENS:
+        return 0.99995
+    return 0.99999

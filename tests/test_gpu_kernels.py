@@ -10,13 +10,13 @@ import pytest
 import torch
 
 from golden_util import DTYPES, case_layer, case_x, fixture, meta
-from gpu_util import assert_close, oracle_fp32, packed_from_layer, run_moe, workspace_for
+from gpu_util import assert_close, fp32_cos, oracle_fp32, packed_from_layer, run_moe, workspace_for
 from oracle import moe_oracle as O
 
 pytestmark = pytest.mark.gpu
 
 REF_MAXABS, REF_COS = 2e-2, 0.9995        # north-star bar vs the reference outputs
-FP32_COS = 0.99999                       # vs the fp32 oracle (output rounding only)
+FP32_COS = 0.99999                       # vs the fp32 oracle (output rounding only; see fp32_cos)
 
 
 def _bits(t):
@@ -160,7 +160,7 @@ def test_layer_vs_reference_golden(name, T):
     if T <= 64:
         ref32 = oracle_fp32(lw, x, idx, w)
         tol = {torch.float32: 1e-4, torch.float16: 2e-3, torch.bfloat16: 1e-2}[x.dtype]
-        assert_close(y, ref32, tol, FP32_COS, f"{name} T={T} vs fp32 oracle")
+        assert_close(y, ref32, tol, fp32_cos(T, x.dtype), f"{name} T={T} vs fp32 oracle")
 
 
 @pytest.mark.parametrize("T", [1, 2, 3, 4, 7, 8, 9, 16, 63, 64, 65, 200])
@@ -174,7 +174,7 @@ def test_token_counts_and_ragged_groups(T):
     layer = O.OracleLayer(lw, torch.bfloat16)
     idx, w = O.compute_routing(x, layer.router, shape.top_k)
     y = run_moe(lw, shape, x, idx, w)
-    assert_close(y, oracle_fp32(lw, x, idx, w), 1e-2, FP32_COS, f"T={T}")
+    assert_close(y, oracle_fp32(lw, x, idx, w), 1e-2, fp32_cos(T, torch.bfloat16), f"T={T}")
 
 
 def test_shared_expert_and_residual():

@@ -19,7 +19,8 @@
 //                                    epoch in the owner's arrival flag
 //   owner    ep_owner_plan           bounded wait for every source's flag, then
 //                                    the routing plan of the received rows
-//            K4 gate/up + down       tcgen05 grouped GEMMs over the received rows
+//            gate/up + down          tcgen05 grouped GEMMs over the received rows
+//                                    (FP8 K7 for bf16, K4 for fp16)
 //            ep_return               each output row back into its source's
 //                                    return region at its source slot; then the
 //                                    return flags
@@ -655,8 +656,12 @@ extern "C" int tm_ep_experts(tm_ep_ctx *c, const uint8_t *w13, const float *s13,
   if (rc) return rc;
   ep_owner_plan<<<1, 1024, smem, s>>>(ep_dev(c), pp);
   TM_LAUNCH_CHECK("ep_owner_plan launch");
-  rc = prefill_expert_outputs(c->base + c->L.rows, rows, c->hidden, c->inter, c->e_loc, 1, c->act, w13, s13, w2,
-                              s2, owner_ws, L, s);
+  // bf16: the FP8 tensor-core GEMMs (owners see ~16 rows per expert); fp16: the dequantising ones
+  rc = c->act == TM_DTYPE_BF16
+           ? f8_expert_outputs(c->base + c->L.rows, rows, c->hidden, c->inter, c->e_loc, 1, w13, s13, w2, s2, nullptr,
+                               nullptr, nullptr, nullptr, nullptr, owner_ws, L, s)
+           : prefill_expert_outputs(c->base + c->L.rows, rows, c->hidden, c->inter, c->e_loc, 1, c->act, w13, s13, w2,
+                                    s2, owner_ws, L, s);
   if (rc) return rc;
   EpReturnLaunch f{c, &L, owner_ws, s};
   return dispatch_act(c->act, f);

@@ -304,12 +304,18 @@ def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out:
                                            _stream(out)), "tm_moe_decode_down_combine")
 
 
-# Calls with at least this many tokens (and no shared expert, 16-bit
-# activations) run on the tensor-core grouped GEMMs (tm_moe_prefill_grouped).
+# Calls with at least this many tokens (16-bit activations, a shared expert
+# only of the routed experts' inter size) run on tensor-core grouped GEMMs.
 # Measured on B200, Qwen3-30B-A3B layer (128 experts, top-8): the decode
 # kernels win at 4 tokens (55 vs 92 us), tie at 8, and the grouped GEMMs win
 # from 16 tokens (167 vs 181 us) to 2048 (298 us vs 9.7 ms).
 PREFILL_MIN_TOKENS = 16
+# bf16 calls of up to this many tokens use the FP8 grouped GEMMs (K7,
+# tm_moe_grouped_f8), larger ones and fp16 the dequantising ones (K4,
+# tm_moe_prefill_grouped).  Measured on B200, Qwen3-30B-A3B layer: K7 / K4
+# 111 / 170 us at 16 tokens, 149 / 233 at 64, 166 / 235 at 256, 228 / 237 at
+# 512, 373 / 247 at 1024; Qwen3.5 64-token layer 177 / 281 us.
+F8_MAX_TOKENS = 512
 
 
 def prefill_eligible(T: int, dtype, packed: PackedExperts, shared, top_k: int = 8) -> bool:
@@ -384,8 +390,8 @@ def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: Pac
     if out is None:
         out = torch.empty_like(x)
     if prefill_eligible(T, x.dtype, packed, shared, k):
-        moe_prefill(x, w, packed, ws, out, residual.contiguous() if residual is not None else None, shared,
-                    shared_gate_w)
+        fn = moe_grouped_f8 if (x.dtype == torch.bfloat16 and T <= F8_MAX_TOKENS) else moe_prefill
+        fn(x, w, packed, ws, out, residual.contiguous() if residual is not None else None, shared, shared_gate_w)
         return out
     moe_gateup(x, k, packed, ws, shared, shared_gate_w, prefetch_down=True)
     moe_down_combine(w, packed, ws, out, shared, residual.contiguous() if residual is not None else None)
