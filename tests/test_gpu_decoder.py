@@ -145,6 +145,36 @@ def test_attn_decode_matches_sdpa(dt, n, splits):
             _ulp_close(got, want.to(dt), dt)
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("nh,nkv,n,splits", [(16, 4, 300, 16), (24, 2, 777, 5), (32, 2, 129, 16), (8, 8, 2048, 12),
+                                             (32, 4, 4096, 64)])
+def test_attn_decode_group_sizes(dt, nh, nkv, n, splits):
+    """Query-head groups of 4, 12, 16 and 1 heads (one and two 8-column MMA
+    blocks, unused columns), requests above the 16-CTA cluster, 16-bit
+    activations: within one act-dtype rounding of fp32 attention."""
+    from turbomoe import ops
+    hd, max_len = 128, 4100
+    g = torch.Generator(device="cuda").manual_seed(nh * 31 + n)
+    q = torch.randn(nh, hd, generator=g, device="cuda").to(dt)
+    kc = torch.randn(nkv, max_len, hd, generator=g, device="cuda").to(dt)
+    vc = torch.randn(nkv, max_len, hd, generator=g, device="cuda").to(dt)
+    kc[:, n:] = float("nan")
+    vc[:, n:] = float("nan")
+    scale = 1.0 / math.sqrt(hd)
+    qf = q.float().view(1, nh, 1, hd)
+    kf = kc[:, :n].float().repeat_interleave(nh // nkv, 0).unsqueeze(0)
+    vf = vc[:, :n].float().repeat_interleave(nh // nkv, 0).unsqueeze(0)
+    want = F.scaled_dot_product_attention(qf, kf, vf, scale=scale)[0, :, 0]
+    ws = torch.zeros(_lib().tm_attn_decode_workspace_bytes(nh, nkv, splits), dtype=torch.uint8, device="cuda")
+    out = torch.full((nh * hd,), float("nan"), dtype=dt, device="cuda")
+    pos = torch.tensor([n - 1], device="cuda")
+    rc = _lib().tm_attn_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), pos.data_ptr(), max_len, nh, nkv, hd,
+                               ops._code(dt), scale, splits, out.data_ptr(), ws.data_ptr(), ws.numel(), _s())
+    assert rc == 0
+    torch.cuda.synchronize()
+    _ulp_close(out.view(nh, hd).float(), want.to(dt), dt)
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 def test_lm_head_argmax(dt):
     from turbomoe import ops

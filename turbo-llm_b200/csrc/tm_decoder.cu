@@ -23,6 +23,9 @@
 // rounded to the act dtype).
 #include "tm_common.cuh"
 
+#include <algorithm>
+#include <mutex>
+
 namespace tmoe {
 
 constexpr int kHeadDim = 128;
@@ -364,6 +367,400 @@ __global__ void __launch_bounds__(kHeadMaxAttnWarps * 32) k8_attn_decode(
   Vec4<TA>::store(out + (int64_t)h * kHeadDim + 4 * lane, res);
 }
 
+// ------------------------------------- decode attention on tensor cores ----
+// 16-bit activations: the same split-K decode attention on mma.sync
+// m16n8k16, the splits of one KV head in one thread-block cluster.  Grid
+// (S, nkv), cluster (S, 1, 1), S <= 16: CTA (split s, KV head g) has 4 warps;
+// warp w takes the 32-position tiles w, w + 4, ... of the split, each tile of
+// K and V copied by the warp itself (cp.async, rows padded to 272 B:
+// conflict-free ldmatrix; rows past the context zero-filled) into its own
+// double buffer.  The products are transposed so that the group's G query
+// heads are the MMA's N = 8 columns (NT = ceil(G / 8) column blocks) and the
+// positions / head dims its M = 16 rows: S^T = K Q^T (A = K rows by ldmatrix,
+// B = Q from registers), scaled, masked, online softmax per head (fp32, a
+// column of S^T: shuffles across the 8 row lanes), then O^T += V^T P^T (A =
+// V by ldmatrix.trans, B = P^T: the C fragment of S^T stored to shared
+// memory as [position][head] and read back by ldmatrix.trans).  P is given
+// as two 16-bit terms hi + lo so that the product carries P to about 2^-17
+// relative like the fp32 reference (one 16-bit rounding of P alone moves
+// outputs by more than an act-dtype ulp at short contexts).  Per 32 positions
+// a warp issues 16 NT + 32 NT MMAs.  The warps' (m, l, O) merge through
+// shared memory into the CTA's partial; after a cluster barrier each CTA
+// reads every split's (m, l) and a slice of every split's O from distributed
+// shared memory and writes that slice of
+// out = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M).  No global
+// workspace, fence or atomic: the merge costs one shared::cluster round trip
+// instead of a device-scope release and a pass over L2.
+constexpr int kAttnMmaWarps = 4;
+constexpr int kAttnMaxCluster = 16;
+constexpr int kAttnRow = kHeadDim * 2 + 16;            // padded shared-memory row (bytes)
+constexpr int kAttnTileBytes = kAttnTile * kAttnRow;   // one K or V tile
+constexpr int kAttnWarpBytes = 2 * 2 * kAttnTileBytes; // double buffer of K and V
+// shared memory: the warps' tiles; each warp's P^T hi and lo [32][16 NT B];
+// each warp's O [warp][16][kAttnObRow] fp32 (row stride 132 floats: the
+// scalar stores of a warp, heads 2t and dims g, hit 32 distinct banks); the
+// CTA's O [16][128] fp32
+constexpr int kAttnObRow = kHeadDim + 4;
+constexpr int kAttnPOff = kAttnMmaWarps * kAttnWarpBytes;
+constexpr int kAttnPWarpBytes = 2 * kAttnTile * 32;     // hi + lo, NT <= 2
+constexpr int kAttnObufOff = kAttnPOff + kAttnMmaWarps * kAttnPWarpBytes;
+constexpr int kAttnCtaOOff = kAttnObufOff + kAttnMmaWarps * 16 * kAttnObRow * 4;
+constexpr int kAttnMmaSmem = kAttnCtaOOff + 16 * kHeadDim * 4;
+static_assert(kAttnMmaSmem <= 227 * 1024, "k8_attn_mma shared memory");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+template <typename TA> struct MmaOp;
+template <> struct MmaOp<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  // (a, b) as two 16-bit terms: hi = round(x), lo = round(x - hi)
+  static __device__ __forceinline__ void split(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+  }
+};
+template <> struct MmaOp<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  static __device__ __forceinline__ void split(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+  }
+};
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// 16-byte cp.async of `src_bytes` (16 or 0: zero fill)
+__device__ __forceinline__ void cp_async16_z(uint32_t dst, const void *src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+template <typename TA, int NT>
+__global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, const TA *k_cache, const TA *v_cache,
+                                                                  const int64_t *position, int64_t max_len, int nh,
+                                                                  int nkv, float scale, TA *out) {
+  extern __shared__ __align__(128) uint8_t am_smem[];
+  __shared__ float s_m[kAttnMmaWarps][16], s_l[kAttnMmaWarps][16];
+  __shared__ float c_m[16], c_l[16];   // this CTA's partial (read by the cluster)
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int G = nh / nkv;
+  const int s = (int)cluster_rank(), S = gridDim.x, gk = blockIdx.y;
+  uint8_t *wbuf = am_smem + w * kAttnWarpBytes;
+  const uint32_t p_hi = smem_u32(am_smem + kAttnPOff + w * kAttnPWarpBytes), p_lo = p_hi + kAttnTile * 16 * NT;
+  float *obuf = reinterpret_cast<float *>(am_smem + kAttnObufOff);
+  float *c_o = reinterpret_cast<float *>(am_smem + kAttnCtaOOff);
+  pdl_wait();
+  // context length; a position past the cache (refused by tm_qk_rope_kv) is clamped
+  const int64_t n = min((int64_t)__ldcg(reinterpret_cast<const long long *>(position)) + 1, max_len);
+  const int64_t per = ((n + S - 1) / S + kAttnTile - 1) / kAttnTile * kAttnTile;
+  const int64_t p_begin = (int64_t)s * per;
+  const int64_t p_end = min(n, p_begin + per);
+  const int ntiles = p_begin < p_end ? (int)((p_end - p_begin + kAttnTile - 1) / kAttnTile) : 0;
+  const TA *kbase = k_cache + (int64_t)gk * max_len * kHeadDim;
+  const TA *vbase = v_cache + (int64_t)gk * max_len * kHeadDim;
+  // this warp's tiles: w, w + 4, ...; 32 rows x 16 pieces of 16 B of K and of V
+  auto issue = [&](int ti, int buf) {
+    const int64_t p0 = p_begin + (int64_t)ti * kAttnTile;
+    const int cnt = (int)min((int64_t)kAttnTile, p_end - p0);
+    const uint32_t kd = smem_u32(wbuf + buf * 2 * kAttnTileBytes), vd = kd + kAttnTileBytes;
+#pragma unroll 4
+    for (int i = lane; i < kAttnTile * 16; i += 32) {
+      const int r = i >> 4, c = i & 15;
+      const bool in = r < cnt;
+      const int64_t off = (p0 + (in ? r : 0)) * kHeadDim + c * 8;
+      cp_async16_z(kd + r * kAttnRow + c * 16, kbase + off, in ? 16 : 0);
+      cp_async16_z(vd + r * kAttnRow + c * 16, vbase + off, in ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  if (w < ntiles) issue(w, 0);
+  // Q^T B fragments: column g8 of block nt = query head gk * G + 8 nt + g8 (zero past G);
+  // k-step kk: dims 16 kk + 2 t4 (+1) and + 8
+  uint32_t qb[NT][8][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int hh = nt * 8 + g8;
+    const TA *qh = q + (int64_t)(gk * G + hh) * kHeadDim;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      qb[nt][kk][0] = hh < G ? __ldcg(reinterpret_cast<const unsigned *>(qh + kk * 16 + 2 * t4)) : 0u;
+      qb[nt][kk][1] = hh < G ? __ldcg(reinterpret_cast<const unsigned *>(qh + kk * 16 + 8 + 2 * t4)) : 0u;
+    }
+  }
+  pdl_trigger();
+  // O^T accumulators: block md = dims 16 md.., column block nt; element j:
+  // dim 16 md + g8 (+8 for j >= 2), head 8 nt + 2 t4 + (j & 1)
+  float o[8][NT][4];
+#pragma unroll
+  for (int md = 0; md < 8; ++md)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[md][nt][0] = o[md][nt][1] = o[md][nt][2] = o[md][nt][3] = 0.f;
+  float m_r[NT][2], l_r[NT][2];   // heads 8 nt + 2 t4 + e
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) m_r[nt][0] = m_r[nt][1] = -INFINITY, l_r[nt][0] = l_r[nt][1] = 0.f;
+  int buf = 0;
+  for (int ti = w; ti < ntiles; ti += kAttnMmaWarps, buf ^= 1) {
+    if (ti + kAttnMmaWarps < ntiles) {
+      issue(ti + kAttnMmaWarps, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    const int cnt = (int)min((int64_t)kAttnTile, p_end - (p_begin + (int64_t)ti * kAttnTile));
+    const uint32_t kd = smem_u32(wbuf + buf * 2 * kAttnTileBytes), vd = kd + kAttnTileBytes;
+    // S^T = K Q^T: row blocks mt (positions 16 mt..) x column blocks nt, 8 steps of 16 dims
+    float sc[2][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t a[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)  // matrices: rows +0/+8 x dims +0/+8
+        ldsm_x4(kd + (mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kAttnRow + (kk * 16 + (lane >> 4) * 8) * 2,
+                a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) MmaOp<TA>::run(sc[mt][nt], a[mt], qb[nt][kk][0], qb[nt][kk][1]);
+    }
+    // scale, mask (position 16 mt + g8 + 8 (j >> 1) < cnt), running max per head
+    float mx[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      mx[nt][0] = mx[nt][1] = -INFINITY;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int pos = mt * 16 + g8 + (j >> 1) * 8;
+          sc[mt][nt][j] = pos < cnt ? sc[mt][nt][j] * scale : -INFINITY;
+          mx[nt][j & 1] = fmaxf(mx[nt][j & 1], sc[mt][nt][j]);
+        }
+    }
+    float corr[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = mx[nt][e];
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+        const float mn = fmaxf(m_r[nt][e], v);
+        corr[nt][e] = expf(m_r[nt][e] - mn);   // 0 on the first tile (m_r = -inf)
+        m_r[nt][e] = mn;
+      }
+    float rs[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      rs[nt][0] = rs[nt][1] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float v = sc[mt][nt][j];
+          const float p = v == -INFINITY ? 0.f : expf(v - m_r[nt][j & 1]);
+          sc[mt][nt][j] = p;
+          rs[nt][j & 1] += p;
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = rs[nt][e];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        l_r[nt][e] = l_r[nt][e] * corr[nt][e] + v;
+      }
+#pragma unroll
+    for (int md = 0; md < 8; ++md)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[md][nt][j] *= corr[nt][j & 1];
+    // P^T to shared memory, [position][head] as hi and lo 16-bit pairs
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t hi, lo;
+          MmaOp<TA>::split(sc[mt][nt][2 * hf], sc[mt][nt][2 * hf + 1], hi, lo);
+          const uint32_t off = (mt * 16 + g8 + 8 * hf) * (16 * NT) + nt * 16 + t4 * 4;
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(p_hi + off), "r"(hi) : "memory");
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(p_lo + off), "r"(lo) : "memory");
+        }
+    __syncwarp();
+    // B fragments of P^T: matrices = positions 0-7, 8-15, 16-23, 24-31 of column block nt
+    uint32_t bh[NT][4], bl[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint32_t off = (lane & 31) * (16 * NT) + nt * 16;
+      ldsm_x4_t(p_hi + off, bh[nt][0], bh[nt][1], bh[nt][2], bh[nt][3]);
+      ldsm_x4_t(p_lo + off, bl[nt][0], bl[nt][1], bl[nt][2], bl[nt][3]);
+    }
+    // O^T += V^T P^T: 2 steps of 16 positions x 8 row blocks of 16 dims
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      uint32_t a[8][4];
+      const int row = ks * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+#pragma unroll
+      for (int md = 0; md < 8; ++md)  // transposed: dims +0/+8 x positions +0/+8
+        ldsm_x4_t(vd + row * kAttnRow + (md * 16 + ((lane >> 3) & 1) * 8) * 2, a[md][0], a[md][1], a[md][2],
+                  a[md][3]);
+#pragma unroll
+      for (int md = 0; md < 8; ++md)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) MmaOp<TA>::run(o[md][nt], a[md], bh[nt][2 * ks], bh[nt][2 * ks + 1]);
+#pragma unroll
+      for (int md = 0; md < 8; ++md)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) MmaOp<TA>::run(o[md][nt], a[md], bl[nt][2 * ks], bl[nt][2 * ks + 1]);
+    }
+    __syncwarp();  // the next issue() and P^T stores overwrite what this tile read
+  }
+  cp_async_wait<0>();
+  // ---- the CTA's partial: the warps' (m, l) and raw O, merged per head
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+    if (g8 == 0) {
+      s_m[w][nt * 8 + 2 * t4] = m_r[nt][0];
+      s_m[w][nt * 8 + 2 * t4 + 1] = m_r[nt][1];
+      s_l[w][nt * 8 + 2 * t4] = l_r[nt][0];
+      s_l[w][nt * 8 + 2 * t4 + 1] = l_r[nt][1];
+    }
+  {
+    float *ob = obuf + w * 16 * kAttnObRow;
+#pragma unroll
+    for (int md = 0; md < 8; ++md)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int hh = nt * 8 + 2 * t4 + (j & 1);
+          if (hh < G) ob[hh * kAttnObRow + md * 16 + g8 + (j >> 1) * 8] = o[md][nt][j];
+        }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * kHeadDim / 4; i += kAttnMmaWarps * 32) {
+    const int r = i / (kHeadDim / 4), c = 4 * (i % (kHeadDim / 4));
+    float M = -INFINITY;
+#pragma unroll
+    for (int ww = 0; ww < kAttnMmaWarps; ++ww)
+      if (s_l[ww][r] > 0.f) M = fmaxf(M, s_m[ww][r]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kAttnMmaWarps; ++ww) {
+      const float f = s_l[ww][r] > 0.f ? expf(s_m[ww][r] - M) : 0.f;
+      L += f * s_l[ww][r];
+      const float4 v = *reinterpret_cast<const float4 *>(obuf + (ww * 16 + r) * kAttnObRow + c);
+      acc.x = fmaf(v.x, f, acc.x);
+      acc.y = fmaf(v.y, f, acc.y);
+      acc.z = fmaf(v.z, f, acc.z);
+      acc.w = fmaf(v.w, f, acc.w);
+    }
+    *reinterpret_cast<float4 *>(c_o + r * kHeadDim + c) = acc;
+    if (c == 0) {
+      c_m[r] = M;
+      c_l[r] = L;
+    }
+  }
+  cluster_sync_all();  // every split's partial is complete
+  // ---- merge the splits through distributed shared memory: 4 lanes per
+  // 4-dim output group (splits sub, sub + 4, ...); this CTA's groups are
+  // s, s + S, ...  Every lane loads all it needs before using any of it.
+  const int sub = lane & 3;
+  for (int q0 = 0; q0 * S < G * kHeadDim / 4; q0 += kAttnMmaWarps * 8) {
+    const int gi = s + S * (q0 + (tid >> 2));
+    const bool valid = gi < G * kHeadDim / 4;
+    const int r = valid ? gi / (kHeadDim / 4) : 0, c = valid ? 4 * (gi % (kHeadDim / 4)) : 0;
+    float mj[kAttnMaxCluster / 4], lj[kAttnMaxCluster / 4];
+    float4 oj[kAttnMaxCluster / 4];
+#pragma unroll
+    for (int u = 0; u < kAttnMaxCluster / 4; ++u) {
+      const int j = sub + 4 * u;
+      const bool in = valid && j < S;
+      lj[u] = in ? ld_cluster_f32(cluster_addr(&c_l[r], j)) : 0.f;
+      mj[u] = in ? ld_cluster_f32(cluster_addr(&c_m[r], j)) : -INFINITY;
+      oj[u] = in ? ld_cluster_f32x4(cluster_addr(c_o + r * kHeadDim + c, j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kAttnMaxCluster / 4; ++u)
+      if (lj[u] > 0.f) M = fmaxf(M, mj[u]);
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+    float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < kAttnMaxCluster / 4; ++u) {
+      const float f = lj[u] > 0.f ? expf(mj[u] - M) : 0.f;
+      L = fmaf(f, lj[u], L);
+      acc[0] = fmaf(oj[u].x, f, acc[0]);
+      acc[1] = fmaf(oj[u].y, f, acc[1]);
+      acc[2] = fmaf(oj[u].z, f, acc[2]);
+      acc[3] = fmaf(oj[u].w, f, acc[3]);
+    }
+#pragma unroll
+    for (int x = 1; x <= 2; x <<= 1) {
+      L += __shfl_xor_sync(0xffffffffu, L, x);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], x);
+    }
+    if (valid && sub == 0) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      float res[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) res[e] = acc[e] * inv;
+      Vec4<TA>::store(out + (int64_t)(gk * G) * kHeadDim + 4 * gi, res);
+    }
+  }
+  cluster_sync_all();  // the other CTAs have read this CTA's partial
+}
+
 // ------------------------------------------------- LM head + greedy argmax ----
 // logits[r] = x . W[r] (W bf16 [vocab][hidden] as in the checkpoint, fp32
 // accumulation, rounded to the act dtype for 16-bit activations), then the
@@ -501,10 +898,79 @@ struct RopeLaunch {
                       (TA *)k_cache, (TA *)v_cache, status);
   }
 };
+// Cluster size for k8_attn_mma: the requested splits (<= 16), halved until
+// a cluster of that many CTAs (one SM each: the tiles take 136 KiB of shared
+// memory) can be resident.  Sizes above 8 need the non-portable opt-in.
+template <typename TA, int NT> int attn_mma_cluster(int *S) {
+  static std::mutex mu;
+  static int fits[kAttnMaxCluster + 1] = {};   // 0 unknown, 1 fits, -1 does not
+  std::lock_guard<std::mutex> g(mu);
+  int rc = ensure_smem(reinterpret_cast<const void *>(k8_attn_mma<TA, NT>), kAttnMmaSmem);
+  if (rc) return rc;
+  static bool opted = false;
+  if (!opted) {
+    rc = cuda_check(cudaFuncSetAttribute(k8_attn_mma<TA, NT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                    "cudaFuncSetAttribute(non-portable cluster)");
+    if (rc) return rc;
+    opted = true;
+  }
+  while (*S > 1) {
+    if (fits[*S] == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(*S, 1);
+      cfg.blockDim = dim3(kAttnMmaWarps * 32);
+      cfg.dynamicSmemBytes = kAttnMmaSmem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = *S;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, k8_attn_mma<TA, NT>, &cfg);
+      if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+      }
+      fits[*S] = n > 0 ? 1 : -1;
+    }
+    if (fits[*S] > 0) break;
+    *S = *S / 2;
+  }
+  return TM_OK;
+}
+
 struct AttnLaunch {
   const void *q, *kc, *vc; const int64_t *pos; int64_t max_len; int nh, nkv, splits; float scale; void *out;
   float *part; unsigned *counters; cudaStream_t s;
+  template <typename TA, int NT> int run_mma() {
+    int S = std::min(splits, kAttnMaxCluster);
+    int rc = attn_mma_cluster<TA, NT>(&S);
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, nkv);
+    cfg.blockDim = dim3(kAttnMmaWarps * 32);
+    cfg.dynamicSmemBytes = kAttnMmaSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cuda_check(cudaLaunchKernelEx(&cfg, k8_attn_mma<TA, NT>, (const TA *)q, (const TA *)kc, (const TA *)vc, pos,
+                                         max_len, nh, nkv, scale, (TA *)out),
+                      "k8_attn_mma launch");
+  }
   template <typename TA> int run() {
+    if constexpr (sizeof(TA) == 2) {
+      if (nh / nkv <= 8) return run_mma<TA, 1>();
+      if (nh / nkv <= 16) return run_mma<TA, 2>();
+    }
     const size_t smem = (size_t)4 * kAttnTile * kHeadDim * sizeof(TA);
     return launch_pdl(k8_attn_decode<TA>, dim3(nkv, splits), dim3(32 * (nh / nkv)), smem, s,
                       "k8_attn_decode launch", (const TA *)q, (const TA *)kc, (const TA *)vc, pos, max_len, nh,
