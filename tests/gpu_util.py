@@ -45,13 +45,14 @@ def assert_close(out, ref, maxabs, cos, what=""):
     return m, c
 
 
-def fp32_cos(T, dtype):
+def fp32_cos(T, dtype, n_experts=128, top_k=8):
     """Cosine bar against the fp32 evaluation of the reference's algorithm.
     0.99999 where the kernels round only the outputs; 0.99995 for bf16 calls
-    of the FP8 grouped GEMMs (turbomoe.ops.F8_MAX_TOKENS), which also round g,
-    u, silu(g) and h to bf16 where the reference's bf16 F.linear / F.silu / *
-    round them (four roundings of up to 2^-9 relative each)."""
+    that run on the FP8 grouped GEMMs (turbomoe.ops.f8_eligible), which also
+    round g, u, silu(g) and h to bf16 where the reference's bf16 F.linear /
+    F.silu / * round them (four roundings of up to 2^-9 relative each)."""
     from turbomoe import ops
-    if dtype == torch.bfloat16 and ops.PREFILL_MIN_TOKENS <= T <= ops.F8_MAX_TOKENS:
+    if (dtype == torch.bfloat16 and T >= ops.PREFILL_MIN_TOKENS
+            and T * top_k <= ops.F8_MAX_ROWS_PER_EXPERT * n_experts):
         return 0.99995
     return 0.99999

@@ -160,7 +160,7 @@ def test_layer_vs_reference_golden(name, T):
     if T <= 64:
         ref32 = oracle_fp32(lw, x, idx, w)
         tol = {torch.float32: 1e-4, torch.float16: 2e-3, torch.bfloat16: 1e-2}[x.dtype]
-        assert_close(y, ref32, tol, fp32_cos(T, x.dtype), f"{name} T={T} vs fp32 oracle")
+        assert_close(y, ref32, tol, fp32_cos(T, x.dtype, shape.experts, shape.top_k), f"{name} T={T} vs fp32 oracle")
 
 
 @pytest.mark.parametrize("T", [1, 2, 3, 4, 7, 8, 9, 16, 63, 64, 65, 200])
@@ -174,7 +174,8 @@ def test_token_counts_and_ragged_groups(T):
     layer = O.OracleLayer(lw, torch.bfloat16)
     idx, w = O.compute_routing(x, layer.router, shape.top_k)
     y = run_moe(lw, shape, x, idx, w)
-    assert_close(y, oracle_fp32(lw, x, idx, w), 1e-2, fp32_cos(T, torch.bfloat16), f"T={T}")
+    assert_close(y, oracle_fp32(lw, x, idx, w), 1e-2, fp32_cos(T, torch.bfloat16, shape.experts, shape.top_k),
+                 f"T={T}")
 
 
 def test_shared_expert_and_residual():

@@ -31,6 +31,8 @@ constexpr int kK3Warps = 4;                // K3 general: 4 warps x 2 half-warps
 constexpr int kK3Threads = kK3Warps * 32;
 constexpr int kK3T1Warps = 8;              // K3 one token: one warp per routed expert
 constexpr int kK3T1Threads = kK3T1Warps * 32;
+constexpr int kK3F8Warps = 16;             // one-token FP8 K3: two warps per expert (K halves)
+constexpr int kK3F8Threads = kK3F8Warps * 32;
 constexpr int kK3T1MaxExperts = 16;        // routed + shared experts the one-token path holds
 constexpr int kK3T1MaxKB = 32;             // 128-column scale blocks per expert row it holds (K <= 4096)
 constexpr int kCombineInKernelMaxT = 64;
@@ -476,25 +478,29 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_mma(GateUpArgs<TA> a) {
 // none of its conversions; fp32 accumulation, block scale per 128 columns.
 // Shared memory: tile, the three e4m3 rows of x (the raw row lands over mid and
 // lo first), block scales.
-template <typename TA>
-__global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
+template <typename TA, int kW, int kSt>
+__global__ void __launch_bounds__(kW * 32) k2_gateup_f8(GateUpArgs<TA> a) {
   static_assert(sizeof(TA) == 2, "16-bit activations");
   extern __shared__ __align__(128) uint8_t k2_smem[];
   const int tile_bytes = 32 * a.H;
-  const int quarter = tile_bytes / kK2Warps;
+  const int part = tile_bytes / kW;  // the slice of the tile each warp waits for
   uint8_t *wtile = k2_smem;
-  uint8_t *xb = k2_smem + tile_bytes;                          // [3][H] e4m3: hi, mid, lo
-  const TA *xraw = reinterpret_cast<const TA *>(xb + a.H);     // [H] act (before the split)
-  float *ssc = reinterpret_cast<float *>(xb + 3 * a.H);        // [2][H/128]
-  __shared__ float red[kK2Warps][2][kRows];
-  __shared__ float xmax[kK2Warps], s_gl[kK2Warps];
+  // the three e4m3 term rows of x are XS = H + 16 bytes apart: the MMA B
+  // loads of lanes reading the hi, mid and lo rows (same column) hit
+  // different banks
+  const int XS = a.H + 16;
+  uint8_t *xb = k2_smem + tile_bytes;                          // [3][XS] e4m3: hi, mid, lo
+  const TA *xraw = reinterpret_cast<const TA *>(xb + XS);      // [H] act (before the split)
+  float *ssc = reinterpret_cast<float *>(xb + 3 * XS);         // [2][H/128]
+  __shared__ float red[kW][2][kRows];
+  __shared__ float xmax[kW], s_gl[kW];
   __shared__ int s_shift;
-  __shared__ __align__(8) uint64_t bar[kK2Warps];
+  __shared__ __align__(8) uint64_t bar[kW];
   __shared__ __align__(8) uint64_t xbar;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrEnter);
   if (tid == 0) {
-    for (int q = 0; q < kK2Warps; ++q) mbar_init(&bar[q], 1);
+    for (int q = 0; q < kW; ++q) mbar_init(&bar[q], 1);
     mbar_init(&xbar, 1);
     mbar_fence_init();
   }
@@ -529,9 +535,9 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
   if (tid == 0) {
     const uint8_t *src = wbase + (int64_t)rg * tile_bytes;
     const uint64_t pol = l2_evict_first();
-    for (int q = 0; q < kK2Warps; ++q) {
-      mbar_arrive_expect_tx(&bar[q], quarter);
-      tma_bulk_g2s_hint(wtile + q * quarter, src + q * quarter, quarter, &bar[q], pol);
+    for (int q = 0; q < kW; ++q) {
+      mbar_arrive_expect_tx(&bar[q], part);
+      tma_bulk_g2s_hint(wtile + q * part, src + q * part, part, &bar[q], pol);
     }
     const uint32_t rowb = (uint32_t)a.H * sizeof(TA);
     mbar_arrive_expect_tx(&xbar, rowb);
@@ -540,18 +546,18 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
   pdl_trigger();
   const int HB = a.H / 128, KC = a.H / 16;
   const int ib = (rg * kRows) / 128;
-  for (int i = tid; i < 2 * HB; i += kK2Threads) ssc[i] = __ldg(sbase + ib * 2 * HB + i);
+  for (int i = tid; i < 2 * HB; i += (kW * 32)) ssc[i] = __ldg(sbase + ib * 2 * HB + i);
   const bool gate_logit = shared_expert && rg == 0;
   if (!tile_ready(&xbar, a.pl.status, 0)) {
     if (tid == 0)
-      for (int q = 0; q < kK2Warps; ++q) mbar_wait_bounded(&bar[q], 0);
+      for (int q = 0; q < kW; ++q) mbar_wait_bounded(&bar[q], 0);
     return;
   }
   // max |x| -> power-of-2 scale; optional shared-gate logit (fp32), same order
   // as k2_gateup_mma
   {
     float m = 0.f, gl = 0.f;
-    const int c_lo = w * (a.H / kK2Warps), c_hi = c_lo + a.H / kK2Warps;
+    const int c_lo = w * (a.H / kW), c_hi = c_lo + a.H / kW;
     for (int c = c_lo + lane; c < c_hi; c += 32) {
       const float v = Act<TA>::to_f(xraw[c]);
       m = fmaxf(m, fabsf(v));
@@ -569,7 +575,7 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
   if (tid == 0) {
     float m = 0.f, gl = 0.f;
 #pragma unroll
-    for (int ww = 0; ww < kK2Warps; ++ww) {
+    for (int ww = 0; ww < kW; ++ww) {
       m = fmaxf(m, xmax[ww]);
       gl += s_gl[ww];
     }
@@ -583,13 +589,13 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
   __syncthreads();
   {  // split: every thread first reads its elements (the raw row overlaps mid/lo)
     constexpr int kMaxSteps = 8;  // H <= 4096 (host checks)
-    const int steps = a.H / (4 * kK2Threads);
+    const int steps = a.H / (4 * (kW * 32));
     const float sc = ldexpf(1.0f, s_shift);
     float v[kMaxSteps][4];
 #pragma unroll
     for (int k = 0; k < kMaxSteps; ++k)
       if (k < steps) {
-        const int c = 4 * (tid + k * kK2Threads);
+        const int c = 4 * (tid + k * (kW * 32));
 #pragma unroll
         for (int u = 0; u < 4; ++u) v[k][u] = Act<TA>::to_f(xraw[c + u]) * sc;
       }
@@ -597,36 +603,45 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
 #pragma unroll
     for (int k = 0; k < kMaxSteps; ++k)
       if (k < steps) {
-        const int c = 4 * (tid + k * kK2Threads);
+        const int c = 4 * (tid + k * (kW * 32));
         uint32_t h, md, l;
         e4m3_split3(v[k], h, md, l);
         *reinterpret_cast<uint32_t *>(xb + c) = h;
-        *reinterpret_cast<uint32_t *>(xb + a.H + c) = md;
-        *reinterpret_cast<uint32_t *>(xb + 2 * a.H + c) = l;
+        *reinterpret_cast<uint32_t *>(xb + XS + c) = md;
+        *reinterpret_cast<uint32_t *>(xb + 2 * XS + c) = l;
       }
   }
   __syncthreads();
-  // this warp's quarter of the weight tile
-  if (!tile_ready(&bar[w], a.pl.status, 0)) {
-    if (tid == 0)
-      for (int q = 0; q < kK2Warps; ++q) mbar_wait_bounded(&bar[q], 0);
-    return;
+  const int cpw = KC / kW;  // 16-column chunks per warp
+  const int kc0 = w * cpw;
+  const int g = lane >> 2, t = lane & 3;
+  // B column n = g: 0 hi, 1 mid, 2 lo (columns 3-7 repeat lo and are not read)
+  const uint8_t *xsel = xb + min(g, 2) * XS + kc0 * 16 + 4 * t;
+  // kSt > 0: the warp's kSt B fragment pairs in registers, loaded while the
+  // weights are still in flight (the MMA loop then reads only the tile)
+  uint32_t bx[kSt > 0 ? kSt : 1][2];
+#pragma unroll
+  for (int st = 0; st < kSt; ++st) {
+    bx[st][0] = *reinterpret_cast<const uint32_t *>(xsel + st * 32);
+    bx[st][1] = *reinterpret_cast<const uint32_t *>(xsel + st * 32 + 16);
   }
-  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrData);
-  if (tid == 0) {  // this CTA's tile is in: HBM can carry K3's weights now
+  // this warp's part of the weight tile: each warp starts its MMAs as soon as
+  // its own part has landed (the parts arrive over microseconds); the CTA
+  // agrees on a timeout at the reduction barrier below
+  const bool part_ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar[w], 0));
+  TM_TRACE_EVENT(a.pl.trace, kTrGateUp, kTrData);  // warp 0's part landed
+  if (tid == 0 && part_ok) {  // HBM can carry K3's weights now
     if (shared_expert) k2_prefetch_down(a.pf_sh_w2, (int64_t)a.H * a.Is, 0, rg, a.H);
     else k2_prefetch_down(a.pf_w2, (int64_t)a.H * a.I, eid, rg, a.H);
   }
-  const int cpw = KC / kK2Warps;  // 16-column chunks per warp
-  const int kc0 = w * cpw;
-  const int g = lane >> 2, t = lane & 3;
   // A (ldmatrix.x4): lanes 0-15 rows 0-15 of chunk kc, lanes 16-31 of chunk kc+1
   const uint32_t wsm = smem_u32(wtile) + (kc0 + (lane >> 4)) * 512 + (lane & 15) * 16;
-  // B column n = g: 0 hi, 1 mid, 2 lo (columns 3-7 repeat lo and are not read)
-  const uint8_t *xsel = xb + min(g, 2) * a.H + kc0 * 16 + 4 * t;
   float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-  for (int blk = 0; blk < cpw / 8; ++blk) {
+  // (kSt > 0: cpw / 8 == kSt / 4, a compile-time trip count keeps bx in registers)
+  const int nblk = part_ok ? (kSt > 0 ? kSt / 4 : cpw / 8) : 0;
+#pragma unroll(kSt > 0 ? kSt / 4 : 2)
+  for (int blk = 0; blk < (kSt > 0 ? kSt / 4 : cpw / 8); ++blk) {
+    if (blk >= nblk) break;
     float dg[2][4], du[2][4];  // four independent MMA chains (two per operand)
 #pragma unroll
     for (int c = 0; c < 2; ++c)
@@ -638,8 +653,14 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
       uint32_t g0, g1, g2, g3, u0, u1, u2, u3;
       ldsm_x4(wsm + kc * 512, g0, g1, g2, g3);
       ldsm_x4(wsm + kc * 512 + 256, u0, u1, u2, u3);
-      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xsel + kc * 16);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xsel + kc * 16 + 16);
+      uint32_t b0, b1;
+      if constexpr (kSt > 0) {
+        b0 = bx[blk * 4 + st][0];
+        b1 = bx[blk * 4 + st][1];
+      } else {
+        b0 = *reinterpret_cast<const uint32_t *>(xsel + kc * 16);
+        b1 = *reinterpret_cast<const uint32_t *>(xsel + kc * 16 + 16);
+      }
       mma_16832_e4m3(dg[st & 1], g0, g1, g2, g3, b0, b1);
       mma_16832_e4m3(du[st & 1], u0, u1, u2, u3, b0, b1);
     }
@@ -661,11 +682,17 @@ __global__ void __launch_bounds__(kK2Threads) k2_gateup_f8(GateUpArgs<TA> a) {
     red[w][1][g] = accu[0] + (accu[1] + lu0 * 0.0625f) * 0.0625f;
     red[w][1][g + 8] = accu[2] + (accu[3] + lu8 * 0.0625f) * 0.0625f;
   }
-  __syncthreads();
+  if (__syncthreads_or(!part_ok)) {  // a part never landed: flag, let the copies finish, no output
+    if (tid == 0) {
+      atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
+      for (int q = 0; q < kW; ++q) mbar_wait_bounded(&bar[q], 0);
+    }
+    return;
+  }
   if (tid < kRows) {
     float gs = 0.f, us = 0.f;
 #pragma unroll
-    for (int ww = 0; ww < kK2Warps; ++ww) {
+    for (int ww = 0; ww < kW; ++ww) {
       gs += red[ww][0][tid];
       us += red[ww][1][tid];
     }
@@ -1136,10 +1163,10 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_mma(DownArgs<TA> a) {
 // column, and the packed e4m3 down tile is multiplied as it is by
 // mma.sync m16n8k32: half the MMAs, no weight conversion.
 template <typename TA>
-__global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
+__global__ void __launch_bounds__(kK3F8Threads) k3_down_t1_f8(DownArgs<TA> a) {
   static_assert(sizeof(TA) == 2, "16-bit activations");
   extern __shared__ __align__(128) uint8_t k3_smem[];
-  __shared__ float ysm[kK3T1MaxExperts][kRows];
+  __shared__ float ysm[kK3T1MaxExperts][2][kRows];   // per expert and K half
   __shared__ float s_sc[kK3T1MaxExperts][kK3T1MaxKB];  // block scales of this CTA's 16 rows
   __shared__ float s_back[kK3T1MaxExperts];            // 2^-shift that undoes h's scaling
   __shared__ int4 s_rec[kK3T1MaxExperts];
@@ -1166,7 +1193,10 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
   __syncthreads();
   const int tile_r = kRows * a.I, tile_s = kRows * a.Is;
   const int Kmax = max(a.I, a.Is);
-  // [routed tiles][shared tile][h fp32: k slots x I, then Is][h e4m3: 3 x Kmax per expert]
+  // term rows of h, 16 bytes apart in bank order: the MMA B loads of lanes
+  // reading the hi, mid and lo rows (same column) hit different banks
+  const int KS = Kmax + 16;
+  // [routed tiles][shared tile][h fp32: k slots x I, then Is][h e4m3: 3 x KS per expert]
   float *hs = reinterpret_cast<float *>(k3_smem + (size_t)n_active * tile_r + tile_s);
   uint8_t *h8 = reinterpret_cast<uint8_t *>(hs + (size_t)a.k * a.I + a.Is);
   if (tid < n_active)
@@ -1185,7 +1215,7 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
   // one dependent global load per 128 columns inside the MMA loop
   {
     const int KB = a.I / 128, KBs = a.Is / 128, rb = (rgo * kRows) / 128;
-    for (int i = tid; i < n_exp * kK3T1MaxKB; i += kK3T1Threads) {
+    for (int i = tid; i < n_exp * kK3T1MaxKB; i += kK3F8Threads) {
       const int e = i / kK3T1MaxKB, b = i % kK3T1MaxKB;
       if (e == n_active) {
         if (b < KBs) s_sc[e][b] = __ldg(a.sh_s2 + (int64_t)rb * KBs + b);
@@ -1218,11 +1248,11 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
     return;
   }
   const int g = lane >> 2, t = lane & 3;
-  for (int e = w; e < n_exp; e += kK3T1Warps) {
+  for (int e = w; e < n_exp; e += kK3F8Warps) {
     const bool sh = e == n_active;
     const int K = sh ? a.Is : a.I;
     const float *hf = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
-    uint8_t *he = h8 + (size_t)e * 3 * Kmax;
+    uint8_t *he = h8 + (size_t)e * 3 * KS;
     // this expert's h -> three e4m3 terms with a power-of-2 scale (warp-local);
     // K % 128 == 0, so each lane's loads come in groups of 4 (issued together)
     float m4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1244,8 +1274,8 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
       uint32_t th, tm, tl;
       e4m3_split3(v, th, tm, tl);
       *reinterpret_cast<uint32_t *>(he + c) = th;
-      *reinterpret_cast<uint32_t *>(he + Kmax + c) = tm;
-      *reinterpret_cast<uint32_t *>(he + 2 * Kmax + c) = tl;
+      *reinterpret_cast<uint32_t *>(he + KS + c) = tm;
+      *reinterpret_cast<uint32_t *>(he + 2 * KS + c) = tl;
     }
     __syncwarp();
   }
@@ -1258,18 +1288,23 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
     return;
   }
   TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrData);
-  for (int e = w; e < n_exp; e += kK3T1Warps) {
+  // work items (expert, K half): warp w takes items w, w + 16, ...; item i is
+  // expert i / 2, half i % 2 (128-column blocks [0, nb/2) and [nb/2, nb))
+  for (int item = w; item < 2 * n_exp; item += kK3F8Warps) {
+    const int e = item >> 1, half = item & 1;
     const bool sh = e == n_active;
     const int K = sh ? a.Is : a.I;
-    const float back = s_back[e];  // written by this warp in the conversion pass
+    const int nb = K / 128, nb0 = (nb + 1) / 2;
+    const int blk_lo = half ? nb0 : 0, blk_hi = half ? nb : nb0;
+    const float back = s_back[e];  // written in the conversion pass (a CTA barrier ago)
     // A (ldmatrix.x4): lanes 0-15 rows 0-15 of chunk kc, lanes 16-31 of chunk kc+1
     const uint32_t wsm = smem_u32(k3_smem + (size_t)e * tile_r) + (lane >> 4) * 256 + (lane & 15) * 16;
     // B column n = g: 0 hi, 1 mid, 2 lo (columns 3-7 repeat lo and are not read)
-    const uint8_t *hsel = h8 + (size_t)e * 3 * Kmax + min(g, 2) * Kmax + 4 * t;
+    const uint8_t *hsel = h8 + (size_t)e * 3 * KS + min(g, 2) * KS + 4 * t;
     const float *srow = s_sc[e];
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
-    for (int blk = 0; blk < K / 128; ++blk) {
+    for (int blk = blk_lo; blk < blk_hi; ++blk) {
       float d[4][4];  // four independent MMA chains, one 32-column step each
 #pragma unroll
       for (int c = 0; c < 4; ++c)
@@ -1292,8 +1327,8 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
     // g + 8 (acc[2], acc[3]); lane (g, t=1) holds lo in acc[0], acc[2]
     const float lo0 = __shfl_down_sync(0xffffffffu, acc[0], 1), lo8 = __shfl_down_sync(0xffffffffu, acc[2], 1);
     if (t == 0) {
-      ysm[e][g] = (acc[0] + (acc[1] + lo0 * 0.0625f) * 0.0625f) * back;
-      ysm[e][g + 8] = (acc[2] + (acc[3] + lo8 * 0.0625f) * 0.0625f) * back;
+      ysm[e][half][g] = (acc[0] + (acc[1] + lo0 * 0.0625f) * 0.0625f) * back;
+      ysm[e][half][g + 8] = (acc[2] + (acc[3] + lo8 * 0.0625f) * 0.0625f) * back;
     }
   }
   TM_TRACE_EVENT(a.pl.trace, kTrDownT1, 4);  // warp 0's MMAs done
@@ -1301,8 +1336,11 @@ __global__ void __launch_bounds__(kK3T1Threads) k3_down_t1_f8(DownArgs<TA> a) {
   if (tid < kRows) {
     float y = 0.f;
     for (int kk = 0; kk < a.k; ++kk)
-      if (s_slot[kk] >= 0) y = fmaf(s_w[kk], ysm[s_map[s_slot[kk]]][tid], y);
-    if (a.has_shared) y = fmaf(shw, ysm[n_active][tid], y);
+      if (s_slot[kk] >= 0) {
+        const int e = s_map[s_slot[kk]];
+        y = fmaf(s_w[kk], ysm[e][0][tid] + ysm[e][1][tid], y);
+      }
+    if (a.has_shared) y = fmaf(shw, ysm[n_active][0][tid] + ysm[n_active][1][tid], y);
     const int nn = rgo * kRows + tid;
     if (a.residual) y += res_pre;
     a.out[nn] = Act<TA>::from_f(y);
@@ -1333,8 +1371,18 @@ struct GateUpLaunch {
   template <typename TA, int kNT> int go(GateUpArgs<TA> &a, int grid) {
     if constexpr (sizeof(TA) == 2) {
       if (kNT == 1 && T == 1 && H <= 4096) {  // one token: FP8 MMAs on the split activation
-        const size_t smem = (size_t)32 * H + (size_t)3 * H + 2 * (H / 128) * sizeof(float);
-        return launch_pdl(k2_gateup_f8<TA>, dim3(grid), dim3(kK2Threads), smem, s, "k2_gateup launch", a);
+        // 8 warps (H % 1024 == 0) split the reduction dimension finer: the
+        // MMA chains of one warp are latency-bound, not the tensor pipe
+        // (H = 1024 / 2048 / 3072 / 4096: the B fragments in registers)
+        const size_t smem = (size_t)32 * H + (size_t)3 * (H + 16) + 2 * (H / 128) * sizeof(float);
+        switch (H) {
+          case 1024: return launch_pdl(k2_gateup_f8<TA, 8, 4>, dim3(grid), dim3(256), smem, s, "k2_gateup launch", a);
+          case 2048: return launch_pdl(k2_gateup_f8<TA, 8, 8>, dim3(grid), dim3(256), smem, s, "k2_gateup launch", a);
+          case 3072: return launch_pdl(k2_gateup_f8<TA, 8, 12>, dim3(grid), dim3(256), smem, s, "k2_gateup launch", a);
+          case 4096: return launch_pdl(k2_gateup_f8<TA, 8, 16>, dim3(grid), dim3(256), smem, s, "k2_gateup launch", a);
+          default: break;
+        }
+        return launch_pdl(k2_gateup_f8<TA, 4, 0>, dim3(grid), dim3(4 * 32), smem, s, "k2_gateup launch", a);
       }
       // tile + x rows (f16, padded; >= the 4 KB reduction area) + block scales
       const size_t smem = (size_t)32 * H + std::max<size_t>((size_t)kNT * (H + 8) * 2, 4096) +
@@ -1407,9 +1455,9 @@ struct DownLaunch {
         std::max(I, a.Is) <= 128 * kK3T1MaxKB) {
       size_t smem = (size_t)max_active * kRows * I + (size_t)kRows * a.Is + ((size_t)k * I + a.Is) * sizeof(float);
       if constexpr (sizeof(TA) == 2) {
-        const size_t smem8 = smem + (size_t)(max_active + a.has_shared) * 3 * std::max(I, a.Is);
+        const size_t smem8 = smem + (size_t)(max_active + a.has_shared) * 3 * (std::max(I, a.Is) + 16);
         if (smem8 <= 200 * 1024)
-          return launch_pdl(k3_down_t1_f8<TA>, dim3(a.RGo), dim3(kK3T1Threads), smem8, s,
+          return launch_pdl(k3_down_t1_f8<TA>, dim3(a.RGo), dim3(kK3F8Threads), smem8, s,
                             "k3_down_t1 launch", a);
         smem += (size_t)(max_active + a.has_shared) * (std::max(I, a.Is) + 8) * 2;
         if (smem <= 200 * 1024)

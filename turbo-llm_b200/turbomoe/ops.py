@@ -310,12 +310,23 @@ def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out:
 # kernels win at 4 tokens (55 vs 92 us), tie at 8, and the grouped GEMMs win
 # from 16 tokens (167 vs 181 us) to 2048 (298 us vs 9.7 ms).
 PREFILL_MIN_TOKENS = 16
-# bf16 calls of up to this many tokens use the FP8 grouped GEMMs (K7,
-# tm_moe_grouped_f8), larger ones and fp16 the dequantising ones (K4,
-# tm_moe_prefill_grouped).  Measured on B200, Qwen3-30B-A3B layer: K7 / K4
-# 111 / 170 us at 16 tokens, 149 / 233 at 64, 166 / 235 at 256, 228 / 237 at
-# 512, 373 / 247 at 1024; Qwen3.5 64-token layer 177 / 281 us.
-F8_MAX_TOKENS = 512
+# bf16 calls with up to this many (token, expert) pairs per expert on average
+# (T * top_k / n_experts) use the FP8 grouped GEMMs (K7, tm_moe_grouped_f8);
+# busier experts and fp16 use the dequantising ones (K4,
+# tm_moe_prefill_grouped).  K7 multiplies groups of <= 32 tokens per weight
+# tile, so its cost grows with the rows per expert while K4's barely does.
+# Measured on B200 (K7 / K4, us): Qwen3-30B-A3B layer (128 experts, top-8)
+# 111 / 170 at 16 tokens, 149 / 233 at 64, 166 / 235 at 256, 228 / 237 at 512
+# (32 per expert), 373 / 247 at 1024 (64 per expert); 64 experts x 256 tokens
+# (32 per expert) 132 / 143; 16 experts x 256 tokens (128 per expert) 104 /
+# 70; Qwen3.5 64-token layer 177 / 281.
+F8_MAX_ROWS_PER_EXPERT = 32
+F8_MAX_TOKENS = 512   # the Qwen3-30B-A3B bound of the rule above (512 * 8 / 128)
+
+
+def f8_eligible(T: int, dtype, packed: PackedExperts, top_k: int) -> bool:
+    """Whether a grouped call (prefill_eligible) runs on K7 rather than K4."""
+    return dtype == torch.bfloat16 and T * top_k <= F8_MAX_ROWS_PER_EXPERT * packed.n_experts
 
 
 def prefill_eligible(T: int, dtype, packed: PackedExperts, shared, top_k: int = 8) -> bool:
@@ -390,7 +401,7 @@ def moe_experts(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, packed: Pac
     if out is None:
         out = torch.empty_like(x)
     if prefill_eligible(T, x.dtype, packed, shared, k):
-        fn = moe_grouped_f8 if (x.dtype == torch.bfloat16 and T <= F8_MAX_TOKENS) else moe_prefill
+        fn = moe_grouped_f8 if f8_eligible(T, x.dtype, packed, k) else moe_prefill
         fn(x, w, packed, ws, out, residual.contiguous() if residual is not None else None, shared, shared_gate_w)
         return out
     moe_gateup(x, k, packed, ws, shared, shared_gate_w, prefetch_down=True)
