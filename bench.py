@@ -743,11 +743,71 @@ def ep_measure(args, rank, world, local, loader, router):
     else:
         res["single_gpu_tokens_per_s"] = res["uniform"]["tokens_per_s"]
         res["strong_scaling_efficiency"] = 1.0
+    if args.ep_ctx > 0:
+        res["attention"] = ep_attention(args, rank, world, local)
     if "zipf" in routers:
         res["zipf"]["routing"] = (f"Zipf s={args.ep_zipf}: router column {H - 1} replaced by log p_e (p_e ~ rank^-s "
                                   f"over a seeded expert permutation) and token coordinate {H - 1} set to 1, so the "
                                   "experts also see that modified coordinate")
     return res
+
+
+def ep_attention(args, rank, world, local):
+    """Decode attention of the batched-decode step: this rank's
+    T = ep_tokens / N sequences (data-parallel: each GPU holds its own
+    sequences' caches) at ``args.ep_ctx`` tokens of bf16 KV context, one layer
+    of the Qwen3-30B-A3B attention (32 query / 4 KV heads, head_dim 128)
+    through tm_attn_decode_batched.  CUDA events over ``args.steps`` calls
+    (layers' caches alternating so that every call reads HBM), max over
+    ranks; HBM bytes = the K and V rows of every sequence's context."""
+    import math
+    from turbomoe import ops
+    from turbomoe._lib import lib
+    Lb = lib()
+    T, ctx = args.ep_tokens // world, args.ep_ctx
+    nh, nkv, hd = 32, 4, 128
+    dev = torch.device("cuda", local)
+    per = nkv * ctx * hd                                     # elements of one sequence's K (or V) cache
+    layer_bytes = 2 * T * per * 2
+    n_layers = max(1, min(4, -(-(1 << 30) // layer_bytes)))  # >= 1 GiB of caches in rotation
+    g = torch.Generator(device=dev).manual_seed(SEED + 7 + rank)
+    caches = [(torch.randn(T * per, generator=g, device=dev).to(torch.bfloat16),
+               torch.randn(T * per, generator=g, device=dev).to(torch.bfloat16)) for _ in range(n_layers)]
+    q = torch.randn(T, nh, hd, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty(T, nh * hd, dtype=torch.bfloat16, device=dev)
+    pos = torch.full((T,), ctx - 1, dtype=torch.int64, device=dev)
+    splits = max(1, min(16, -(-2 * 148 // (nkv * T))))
+    s = torch.cuda.current_stream(dev).cuda_stream
+    code = ops._code(torch.bfloat16)
+
+    def call(i):
+        kc, vc = caches[i % n_layers]
+        rc = Lb.tm_attn_decode_batched(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), pos.data_ptr(), T, per, ctx, nh,
+                                       nkv, hd, code, 1.0 / math.sqrt(hd), splits, out.data_ptr(), s)
+        if rc != 0:
+            raise RuntimeError(f"tm_attn_decode_batched: {Lb.tm_last_error().decode()}")
+
+    for i in range(args.warmup):
+        call(i)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        call(i)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    us = max_over_ranks(e0.elapsed_time(e1), world) / args.steps * 1000
+    gbs = T * per * 2 * 2 / (us * 1e-6) / 1e9
+    peak = _peaks()[0]
+    del caches
+    return {"kernel": "k8_attn_mma via tm_attn_decode_batched (mma.sync, splits of a KV head merged in a cluster)",
+            "sequences_per_rank": T, "context": ctx, "heads": f"{nh} q / {nkv} kv x {hd}", "splits": splits,
+            "us_per_layer": round(us, 1), "hbm_gbs": round(gbs, 1),
+            "frac": round(gbs / peak, 3) if peak else None,
+            "bytes_per_layer_per_rank": T * per * 2 * 2,
+            "timing": f"CUDA events over {args.steps} calls, {n_layers} layers' caches in rotation, max over ranks"}
 
 
 # ------------------------------------------------- expert-parallel decode ----
@@ -955,6 +1015,9 @@ def main():
                     help="decode: batch-1 decode (replicas for N>1); ep: expert-parallel batched decode")
     ap.add_argument("--ep-tokens", type=int, default=256,
                     help="expert-parallel batched decode: sequences over all ranks (0 = skip the ep object)")
+    ap.add_argument("--ep-ctx", type=int, default=4096,
+                    help="expert-parallel decode: also time the batched decode attention of each rank's sequences "
+                         "at this KV context (0 = skip)")
     ap.add_argument("--ep-zipf", type=float, default=1.2,
                     help="expert-parallel decode: also time Zipf-skewed routing with this exponent (0 = skip)")
     ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",

@@ -334,6 +334,20 @@ int64_t tm_attn_decode_workspace_bytes(int n_heads, int n_kv_heads, int splits);
 int tm_attn_decode(const void *q, const void *k_cache, const void *v_cache, const int64_t *position,
                    int64_t max_len, int n_heads, int n_kv_heads, int head_dim, int act_dtype, float scale,
                    int splits, void *out, void *ws, int64_t ws_bytes, void *stream);
+/* Batched decode (one query token per sequence, bf16/fp16): sequence b reads
+ * q + b * n_heads * 128 and writes out + b * n_heads * 128, its caches start
+ * at k_cache / v_cache + b * kv_batch_stride elements (each
+ * [n_kv_heads][max_len][128], as tm_qk_rope_kv writes them) and its context is
+ * positions[b] + 1 (ragged over the batch).  `splits` (<= 16 used) CTAs per
+ * (sequence, KV head) form one thread-block cluster and merge through
+ * distributed shared memory; no workspace.  The reference's KVCache
+ * (cache/kv_cache.py:28-54) appends [batch, kv_heads, new, 128] slices with
+ * one sequence length for the whole batch and attends through Hugging Face
+ * attention; here every sequence has its own length (the expert-parallel
+ * batched-decode configuration). */
+int tm_attn_decode_batched(const void *q, const void *k_cache, const void *v_cache, const int64_t *positions,
+                           int batch, int64_t kv_batch_stride, int64_t max_len, int n_heads, int n_kv_heads,
+                           int head_dim, int act_dtype, float scale, int splits, void *out, void *stream);
 /* LM head and greedy choice: logits = x . W^T (W bf16 [vocab][hidden], fp32
  * accumulation, rounded to act for 16-bit act), optional logits output (act
  * [vocab], NULL to skip), *token = index of the largest logit (lowest index

@@ -175,6 +175,64 @@ def test_attn_decode_group_sizes(dt, nh, nkv, n, splits):
     _ulp_close(out.view(nh, hd).float(), want.to(dt), dt)
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("nh,nkv,splits", [(32, 4, 1), (32, 4, 3), (16, 1, 16)])
+def test_attn_decode_batched_ragged(dt, nh, nkv, splits):
+    """tm_attn_decode_batched: five sequences with their own context lengths
+    (1 to the whole cache), caches one padded stride apart, positions past each
+    context poisoned; each sequence within one act-dtype rounding of fp32
+    attention, and bit-identical to the one-sequence entry point."""
+    from turbomoe import ops
+    B, hd, max_len = 5, 128, 700
+    lengths = [1, 33, 700, 257, 64]
+    stride = nkv * max_len * hd + 8 * hd          # elements between sequences (padded)
+    g = torch.Generator(device="cuda").manual_seed(nh + splits)
+    q = torch.randn(B, nh, hd, generator=g, device="cuda").to(dt)
+    kbuf = torch.randn(B * stride, generator=g, device="cuda").to(dt)
+    vbuf = torch.randn(B * stride, generator=g, device="cuda").to(dt)
+    kc = kbuf.view(B, stride)[:, : nkv * max_len * hd].view(B, nkv, max_len, hd)
+    vc = vbuf.view(B, stride)[:, : nkv * max_len * hd].view(B, nkv, max_len, hd)
+    for b, n in enumerate(lengths):
+        kc[b, :, n:] = float("nan")
+        vc[b, :, n:] = float("nan")
+    pos = torch.tensor([n - 1 for n in lengths], device="cuda")
+    out = torch.full((B, nh * hd), float("nan"), dtype=dt, device="cuda")
+    scale = 1.0 / math.sqrt(hd)
+    rc = _lib().tm_attn_decode_batched(q.data_ptr(), kbuf.data_ptr(), vbuf.data_ptr(), pos.data_ptr(), B, stride,
+                                       max_len, nh, nkv, hd, ops._code(dt), scale, splits, out.data_ptr(), _s())
+    assert rc == 0
+    torch.cuda.synchronize()
+    for b, n in enumerate(lengths):
+        qf = q[b].float().view(1, nh, 1, hd)
+        kf = kc[b, :, :n].float().repeat_interleave(nh // nkv, 0).unsqueeze(0)
+        vf = vc[b, :, :n].float().repeat_interleave(nh // nkv, 0).unsqueeze(0)
+        want = F.scaled_dot_product_attention(qf, kf, vf, scale=scale)[0, :, 0]
+        _ulp_close(out[b].view(nh, hd).float(), want.to(dt), dt)
+    # sequence 3 through the one-sequence entry point: the same kernel, the same bits
+    ws = torch.zeros(_lib().tm_attn_decode_workspace_bytes(nh, nkv, splits), dtype=torch.uint8, device="cuda")
+    one = torch.empty(nh * hd, dtype=dt, device="cuda")
+    kc3, vc3 = kc[3].contiguous(), vc[3].contiguous()
+    assert _lib().tm_attn_decode(q[3].contiguous().data_ptr(), kc3.data_ptr(), vc3.data_ptr(), pos[3:4].data_ptr(),
+                                 max_len, nh, nkv, hd, ops._code(dt), scale, splits, one.data_ptr(), ws.data_ptr(),
+                                 ws.numel(), _s()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(one, out[3])
+
+
+def test_attn_decode_batched_rejects():
+    """Host checks of the batched entry point (no launch): fp32, a stride
+    shorter than one sequence's caches, batch 0."""
+    from turbomoe import ops
+    t = torch.zeros(4096, dtype=torch.bfloat16, device="cuda")
+    pos = torch.zeros(2, dtype=torch.int64, device="cuda")
+    L = _lib()
+    args = lambda dt, B, stride: (t.data_ptr(), t.data_ptr(), t.data_ptr(), pos.data_ptr(), B, stride, 8, 8, 1, 128,
+                                  ops._code(dt), 0.1, 1, t.data_ptr(), _s())
+    assert L.tm_attn_decode_batched(*args(torch.float32, 2, 1024)) != 0
+    assert L.tm_attn_decode_batched(*args(torch.bfloat16, 2, 512)) != 0
+    assert L.tm_attn_decode_batched(*args(torch.bfloat16, 0, 1024)) != 0
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 def test_lm_head_argmax(dt):
     from turbomoe import ops

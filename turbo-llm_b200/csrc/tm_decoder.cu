@@ -395,17 +395,19 @@ constexpr int kAttnMmaWarps = 4;
 constexpr int kAttnMaxCluster = 16;
 constexpr int kAttnRow = kHeadDim * 2 + 16;            // padded shared-memory row (bytes)
 constexpr int kAttnTileBytes = kAttnTile * kAttnRow;   // one K or V tile
-constexpr int kAttnWarpBytes = 2 * 2 * kAttnTileBytes; // double buffer of K and V
-// shared memory: the warps' tiles; each warp's P^T hi and lo [32][16 NT B];
-// each warp's O [warp][16][kAttnObRow] fp32 (row stride 132 floats: the
-// scalar stores of a warp, heads 2t and dims g, hit 32 distinct banks); the
-// CTA's O [16][128] fp32
+constexpr int kAttnStages = 3;                                    // tiles in flight per warp
+constexpr int kAttnWarpBytes = kAttnStages * 2 * kAttnTileBytes;  // ring of K and V tiles
+// shared memory: the warps' tile rings; each warp's P^T hi and lo [32][16 NT
+// B].  After the loop the ring space holds each warp's O [warp][16][kAttnObRow]
+// fp32 (row stride 132 floats: the scalar stores of a warp, heads 2t and dims
+// g, hit 32 distinct banks) and the CTA's O [16][128] fp32.
 constexpr int kAttnObRow = kHeadDim + 4;
 constexpr int kAttnPOff = kAttnMmaWarps * kAttnWarpBytes;
 constexpr int kAttnPWarpBytes = 2 * kAttnTile * 32;     // hi + lo, NT <= 2
-constexpr int kAttnObufOff = kAttnPOff + kAttnMmaWarps * kAttnPWarpBytes;
+constexpr int kAttnObufOff = 0;
 constexpr int kAttnCtaOOff = kAttnObufOff + kAttnMmaWarps * 16 * kAttnObRow * 4;
-constexpr int kAttnMmaSmem = kAttnCtaOOff + 16 * kHeadDim * 4;
+constexpr int kAttnMmaSmem = kAttnPOff + kAttnMmaWarps * kAttnPWarpBytes;
+static_assert(kAttnCtaOOff + 16 * kHeadDim * 4 <= kAttnPOff, "merge buffers fit in the tile rings");
 static_assert(kAttnMmaSmem <= 227 * 1024, "k8_attn_mma shared memory");
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -470,10 +472,13 @@ __device__ __forceinline__ void cp_async16_z(uint32_t dst, const void *src, int 
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 
+// Sequence b = blockIdx.z of a batch: its query q + b * nh * 128, its caches
+// k_cache / v_cache + b * kv_bstride, its position position[b], its output
+// out + b * nh * 128 (one sequence: gridDim.z = 1).
 template <typename TA, int NT>
 __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, const TA *k_cache, const TA *v_cache,
                                                                   const int64_t *position, int64_t max_len, int nh,
-                                                                  int nkv, float scale, TA *out) {
+                                                                  int nkv, float scale, TA *out, int64_t kv_bstride) {
   extern __shared__ __align__(128) uint8_t am_smem[];
   __shared__ float s_m[kAttnMmaWarps][16], s_l[kAttnMmaWarps][16];
   __shared__ float c_m[16], c_l[16];   // this CTA's partial (read by the cluster)
@@ -485,16 +490,22 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
   const uint32_t p_hi = smem_u32(am_smem + kAttnPOff + w * kAttnPWarpBytes), p_lo = p_hi + kAttnTile * 16 * NT;
   float *obuf = reinterpret_cast<float *>(am_smem + kAttnObufOff);
   float *c_o = reinterpret_cast<float *>(am_smem + kAttnCtaOOff);
+  const int64_t bz = blockIdx.z;
+  q += bz * nh * kHeadDim;
+  out += bz * nh * kHeadDim;
   pdl_wait();
   // context length; a position past the cache (refused by tm_qk_rope_kv) is clamped
-  const int64_t n = min((int64_t)__ldcg(reinterpret_cast<const long long *>(position)) + 1, max_len);
+  const int64_t n = min((int64_t)__ldcg(reinterpret_cast<const long long *>(position) + bz) + 1, max_len);
   const int64_t per = ((n + S - 1) / S + kAttnTile - 1) / kAttnTile * kAttnTile;
   const int64_t p_begin = (int64_t)s * per;
   const int64_t p_end = min(n, p_begin + per);
   const int ntiles = p_begin < p_end ? (int)((p_end - p_begin + kAttnTile - 1) / kAttnTile) : 0;
-  const TA *kbase = k_cache + (int64_t)gk * max_len * kHeadDim;
-  const TA *vbase = v_cache + (int64_t)gk * max_len * kHeadDim;
+  const TA *kbase = k_cache + bz * kv_bstride + (int64_t)gk * max_len * kHeadDim;
+  const TA *vbase = v_cache + bz * kv_bstride + (int64_t)gk * max_len * kHeadDim;
   // this warp's tiles: w, w + 4, ...; 32 rows x 16 pieces of 16 B of K and of V
+  // (one cp.async group per tile slot, committed by the caller: empty groups
+  // keep the count uniform, so the wait below is always "all but the newest
+  // kAttnStages - 1")
   auto issue = [&](int ti, int buf) {
     const int64_t p0 = p_begin + (int64_t)ti * kAttnTile;
     const int cnt = (int)min((int64_t)kAttnTile, p_end - p0);
@@ -507,9 +518,12 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
       cp_async16_z(kd + r * kAttnRow + c * 16, kbase + off, in ? 16 : 0);
       cp_async16_z(vd + r * kAttnRow + c * 16, vbase + off, in ? 16 : 0);
     }
-    cp_async_commit();
   };
-  if (w < ntiles) issue(w, 0);
+#pragma unroll
+  for (int j = 0; j < kAttnStages - 1; ++j) {  // prologue: tiles w, w + 4, ...
+    if (w + j * kAttnMmaWarps < ntiles) issue(w + j * kAttnMmaWarps, j);
+    cp_async_commit();
+  }
   // Q^T B fragments: column g8 of block nt = query head gk * G + 8 nt + g8 (zero past G);
   // k-step kk: dims 16 kk + 2 t4 (+1) and + 8
   uint32_t qb[NT][8][2];
@@ -535,12 +549,12 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) m_r[nt][0] = m_r[nt][1] = -INFINITY, l_r[nt][0] = l_r[nt][1] = 0.f;
   int buf = 0;
-  for (int ti = w; ti < ntiles; ti += kAttnMmaWarps, buf ^= 1) {
-    if (ti + kAttnMmaWarps < ntiles) {
-      issue(ti + kAttnMmaWarps, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+  for (int ti = w; ti < ntiles; ti += kAttnMmaWarps, buf = buf == kAttnStages - 1 ? 0 : buf + 1) {
+    {
+      const int tn = ti + (kAttnStages - 1) * kAttnMmaWarps;
+      if (tn < ntiles) issue(tn, buf == 0 ? kAttnStages - 1 : buf - 1);  // the slot tile ti - 4 used
+      cp_async_commit();
+      cp_async_wait<kAttnStages - 1>();
     }
     __syncwarp();
     const int cnt = (int)min((int64_t)kAttnTile, p_end - (p_begin + (int64_t)ti * kAttnTile));
@@ -663,6 +677,7 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
     __syncwarp();  // the next issue() and P^T stores overwrite what this tile read
   }
   cp_async_wait<0>();
+  __syncthreads();  // every warp is done with its tile ring, which now holds the merge buffers
   // ---- the CTA's partial: the warps' (m, l) and raw O, merged per head
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -944,12 +959,13 @@ template <typename TA, int NT> int attn_mma_cluster(int *S) {
 struct AttnLaunch {
   const void *q, *kc, *vc; const int64_t *pos; int64_t max_len; int nh, nkv, splits; float scale; void *out;
   float *part; unsigned *counters; cudaStream_t s;
+  int batch = 1; int64_t kv_bstride = 0;
   template <typename TA, int NT> int run_mma() {
     int S = std::min(splits, kAttnMaxCluster);
     int rc = attn_mma_cluster<TA, NT>(&S);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(S, nkv);
+    cfg.gridDim = dim3(S, nkv, batch);
     cfg.blockDim = dim3(kAttnMmaWarps * 32);
     cfg.dynamicSmemBytes = kAttnMmaSmem;
     cfg.stream = s;
@@ -963,7 +979,7 @@ struct AttnLaunch {
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cuda_check(cudaLaunchKernelEx(&cfg, k8_attn_mma<TA, NT>, (const TA *)q, (const TA *)kc, (const TA *)vc, pos,
-                                         max_len, nh, nkv, scale, (TA *)out),
+                                         max_len, nh, nkv, scale, (TA *)out, kv_bstride),
                       "k8_attn_mma launch");
   }
   template <typename TA> int run() {
@@ -1052,6 +1068,40 @@ extern "C" int tm_attn_decode(const void *q, const void *k_cache, const void *v_
   AttnLaunch f{q, k_cache, v_cache, position, max_len, n_heads, n_kv_heads, splits, scale, out, part, counters,
                as_stream(stream)};
   return dispatch_act(act_dtype, f);
+}
+
+// A batch of sequences (batched decode): the same tensor-core kernel with the
+// sequence as the grid's third dimension; 16-bit activations only.
+struct AttnBatchLaunch {
+  AttnLaunch f;
+  template <typename TA> int run() {
+    if constexpr (sizeof(TA) == 2) {
+      if (f.nh / f.nkv <= 8) return f.run_mma<TA, 1>();
+      return f.run_mma<TA, 2>();
+    }
+    return fail(TM_ERR_UNSUPPORTED, "batched decode attention needs 16-bit activations");
+  }
+};
+
+extern "C" int tm_attn_decode_batched(const void *q, const void *k_cache, const void *v_cache,
+                                      const int64_t *positions, int batch, int64_t kv_batch_stride,
+                                      int64_t max_len, int n_heads, int n_kv_heads, int head_dim, int act_dtype,
+                                      float scale, int splits, void *out, void *stream) {
+  TM_REQUIRE(q && k_cache && v_cache && positions && out, "null pointer");
+  TM_REQUIRE(head_dim == kHeadDim, "head_dim %d unsupported (128)", head_dim);
+  TM_REQUIRE(act_dtype == TM_DTYPE_BF16 || act_dtype == TM_DTYPE_F16, "16-bit activations only");
+  TM_REQUIRE(n_kv_heads >= 1 && n_kv_heads <= 65535 && n_heads % n_kv_heads == 0 && n_heads / n_kv_heads <= 16,
+             "%d query heads over %d KV heads unsupported (at most 16 per KV head)", n_heads, n_kv_heads);
+  TM_REQUIRE(batch >= 1 && batch <= 65535, "batch %d out of range (1..65535)", batch);
+  TM_REQUIRE(splits >= 1 && max_len >= 1, "bad splits %d / max_len %lld", splits, (long long)max_len);
+  TM_REQUIRE(kv_batch_stride >= (int64_t)n_kv_heads * max_len * kHeadDim || batch == 1,
+             "kv_batch_stride %lld smaller than one sequence's cache", (long long)kv_batch_stride);
+  TM_REQUIRE(kv_batch_stride % 8 == 0, "kv_batch_stride must keep rows 16-byte aligned");
+  TM_REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(out, 16),
+             "buffers must be 16-byte aligned");
+  AttnBatchLaunch b{AttnLaunch{q, k_cache, v_cache, positions, max_len, n_heads, n_kv_heads, splits, scale, out,
+                               nullptr, nullptr, as_stream(stream), batch, kv_batch_stride}};
+  return dispatch_act(act_dtype, b);
 }
 
 extern "C" int64_t tm_lm_head_workspace_bytes(void) {
