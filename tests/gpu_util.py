@@ -56,3 +56,17 @@ def fp32_cos(T, dtype, n_experts=128, top_k=8):
             and T * top_k <= ops.F8_MAX_ROWS_PER_EXPERT * n_experts):
         return 0.99995
     return 0.99999
+
+
+def k7_layer(x, idx, w, packed, ws, residual=None):
+    """The routed layer on the FP8 grouped GEMMs (K7) whatever the rows per
+    expert: the kernels an expert-parallel owner runs (tm_ep_experts), so an
+    EP output can be compared with it bit for bit."""
+    from turbomoe import ops
+    ws.ensure(x.shape[0], idx.shape[1])
+    if not ops.plan_matches(ws, idx):
+        ops.route_plan(idx, packed.n_experts, ws)
+    out = torch.empty_like(x)
+    ops.moe_grouped_f8(x, w.to(x.dtype).contiguous(), packed, ws, out,
+                       residual.contiguous() if residual is not None else None)
+    return out

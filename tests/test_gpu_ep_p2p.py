@@ -14,7 +14,7 @@ import ctypes as C
 import pytest
 import torch
 
-from gpu_util import oracle_fp32
+from gpu_util import k7_layer, oracle_fp32
 from oracle import moe_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -45,9 +45,9 @@ def test_ep_p2p_single_rank_matches_layer():
                               device="cuda").to(x.dtype)
             out = ep.forward(x, residual=res)
             idx, w = ops.router_topk(x, router, K, ws)
-            ref = ops.moe_experts(x, idx, w, full, ws, residual=res)
             assert ep.status() == 0
-            if T >= ops.PREFILL_MIN_TOKENS:
+            if T >= ops.PREFILL_MIN_TOKENS:   # the owner's kernels (K7) on one GPU: the same bits
+                ref = k7_layer(x, idx, w, full, ws, residual=res)
                 assert torch.equal(out, ref), (T, (out.float() - ref.float()).abs().max().item())
             # against the fp32 oracle of the reference's layer, same routing
             want = oracle_fp32(lw, x, idx, w) + res.float().cpu()
