@@ -54,9 +54,9 @@ LAYER_BYTES = 8 * EXPERT_BYTES + 8 * 288 * 4 + 128 * 2048 * 2 + 2 * 2048 * 2  # 
 # dram__bytes_read.sum + dram__bytes_write.sum of one K2 launch of this
 # workload, read from an ncu capture (not measured by this script: ncu replays
 # kernels, so it cannot run inside a timed bench)
-K2_TRAFFIC = 37772800
-K2_TRAFFIC_SOURCE = ("ncu --set full capture of k2_gateup_f8 in this workload (4-layer decode step, "
-                     "dram__bytes_read.sum + dram__bytes_write.sum of one launch)")
+K2_TRAFFIC = 37789440
+K2_TRAFFIC_SOURCE = ("ncu --set full capture of k2_gateup_f8<bf16, 8, 8> in this workload (4-layer decode step, "
+                     "dram__bytes_read.sum + dram__bytes_write.sum of one launch: 37,789,440 + 0 B)")
 
 
 def _peaks():
