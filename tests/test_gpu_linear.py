@@ -67,3 +67,23 @@ def test_fp8_linear_attention_shapes(N, K):
     out = ops.fp8_linear(x.cuda(), pl).cpu()
     want32 = F.linear(x.float(), O.dequantize_weight(w, s, torch.float32))
     assert_close(out.float(), want32, _one_rounding(want32, torch.bfloat16), 0.99999, f"fp8_linear {N}x{K}")
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("N,K", [(5120, 2048), (128, 4096), (256, 6144)])
+def test_fp8_linear_one_token_fp8_path(dt, N, K):
+    """One-token calls with K % 2048 == 0 run on FP8 MMAs with the token split
+    into three e4m3 terms (k6_linear_t1_f8): within one act-dtype rounding of
+    the fp32 product, with and without the residual; the fused q/k/v shape
+    and K = 6144 (24 MMA steps per warp)."""
+    from turbomoe import ops, synth
+    w, s = _weight(N, K, 3 * N + K)
+    pl = ops.pack_linear(w.cuda(), s.cuda())
+    x = synth.make_hidden(1, K, N, dtype=dt)
+    res = torch.randn(1, N, generator=torch.Generator().manual_seed(N)).to(dt)
+    want32 = F.linear(x.float(), O.dequantize_weight(w, s, torch.float32))
+    out = ops.fp8_linear(x.cuda(), pl).cpu()
+    assert_close(out.float(), want32, _one_rounding(want32, dt), 0.99999, f"fp8_linear t1 {dt} {N}x{K}")
+    out_r = ops.fp8_linear(x.cuda(), pl, residual=res.cuda()).cpu()
+    want_r = want32 + res.float()
+    assert_close(out_r.float(), want_r, _one_rounding(want_r, dt), 0.99999, f"fp8_linear t1 + residual {dt}")

@@ -19,7 +19,8 @@
 // into f16 (exact for bf16/fp16 values) and multiplied on mma.sync m16n8k16
 // (e4m3 -> f16 exact, fp32 accumulation, block scale per 128 columns); the
 // four warps' K partial sums are added in warp order and rounded once to the
-// act dtype.  HBM-bound for decode-sized calls (one pass over W).
+// act dtype.  HBM-bound for decode-sized calls (one pass over W).  One-token
+// calls with K % 2048 == 0 take k6_linear_t1_f8 (FP8 MMAs, no conversion).
 #include "tm_common.cuh"
 
 namespace tmoe {
@@ -175,6 +176,163 @@ __global__ void __launch_bounds__(kLinThreads) k6_linear(LinArgs<TA> a) {
   }
 }
 
+// One token, 16-bit activations (the decode step's projections): the token
+// enters FP8 mma.sync m16n8k32 as three e4m3 terms x * 2^s ~= hi + mid/16 +
+// lo/256 (one MMA column each, rows 16 bytes apart in bank order; the same
+// split as the one-token expert kernels), the packed e4m3 tile is multiplied
+// as it is (no e4m3 -> f16 conversion).  kW warps split K; each warp waits
+// only for its own part of the tile and holds its kSt B fragment pairs in
+// registers; four independent MMA chains, block scale per 128 columns; the
+// warps' partial sums are added in warp order and rounded once to the act
+// dtype.
+template <typename TA, int kW, int kSt>
+__global__ void __launch_bounds__(kW * 32) k6_linear_t1_f8(LinArgs<TA> a) {
+  static_assert(sizeof(TA) == 2, "16-bit activations");
+  extern __shared__ __align__(128) uint8_t lin_smem[];
+  const int tile_bytes = kLinRows * a.K;
+  const int part = tile_bytes / kW;
+  const int XS = a.K + 16;
+  uint8_t *wtile = lin_smem;
+  uint8_t *xb = lin_smem + tile_bytes;                          // [3][XS] e4m3: hi, mid, lo
+  const TA *xraw = reinterpret_cast<const TA *>(xb + XS);       // [K] act (before the split)
+  float *ssc = reinterpret_cast<float *>(xb + 3 * XS);          // [K/128]
+  __shared__ float red[kW][kLinRows];
+  __shared__ float xmax[kW];
+  __shared__ int s_shift;
+  __shared__ __align__(8) uint64_t bar[kW];
+  __shared__ __align__(8) uint64_t xbar;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int rg = blockIdx.x;
+  const int KB = a.K / 128;
+  if (tid == 0) {
+    for (int q = 0; q < kW; ++q) mbar_init(&bar[q], 1);
+    mbar_init(&xbar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (tid == 0) {  // W does not depend on the previous kernel: stream it now
+    const uint8_t *src = a.w + (int64_t)rg * tile_bytes;
+    for (int q = 0; q < kW; ++q) {
+      mbar_arrive_expect_tx(&bar[q], part);
+      tma_bulk_g2s_hint(wtile + q * part, src + q * part, part, &bar[q], l2_evict_first());
+    }
+  }
+  for (int i = tid; i < KB; i += kW * 32) ssc[i] = __ldg(a.s + (int64_t)((rg * kLinRows) / 128) * KB + i);
+  pdl_trigger();
+  pdl_wait();  // x (and the residual) come from earlier kernels
+  if (tid == 0) {
+    const uint32_t rowb = (uint32_t)a.K * sizeof(TA);
+    mbar_arrive_expect_tx(&xbar, rowb);
+    tma_bulk_g2s(const_cast<TA *>(xraw), a.x, rowb, &xbar);
+  }
+  const bool xok = mbar_wait_bounded(&xbar, 0);
+  if (__syncthreads_or(!xok)) {
+    if (tid == 0) {
+      if (a.status) atomicOr(a.status, TM_STATUS_TIMEOUT);
+      mbar_wait_bounded(&xbar, 0);
+      for (int q = 0; q < kW; ++q) mbar_wait_bounded(&bar[q], 0);
+    }
+    return;
+  }
+  {  // max |x| -> power-of-2 scale
+    float m = 0.f;
+    const int c_lo = w * (a.K / kW), c_hi = c_lo + a.K / kW;
+    for (int c = c_lo + lane; c < c_hi; c += 32) m = fmaxf(m, fabsf(Act<TA>::to_f(xraw[c])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) xmax[w] = m;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float m = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kW; ++ww) m = fmaxf(m, xmax[ww]);
+    s_shift = e4m3_shift(m);
+  }
+  __syncthreads();
+  {  // split: every thread first reads its elements (the raw row overlaps mid/lo)
+    constexpr int kMaxSteps = 6;  // K <= 6144 at 256 threads
+    const int steps = a.K / (4 * kW * 32);
+    const float sc = ldexpf(1.0f, s_shift);
+    float v[kMaxSteps][4];
+#pragma unroll
+    for (int k = 0; k < kMaxSteps; ++k)
+      if (k < steps) {
+        const int c = 4 * (tid + k * kW * 32);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[k][u] = Act<TA>::to_f(xraw[c + u]) * sc;
+      }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kMaxSteps; ++k)
+      if (k < steps) {
+        const int c = 4 * (tid + k * kW * 32);
+        uint32_t h, md, l;
+        e4m3_split3(v[k], h, md, l);
+        *reinterpret_cast<uint32_t *>(xb + c) = h;
+        *reinterpret_cast<uint32_t *>(xb + XS + c) = md;
+        *reinterpret_cast<uint32_t *>(xb + 2 * XS + c) = l;
+      }
+  }
+  __syncthreads();
+  const int cpw = (a.K / 16) / kW;  // 16-column chunks per warp (== 2 * kSt)
+  const int kc0 = w * cpw;
+  const int g = lane >> 2, t = lane & 3;
+  // B column n = g: 0 hi, 1 mid, 2 lo (columns 3-7 repeat lo and are not read)
+  const uint8_t *xsel = xb + min(g, 2) * XS + kc0 * 16 + 4 * t;
+  uint32_t bx[kSt][2];
+#pragma unroll
+  for (int st = 0; st < kSt; ++st) {
+    bx[st][0] = *reinterpret_cast<const uint32_t *>(xsel + st * 32);
+    bx[st][1] = *reinterpret_cast<const uint32_t *>(xsel + st * 32 + 16);
+  }
+  const bool part_ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar[w], 0));
+  // A (ldmatrix.x4): lanes 0-15 rows 0-15 of chunk kc, lanes 16-31 of chunk kc+1
+  const uint32_t wsm = smem_u32(wtile) + (kc0 + (lane >> 4)) * 256 + (lane & 15) * 16;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (part_ok) {
+#pragma unroll
+    for (int blk = 0; blk < kSt / 4; ++blk) {
+      float d[4][4];  // four independent MMA chains, one 32-column step each
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d[c][q] = 0.f;
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(wsm + (blk * 8 + 2 * st) * 256, a0, a1, a2, a3);
+        mma_16832_e4m3(d[st], a0, a1, a2, a3, bx[blk * 4 + st][0], bx[blk * 4 + st][1]);
+      }
+      const float sblk = ssc[(kc0 + blk * 8) / 8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = fmaf((d[0][q] + d[1][q]) + (d[2][q] + d[3][q]), sblk, acc[q]);
+    }
+  }
+  // D: lane (g, t=0) holds columns hi, mid of rows g, g+8; lane (g, t=1) lo
+  const float lo0 = __shfl_down_sync(0xffffffffu, acc[0], 1), lo8 = __shfl_down_sync(0xffffffffu, acc[2], 1);
+  if (t == 0) {
+    red[w][g] = acc[0] + (acc[1] + lo0 * 0.0625f) * 0.0625f;
+    red[w][g + 8] = acc[2] + (acc[3] + lo8 * 0.0625f) * 0.0625f;
+  }
+  if (__syncthreads_or(!part_ok)) {  // a part never landed: flag, let the copies finish, no output
+    if (tid == 0) {
+      if (a.status) atomicOr(a.status, TM_STATUS_TIMEOUT);
+      for (int q = 0; q < kW; ++q) mbar_wait_bounded(&bar[q], 0);
+    }
+    return;
+  }
+  if (tid < kLinRows) {
+    float y = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kW; ++ww) y += red[ww][tid];
+    y *= ldexpf(1.0f, -s_shift);
+    const int64_t o = (int64_t)rg * kLinRows + tid;
+    if (a.residual) y += Act<TA>::to_f(Act<TA>::ld_cg(a.residual + o));
+    a.out[o] = Act<TA>::from_f(y);
+  }
+}
+
 // fp32 activations: a CUDA-core kernel on the same packed layout.  Every
 // weight is dequantised as the reference's fp32 load_weight does (e4m3 ->
 // fp32 exactly, times its block scale: one fp32 rounding) and accumulated in
@@ -223,6 +381,12 @@ static size_t linear_smem(int K) {
 struct LinearLaunch {
   const void *x; int64_t T; int K, N;
   const uint8_t *w; const float *s; const void *residual; void *out; uint32_t *status; cudaStream_t st;
+  template <typename TA, int kSt> int launch_t1(const LinArgs<TA> &a, size_t smem) {
+    int rc = ensure_smem(reinterpret_cast<const void *>(k6_linear_t1_f8<TA, 8, kSt>), smem);
+    if (rc) return rc;
+    return launch_pdl(k6_linear_t1_f8<TA, 8, kSt>, dim3(N / kLinRows), dim3(8 * 32), smem, st,
+                      "k6_linear_t1_f8 launch", a);
+  }
   template <typename TA> int run() {
     if constexpr (sizeof(TA) != 2) {
       LinArgs<float> a;
@@ -233,6 +397,14 @@ struct LinearLaunch {
       LinArgs<TA> a;
       a.x = (const TA *)x; a.w = w; a.s = s; a.residual = (const TA *)residual; a.out = (TA *)out;
       a.status = status; a.T = (int)T; a.K = K; a.N = N;
+      if (T == 1 && K % 2048 == 0 && K <= 6144) {  // one token: FP8 MMAs on the split activation, 8 warps
+        const size_t smem1 = (size_t)kLinRows * K + (size_t)3 * (K + 16) + (size_t)(K / 128) * sizeof(float);
+        switch (K) {  // kSt = 32-column MMA steps per warp = K / 256
+          case 2048: return launch_t1<TA, 8>(a, smem1);
+          case 4096: return launch_t1<TA, 16>(a, smem1);
+          default: return launch_t1<TA, 24>(a, smem1);
+        }
+      }
       const size_t smem = linear_smem(K);
       int rc = ensure_smem(reinterpret_cast<const void *>(k6_linear<TA>), smem);
       if (rc) return rc;
