@@ -470,6 +470,8 @@ def run_ours(args, rank, world, local):
     }
     if args.ep_tokens > 0:
         res["ep"] = ep_measure(args, rank, world, local, loader, router)
+    if args.loader_layers > 0 and world == 1:
+        res["loader"] = loader_measure(args, local)
     if args.model_tokens > 0 and world == 1:
         res["full_model"] = model_measure(args, local)
     if prefill is not None:
@@ -539,6 +541,47 @@ def model_measure(args, local):
     del dec, L
     torch.cuda.empty_cache()
     return out
+
+
+def loader_measure(args, local):
+    """The safetensors -> packed upload path (ExpertLoader on an HF snapshot:
+    SafetensorsSource.layer_experts reads, stacks and pins each layer's 384
+    e4m3 tensors and their scales, copies them to the GPU, tm_pack_experts
+    packs them): a Qwen3-30B-A3B-shaped seeded checkpoint of
+    ``args.loader_layers`` layers written to a temporary directory, then
+    ExpertLoader(snapshot).upload() timed by the host clock with the device
+    synchronised.  The files were just written, so they are read from the page
+    cache: this times the host and PCIe side of the path, not a disk."""
+    import shutil
+    import tempfile
+    from loader.expert_loader import ExpertLoader
+    from turbomoe import synth
+    shape = synth.QWEN3_30B_A3B
+    n = args.loader_layers
+    dev = torch.device("cuda", local)
+    d = tempfile.mkdtemp(prefix="tm_snapshot_")
+    try:
+        t0 = time.time()
+        synth.write_checkpoint(d, shape, SEED, layers=n, device=dev)
+        write_s = time.time() - t0
+        file_bytes = sum(os.path.getsize(os.path.join(d, f)) for f in os.listdir(d))
+        torch.cuda.synchronize()
+        t0 = time.time()
+        L = ExpertLoader(d, config={"execution": {"dtype": "bf16"}})
+        L.upload()
+        torch.cuda.synchronize()
+        up_s = time.time() - t0
+        expert_bytes = n * shape.experts * (EXPERT_BYTES + 288 * 4)
+        del L
+        torch.cuda.empty_cache()
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    return {"workload": f"safetensors snapshot of {n} Qwen3-30B-A3B layer(s) ({shape.experts} FP8 experts each) -> "
+                        "packed device layout (ExpertLoader.upload: safetensors reads, stack + pin, H2D, "
+                        "tm_pack_experts); files in the page cache",
+            "layers": n, "file_bytes": file_bytes, "expert_bytes": expert_bytes, "upload_s": round(up_s, 3),
+            "gb_per_s": round(expert_bytes / up_s / 1e9, 2),
+            "model_48_layers_s_estimate": round(48 * up_s / n, 1), "checkpoint_write_s": round(write_s, 1)}
 
 
 # ------------------------------------- expert parallelism on every line ----
@@ -1011,6 +1054,9 @@ def main():
     ap.add_argument("--model-tokens", type=int, default=256,
                     help="also time greedy decode of the whole model: tokens generated (0 = skip; 1 GPU only)")
     ap.add_argument("--model-prompt", type=int, default=2048, help="prompt length of the whole-model decode")
+    ap.add_argument("--loader-layers", type=int, default=1,
+                    help="also time the safetensors -> packed upload of a snapshot of this many layers "
+                         "(0 = skip; 1 GPU only)")
     ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
                     help="decode: batch-1 decode (replicas for N>1); ep: expert-parallel batched decode")
     ap.add_argument("--ep-tokens", type=int, default=256,

@@ -193,17 +193,20 @@ def layer_state_dict(lw: LayerWeights, layer: int, prefix="model.layers", zero_s
 
 
 def write_checkpoint(path: str, shape: MoEShape, seed: int, layers: int = 1,
-                     zero_shared: bool | None = None, model_type=None):
+                     zero_shared: bool | None = None, model_type=None, device="cpu"):
     """Write a seeded FP8 safetensors checkpoint directory (config.json,
-    model.safetensors.index.json, one shard per layer)."""
+    model.safetensors.index.json, one shard per layer).  ``device``: where the
+    weights are generated (the seeded values differ between CPU and CUDA
+    generators; the files are the same format)."""
     from safetensors.torch import save_file
     os.makedirs(path, exist_ok=True)
     if zero_shared is None:
         zero_shared = shape.shared_inter == 0
     weight_map = {}
     for l in range(layers):
-        lw = make_layer(shape, seed, l)
+        lw = make_layer(shape, seed, l, device=device)
         sd = layer_state_dict(lw, l, zero_shared=zero_shared)
+        del lw
         fname = f"layer-{l:05d}.safetensors"
         save_file(sd, os.path.join(path, fname))
         weight_map.update({k: fname for k in sd})
