@@ -135,6 +135,14 @@ int tm_router_topk(const void *x, int64_t tokens, int hidden, int act_dtype,
                    const void *router_w, int n_experts, int top_k, int64_t *topk_idx,
                    void *topk_w, void *logits_out, void *ws, int64_t ws_bytes,
                    void *stream);
+/* One token, bf16/fp16, E <= 128, top_k <= 8, hidden <= 2048: RMSNorm of x
+ * (tm_rmsnorm's arithmetic, the same bits) written to x_norm_out, then
+ * tm_router_topk of the normalised token, in one launch: the decode step's
+ * post-attention norm fused into the router (the expert kernels then read
+ * x_norm_out). */
+int tm_rmsnorm_router_topk(const void *x, int hidden, int act_dtype, const void *norm_w, float eps,
+                           void *x_norm_out, const void *router_w, int n_experts, int top_k, int64_t *topk_idx,
+                           void *topk_w, void *logits_out, void *ws, int64_t ws_bytes, void *stream);
 
 /* Build only the routing plan from caller-supplied top-k indices (used when
  * MoEExecutor.execute_layer receives indices that did not come from
@@ -295,6 +303,12 @@ int tm_pack_linear(const uint8_t *w, int out_features, int in_features, uint8_t 
 int tm_fp8_linear(const void *x, int64_t tokens, int in_features, int out_features, int act_dtype,
                   const uint8_t *w_packed, const float *scale_inv, const void *residual, void *out,
                   uint32_t *status, void *stream);
+/* One token, bf16/fp16: RMSNorm of x (tm_rmsnorm's arithmetic, the same bits)
+ * then tm_fp8_linear of the normalised row, in one kernel (hidden 2048 or
+ * 4096): the decode step's input norm fused into the q/k/v projection. */
+int tm_rmsnorm_fp8_linear(const void *x, int hidden, int act_dtype, const void *norm_w, float eps,
+                          int out_features, const uint8_t *w_packed, const float *scale_inv,
+                          const void *residual, void *out, uint32_t *status, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* The rest of a Qwen3-MoE decode step (the full-model loop around the MoE

@@ -401,3 +401,53 @@ def test_small_model_bf16_teacher_forced():
             checked += 1
             assert got[i] == seq[i + 1], (i, got[i], seq[i + 1], margin)
     assert checked >= 8
+
+
+# ------------------------------------------------------------ fused norms ----
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_rmsnorm_fused_entry_points_same_bits(dt):
+    """tm_rmsnorm_fp8_linear == tm_rmsnorm then tm_fp8_linear, and
+    tm_rmsnorm_router_topk == tm_rmsnorm then tm_router_topk (indices, weights,
+    the normalised token), bit for bit: the fused kernels use tm_rmsnorm's
+    thread decomposition and order of sums."""
+    from turbomoe import ops, synth
+    H, N, E, k = 2048, 5120, 128, 8
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = (torch.randn(1, H, generator=g, device="cuda") * 3).to(dt)
+    nw = (1 + 0.1 * torch.randn(H, generator=g, device="cuda")).to(dt)
+    w8, s8 = synth.quantize_fp8_block(torch.randn(N, H, generator=torch.Generator().manual_seed(9)) * 0.02)
+    pl = ops.pack_linear(w8.cuda(), s8.cuda())
+    router = (torch.randn(E, H, generator=g, device="cuda") * 0.02).to(dt)
+    L = _lib()
+    normed = torch.empty_like(x)
+    assert L.tm_rmsnorm(x.data_ptr(), 1, H, ops._code(dt), nw.data_ptr(), 1e-6, normed.data_ptr(), _s()) == 0
+    want_lin = ops.fp8_linear(normed, pl)
+    got_lin = ops.rmsnorm_fp8_linear(x, nw, 1e-6, pl)
+    ws = ops.Workspace("cuda", E, k, H, 768)
+    want_idx, want_w = ops.router_topk(normed, router, k, ws)
+    xn = torch.full_like(x, float("nan"))
+    got_idx, got_w = ops.rmsnorm_router_topk(x, nw, 1e-6, router, k, ws, xn)
+    torch.cuda.synchronize()
+    assert torch.equal(got_lin, want_lin)
+    assert torch.equal(xn, normed)
+    assert torch.equal(got_idx, want_idx) and torch.equal(got_w, want_w)
+
+
+def test_decoder_fused_norms_same_bits():
+    """The bf16 decoder with its norms fused into the q/k/v projection and the
+    router gives the same hidden states, KV caches and greedy choices as with
+    the separate RMSNorm kernels (hidden 2048, two layers)."""
+    from turbomoe import synth_model as S
+    cfg = S.config(**dict(SMALL, hidden_size=2048, num_attention_heads=8, num_key_value_heads=2))
+    dec = _decoder(cfg, 21, torch.bfloat16, 64)
+    assert dec.fused_norms
+    seq = [5, 77, 2048, 9, 1000, 3, 2999, 15, 640, 1]
+    got_f = dec.teacher_forced(seq)
+    x_f, kv_f = dec.x.clone(), dec.kv.clone()
+    dec.fused_norms = False
+    dec.reset()
+    got_u = dec.teacher_forced(seq)
+    torch.cuda.synchronize()
+    assert got_f == got_u
+    assert torch.equal(dec.x, x_f)
+    assert torch.equal(dec.kv, kv_f)

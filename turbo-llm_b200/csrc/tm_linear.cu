@@ -38,6 +38,8 @@ template <typename TA> struct LinArgs {
   TA *out;
   uint32_t *status;  // optional TM_STATUS_* word
   int T, K, N;
+  const TA *norm_w;  // k6_linear_t1_f8 only (NULL: none): RMSNorm of x with this weight first
+  float eps;
 };
 
 template <typename TA>
@@ -198,6 +200,7 @@ __global__ void __launch_bounds__(kW * 32) k6_linear_t1_f8(LinArgs<TA> a) {
   float *ssc = reinterpret_cast<float *>(xb + 3 * XS);          // [K/128]
   __shared__ float red[kW][kLinRows];
   __shared__ float xmax[kW];
+  __shared__ float nred[kW];
   __shared__ int s_shift;
   __shared__ __align__(8) uint64_t bar[kW];
   __shared__ __align__(8) uint64_t xbar;
@@ -218,6 +221,17 @@ __global__ void __launch_bounds__(kW * 32) k6_linear_t1_f8(LinArgs<TA> a) {
     }
   }
   for (int i = tid; i < KB; i += kW * 32) ssc[i] = __ldg(a.s + (int64_t)((rg * kLinRows) / 128) * KB + i);
+  // RMSNorm weights (they do not depend on the previous kernel): thread tid
+  // owns elements (c * 256 + tid) * 4 .. + 3, c < 4, as k8_rmsnorm does
+  const bool norm = a.norm_w != nullptr;
+  float wv[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = (c * 256 + tid) * 4 + e;
+      wv[c][e] = (norm && i < a.K) ? Act<TA>::to_f(a.norm_w[i]) : 0.f;
+    }
   pdl_trigger();
   pdl_wait();  // x (and the residual) come from earlier kernels
   if (tid == 0) {
@@ -234,6 +248,65 @@ __global__ void __launch_bounds__(kW * 32) k6_linear_t1_f8(LinArgs<TA> a) {
     }
     return;
   }
+  if (norm) {
+    // Qwen3MoeRMSNorm of the token with k8_rmsnorm's arithmetic and thread
+    // decomposition (8 warps of 256 threads, the same sums in the same order:
+    // the same bits), kept in registers; then max |y| and the split of y
+    float v[4][4];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = (c * 256 + tid) * 4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[c][e] = 0.f;
+      if (i < a.K) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[c][e] = Act<TA>::to_f(xraw[i + e]);
+          ss = fmaf(v[c][e], v[c][e], ss);
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) nred[w] = ss;
+    __syncthreads();  // (also: every thread has read its raw x, which the split overwrites)
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kW; ++i) tot += nred[i];
+    const float r = rsqrtf(tot / (float)a.K + a.eps);
+    float m = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[c][e] = Act<TA>::round(Act<TA>::round(v[c][e] * r) * wv[c][e]);
+        m = fmaxf(m, fabsf(v[c][e]));
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) xmax[w] = m;
+    __syncthreads();
+    if (tid == 0) {
+      float mm = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kW; ++ww) mm = fmaxf(mm, xmax[ww]);
+      s_shift = e4m3_shift(mm);
+    }
+    __syncthreads();
+    const float sc = ldexpf(1.0f, s_shift);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = (c * 256 + tid) * 4;
+      if (i < a.K) {
+        float q[4] = {v[c][0] * sc, v[c][1] * sc, v[c][2] * sc, v[c][3] * sc};
+        uint32_t h, md, l;
+        e4m3_split3(q, h, md, l);
+        *reinterpret_cast<uint32_t *>(xb + i) = h;
+        *reinterpret_cast<uint32_t *>(xb + XS + i) = md;
+        *reinterpret_cast<uint32_t *>(xb + 2 * XS + i) = l;
+      }
+    }
+  } else {
   {  // max |x| -> power-of-2 scale
     float m = 0.f;
     const int c_lo = w * (a.K / kW), c_hi = c_lo + a.K / kW;
@@ -273,6 +346,7 @@ __global__ void __launch_bounds__(kW * 32) k6_linear_t1_f8(LinArgs<TA> a) {
         *reinterpret_cast<uint32_t *>(xb + XS + c) = md;
         *reinterpret_cast<uint32_t *>(xb + 2 * XS + c) = l;
       }
+  }
   }
   __syncthreads();
   const int cpw = (a.K / 16) / kW;  // 16-column chunks per warp (== 2 * kSt)
@@ -381,6 +455,7 @@ static size_t linear_smem(int K) {
 struct LinearLaunch {
   const void *x; int64_t T; int K, N;
   const uint8_t *w; const float *s; const void *residual; void *out; uint32_t *status; cudaStream_t st;
+  const void *norm_w = nullptr; float eps = 0.f;   // one-token FP8 path only
   template <typename TA, int kSt> int launch_t1(const LinArgs<TA> &a, size_t smem) {
     int rc = ensure_smem(reinterpret_cast<const void *>(k6_linear_t1_f8<TA, 8, kSt>), smem);
     if (rc) return rc;
@@ -392,11 +467,13 @@ struct LinearLaunch {
       LinArgs<float> a;
       a.x = (const float *)x; a.w = w; a.s = s; a.residual = (const float *)residual; a.out = (float *)out;
       a.status = status; a.T = (int)T; a.K = K; a.N = N;
+      a.norm_w = nullptr; a.eps = 0.f;
       return launch_pdl(k6_linear_f32, dim3(N / kLinRows), dim3(kLinThreads), 0, st, "k6_linear_f32 launch", a);
     } else {
       LinArgs<TA> a;
       a.x = (const TA *)x; a.w = w; a.s = s; a.residual = (const TA *)residual; a.out = (TA *)out;
       a.status = status; a.T = (int)T; a.K = K; a.N = N;
+      a.norm_w = (const TA *)norm_w; a.eps = eps;
       if (T == 1 && K % 2048 == 0 && K <= 6144) {  // one token: FP8 MMAs on the split activation, 8 warps
         const size_t smem1 = (size_t)kLinRows * K + (size_t)3 * (K + 16) + (size_t)(K / 128) * sizeof(float);
         switch (K) {  // kSt = 32-column MMA steps per warp = K / 256
@@ -430,5 +507,22 @@ extern "C" int tm_fp8_linear(const void *x, int64_t tokens, int in_features, int
              "x, w_packed and out must be 16-byte aligned");
   LinearLaunch f{x, tokens, in_features, out_features, w_packed, scale_inv, residual, out, status,
                  as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
+extern "C" int tm_rmsnorm_fp8_linear(const void *x, int hidden, int act_dtype, const void *norm_w, float eps,
+                                     int out_features, const uint8_t *w_packed, const float *scale_inv,
+                                     const void *residual, void *out, uint32_t *status, void *stream) {
+  TM_REQUIRE(x && norm_w && w_packed && scale_inv && out, "null pointer");
+  TM_REQUIRE(act_dtype == TM_DTYPE_BF16 || act_dtype == TM_DTYPE_F16, "16-bit activations only");
+  TM_REQUIRE(hidden == 2048 || hidden == 4096, "hidden %d unsupported (2048 or 4096)", hidden);
+  TM_REQUIRE(out_features % 128 == 0 && out_features > 0, "out_features %d must be a positive multiple of 128",
+             out_features);
+  TM_REQUIRE(aligned(x, 16) && aligned(w_packed, 16) && aligned(out, 16) && aligned(norm_w, 2) &&
+                 (!residual || aligned(residual, 2)),
+             "x, w_packed and out must be 16-byte aligned");
+  LinearLaunch f{x, 1, hidden, out_features, w_packed, scale_inv, residual, out, status, as_stream(stream)};
+  f.norm_w = norm_w;
+  f.eps = eps;
   return dispatch_act(act_dtype, f);
 }

@@ -208,6 +208,12 @@ template <typename TA> struct RouterArgs {
   int EPW;         // experts per warp per CTA
   int n_etiles, n_ttiles;
   PlanPtrs pp;
+  // one-token router only (NULL: none): x is first RMS-normalised with this
+  // weight (Qwen3MoeRMSNorm, k8_rmsnorm's arithmetic), the routing uses the
+  // normalised token, and CTA 0 writes it to x_norm_out for the expert kernels
+  const TA *norm_w;
+  float eps;
+  TA *x_norm_out;
 };
 
 // Routing plan of a call with at most 32 (token, rank) pairs: one warp,
@@ -719,7 +725,7 @@ __global__ void __launch_bounds__(kRouterThreads) k1_router_cluster(RouterArgs<T
 constexpr int kT1MaxK = 8;
 constexpr int kT1Warps = kClusterMaxE / kClusterCTAs;  // 16: one expert row per warp
 constexpr int kT1Threads = kT1Warps * 32;
-template <typename TA>
+template <typename TA, bool kNorm>
 __global__ void __launch_bounds__(kT1Threads) k1_router_t1(RouterArgs<TA> a) {
   static_assert(sizeof(TA) == 2, "16-bit activations");
   extern __shared__ __align__(128) uint8_t r_smem[];  // x row
@@ -727,6 +733,7 @@ __global__ void __launch_bounds__(kT1Threads) k1_router_t1(RouterArgs<TA> a) {
   __shared__ __align__(16) float s_logit[kClusterMaxE];
   __shared__ __align__(8) uint64_t bar;   // x copy
   __shared__ __align__(8) uint64_t lbar;  // CTA 0: 4 * E bytes of logits from the cluster
+  __shared__ float nred[8];
   constexpr int V = 8;
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
@@ -747,6 +754,17 @@ __global__ void __launch_bounds__(kT1Threads) k1_router_t1(RouterArgs<TA> a) {
     for (int i = 0; i < 8; ++i)
       if (i < vpl) row[i] = ldg_stream(src + i * 32 + lane);
   }
+  // RMSNorm weights (independent of the previous kernel): threads 0-255 own
+  // elements (c * 256 + tid) * 4 .. + 3, c < 4, as k8_rmsnorm does
+  constexpr bool norm = kNorm;   // a separate instance: the plain router keeps its registers
+  float nwv[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = (c * 256 + tid) * 4 + e;
+      nwv[c][e] = (norm && tid < 256 && i < a.H) ? Act<TA>::to_f(a.norm_w[i]) : 0.f;
+    }
   cluster.sync();  // every CTA runs and CTA 0's lbar is initialised (off the critical path)
   pdl_trigger();
   pdl_wait();  // x comes from the previous kernel
@@ -758,6 +776,48 @@ __global__ void __launch_bounds__(kT1Threads) k1_router_t1(RouterArgs<TA> a) {
   }
   const bool ok = mbar_wait_bounded(&bar, 0);
   if (!ok && lane == 0) atomicOr(a.pp.status, TM_STATUS_TIMEOUT);
+  if (norm) {
+    // Qwen3MoeRMSNorm of the token on threads 0-255 with k8_rmsnorm's sums in
+    // its order (the same bits in every CTA of the cluster and as the
+    // separate kernel); the normalised token replaces x in shared memory
+    float v[4][4];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = (c * 256 + tid) * 4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[c][e] = 0.f;
+      if (tid < 256 && i < a.H) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[c][e] = Act<TA>::to_f(xs[i + e]);
+          ss = fmaf(v[c][e], v[c][e], ss);
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0 && w < 8) nred[w] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += nred[i];
+    const float r = rsqrtf(tot / (float)a.H + a.eps);
+    if (tid < 256) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int i = (c * 256 + tid) * 4;
+        if (i < a.H) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const TA y = Act<TA>::from_f(Act<TA>::round(v[c][e] * r) * nwv[c][e]);
+            xs[i + e] = y;
+            if (crank == 0) a.x_norm_out[i + e] = y;
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -1291,6 +1351,7 @@ struct RouterLaunch {
   const WsLayout *L;
   int T, H, E, k;
   cudaStream_t s;
+  const void *norm_w = nullptr; float eps = 0.f; void *x_norm_out = nullptr;   // one-token router only
   template <typename TA> int run() {
     RouterArgs<TA> a;
     a.x = (const TA *)x;
@@ -1301,6 +1362,7 @@ struct RouterLaunch {
     a.logits_ws = ws_ptr<float>(ws, L->logits);
     a.tile_cnt = ws_ptr<int>(ws, L->router_cnt);
     a.T = T; a.H = H; a.E = E; a.k = k;
+    a.norm_w = (const TA *)norm_w; a.eps = eps; a.x_norm_out = (TA *)x_norm_out;
     if constexpr (sizeof(TA) == 2) {
       // decode-sized call: one thread-block cluster, no global synchronisation
       if (T <= kClusterMaxTFast && E <= kClusterMaxE && H / 8 <= 32 * 8 && (H / 8) % 32 == 0 && k <= 32) {
@@ -1309,9 +1371,13 @@ struct RouterLaunch {
         a.n_ttiles = 1;
         a.n_etiles = kClusterCTAs;
         const dim3 grid(kClusterCTAs), block(kRouterThreads);
-        if (T == 1 && k <= kT1MaxK)
-          return launch_cluster_pdl(k1_router_t1<TA>, grid, dim3(kT1Threads), (size_t)H * sizeof(TA), kClusterCTAs,
-                                    s, "k1_router launch", a);
+        if (T == 1 && k <= kT1MaxK) {
+          if (norm_w != nullptr)
+            return launch_cluster_pdl(k1_router_t1<TA, true>, grid, dim3(kT1Threads), (size_t)H * sizeof(TA),
+                                      kClusterCTAs, s, "k1_router launch", a);
+          return launch_cluster_pdl(k1_router_t1<TA, false>, grid, dim3(kT1Threads), (size_t)H * sizeof(TA),
+                                    kClusterCTAs, s, "k1_router launch", a);
+        }
         const size_t smem = std::max((size_t)T * H * sizeof(TA), plan_smem(kRouterWarps, E));
         switch (T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8) {
           case 1: return launch_cluster_pdl(k1_router_cluster<TA, 1>, grid, block, smem, kClusterCTAs, s, "k1_router launch", a);
@@ -1402,6 +1468,29 @@ extern "C" int tm_router_topk(const void *x, int64_t tokens, int hidden, int act
   if (rc) return rc;
   RouterLaunch f{x, router_w, topk_idx, topk_w, logits_out, ws, &L, (int)tokens, hidden, n_experts, top_k,
                  as_stream(stream)};
+  return dispatch_act(act_dtype, f);
+}
+
+extern "C" int tm_rmsnorm_router_topk(const void *x, int hidden, int act_dtype, const void *norm_w, float eps,
+                                      void *x_norm_out, const void *router_w, int n_experts, int top_k,
+                                      int64_t *topk_idx, void *topk_w, void *logits_out, void *ws, int64_t ws_bytes,
+                                      void *stream) {
+  TM_REQUIRE(x && norm_w && x_norm_out && router_w && topk_idx && topk_w, "null pointer");
+  TM_REQUIRE(act_dtype == TM_DTYPE_BF16 || act_dtype == TM_DTYPE_F16, "16-bit activations only");
+  TM_REQUIRE(hidden % 256 == 0 && hidden >= 256 && hidden <= 2048, "hidden %d must be a multiple of 256 up to 2048",
+             hidden);
+  TM_REQUIRE(n_experts >= 1 && n_experts <= kClusterMaxE && top_k >= 1 && top_k <= kT1MaxK && top_k <= n_experts,
+             "n_experts %d / top_k %d outside the one-token router (E <= %d, k <= %d)", n_experts, top_k,
+             kClusterMaxE, kT1MaxK);
+  TM_REQUIRE(aligned(x, 16) && aligned(router_w, 16) && aligned(x_norm_out, 16) && aligned(norm_w, 2),
+             "x, router_w and x_norm_out must be 16-byte aligned");
+  WsLayout L;
+  int rc = ws_check(ws, ws_bytes, 1, n_experts, top_k, hidden, 0, 0, &L);
+  if (rc) return rc;
+  RouterLaunch f{x, router_w, topk_idx, topk_w, logits_out, ws, &L, 1, hidden, n_experts, top_k, as_stream(stream)};
+  f.norm_w = norm_w;
+  f.eps = eps;
+  f.x_norm_out = x_norm_out;
   return dispatch_act(act_dtype, f);
 }
 

@@ -40,6 +40,8 @@ SIGNATURES = {
     "tm_workspace_status": (_i, [_p, _i64, C.POINTER(C.c_uint32), _p]),
     "tm_plan_offsets": (_i, [_i64, _i, _i, C.POINTER(C.c_int64)]),
     "tm_router_topk": (_i, [_p, _i64, _i, _i, _p, _i, _i, _p, _p, _p, _p, _i64, _p]),
+    "tm_rmsnorm_router_topk": (_i, [_p, _i, _i, _p, C.c_float, _p, _p, _i, _i, _p, _p, _p, _p, _i64, _p]),
+    "tm_rmsnorm_fp8_linear": (_i, [_p, _i, _i, _p, C.c_float, _i, _p, _p, _p, _p, _p, _p]),
     "tm_route_plan": (_i, [_p, _i64, _i, _i, _p, _i64, _p]),
     "tm_moe_decode_gateup": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p, _p, _i64, _p]),
     "tm_moe_decode_gateup_prefetch": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p, _p, _p, _p,

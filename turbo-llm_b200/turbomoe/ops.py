@@ -204,6 +204,27 @@ def router_topk(x: torch.Tensor, router_w: torch.Tensor, top_k: int, ws: Workspa
     return (idx, w, logits) if want_logits else (idx, w)
 
 
+def rmsnorm_router_topk(x: torch.Tensor, norm_w: torch.Tensor, eps: float, router_w: torch.Tensor, top_k: int,
+                        ws: Workspace, x_norm_out: torch.Tensor):
+    """One token: RMSNorm of ``x`` (written to ``x_norm_out``) and the router on
+    the normalised token in one launch (tm_rmsnorm_router_topk).  Returns
+    ``(idx, w)`` and leaves the plan in ``ws``, like ``router_topk``."""
+    _need_cuda(x, norm_w, router_w, x_norm_out)
+    T, H = x.shape
+    if T != 1:
+        raise TurboMoEError("rmsnorm_router_topk takes one token")
+    E = router_w.shape[0]
+    buf = ws.ensure(1, top_k)
+    idx = torch.empty(1, top_k, dtype=torch.int64, device=x.device)
+    w = torch.empty(1, top_k, dtype=x.dtype, device=x.device)
+    check(lib().tm_rmsnorm_router_topk(x.contiguous().data_ptr(), H, _code(x.dtype), norm_w.data_ptr(), eps,
+                                       x_norm_out.data_ptr(), router_w.contiguous().data_ptr(), E, top_k,
+                                       idx.data_ptr(), w.data_ptr(), None, buf.data_ptr(), buf.numel(),
+                                       _stream(x)), "tm_rmsnorm_router_topk")
+    _set_plan(ws, idx)
+    return idx, w
+
+
 def read_plan(ws: Workspace, tokens: int, top_k: int):
     """Copy the routing plan of the last router/plan call out of ``ws`` (host
     tensors; synchronises).  Returns dict(n_active, counts [E], offsets [E+1],
@@ -428,6 +449,22 @@ def pack_linear(w_fp8: torch.Tensor, scale_inv: torch.Tensor) -> PackedLinear:
     out = torch.empty(N * K, dtype=torch.uint8, device=w.device)
     check(lib().tm_pack_linear(w.data_ptr(), N, K, out.data_ptr(), _stream(w)), "tm_pack_linear")
     return PackedLinear(out, scale_inv.float().contiguous(), N, K)
+
+
+def rmsnorm_fp8_linear(x: torch.Tensor, norm_w: torch.Tensor, eps: float, pl: PackedLinear,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """One token: ``F.linear(RMSNorm(x), dequantize(W))`` in one kernel
+    (tm_rmsnorm_fp8_linear; hidden 2048 or 4096, bf16/fp16)."""
+    _need_cuda(x, norm_w)
+    T, K = x.shape
+    if T != 1 or K != pl.in_features:
+        raise TurboMoEError(f"rmsnorm_fp8_linear takes one token of {pl.in_features} features")
+    if out is None:
+        out = torch.empty(1, pl.out_features, dtype=x.dtype, device=x.device)
+    check(lib().tm_rmsnorm_fp8_linear(x.contiguous().data_ptr(), K, _code(x.dtype), norm_w.data_ptr(), eps,
+                                      pl.out_features, pl.w.data_ptr(), pl.s.data_ptr(), None, out.data_ptr(), None,
+                                      _stream(x)), "tm_rmsnorm_fp8_linear")
+    return out
 
 
 def fp8_linear(x: torch.Tensor, pl: PackedLinear, residual: torch.Tensor | None = None,
