@@ -519,6 +519,7 @@ def model_measure(args, local):
     ms = e0.elapsed_time(e1)
     st = int(dec.status.item())
     fused = bool(dec.fused_norms)
+    fused_rope = bool(dec.fused_rope)
     t = time.perf_counter()
     toks = dec.generate(prompt, N)
     e2e_s = time.perf_counter() - t
@@ -537,8 +538,8 @@ def model_measure(args, local):
            "frac": round(step_bytes / (ms / N / 1000.0) / 1e9 / hbm, 4),
            "e2e": {"tokens_per_s_incl_prefill": round(N / e2e_s, 1), "seconds": round(e2e_s, 3),
                    "path": "Qwen3MoeDecoder.generate (prompt ids from host, one position per step, ids read back)"},
-           "kernel_launches_per_token": 3 + 48 * (7 if fused else 9),
-           "norms_fused": fused,
+           "kernel_launches_per_token": 3 + 48 * (9 - (2 if fused else 0) - (1 if fused_rope else 0)),
+           "norms_fused": fused, "rope_fused_into_attention": fused_rope,
            "build_s": round(build_s, 1), "status": st, "distinct_generated": len(set(toks))}
     del dec, L
     torch.cuda.empty_cache()

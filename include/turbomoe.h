@@ -348,6 +348,16 @@ int64_t tm_attn_decode_workspace_bytes(int n_heads, int n_kv_heads, int splits);
 int tm_attn_decode(const void *q, const void *k_cache, const void *v_cache, const int64_t *position,
                    int64_t max_len, int n_heads, int n_kv_heads, int head_dim, int act_dtype, float scale,
                    int splits, void *out, void *ws, int64_t ws_bytes, void *stream);
+/* One query token, bf16/fp16: tm_qk_rope_kv and tm_attn_decode in one launch.
+ * qkv is the fused q/k/v projection output [(n_heads + 2 n_kv_heads) * 128];
+ * the query heads get q_norm + rotary inside the attention kernel, this
+ * step's k (k_norm + rotary) and v are appended to k_cache / v_cache at
+ * *position and attended to; same bits as the two calls.  A position at or
+ * past max_len appends nothing (the separate call flags it). */
+int tm_qk_rope_attn_decode(const void *qkv, const void *q_norm_w, const void *k_norm_w, float eps,
+                           const void *rope_table, const int64_t *position, int64_t max_len, int n_heads,
+                           int n_kv_heads, int head_dim, int act_dtype, float scale, int splits, void *k_cache,
+                           void *v_cache, void *out, void *stream);
 /* Batched decode (one query token per sequence, bf16/fp16): sequence b reads
  * q + b * n_heads * 128 and writes out + b * n_heads * 128, its caches start
  * at k_cache / v_cache + b * kv_batch_stride elements (each

@@ -435,19 +435,65 @@ def test_rmsnorm_fused_entry_points_same_bits(dt):
 
 def test_decoder_fused_norms_same_bits():
     """The bf16 decoder with its norms fused into the q/k/v projection and the
-    router gives the same hidden states, KV caches and greedy choices as with
-    the separate RMSNorm kernels (hidden 2048, two layers)."""
+    router, and its q/k norm + rotary + KV append fused into the attention,
+    gives the same hidden states, KV caches and greedy choices as with the
+    separate kernels (hidden 2048, two layers, 40 positions: several tiles
+    and splits)."""
     from turbomoe import synth_model as S
     cfg = S.config(**dict(SMALL, hidden_size=2048, num_attention_heads=8, num_key_value_heads=2))
     dec = _decoder(cfg, 21, torch.bfloat16, 64)
-    assert dec.fused_norms
-    seq = [5, 77, 2048, 9, 1000, 3, 2999, 15, 640, 1]
+    assert dec.fused_norms and dec.fused_rope
+    seq = [(5 + 37 * i) % 3000 for i in range(40)]
     got_f = dec.teacher_forced(seq)
     x_f, kv_f = dec.x.clone(), dec.kv.clone()
     dec.fused_norms = False
+    dec.fused_rope = False
     dec.reset()
     got_u = dec.teacher_forced(seq)
     torch.cuda.synchronize()
     assert got_f == got_u
     assert torch.equal(dec.x, x_f)
     assert torch.equal(dec.kv, kv_f)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("pos,splits", [(0, 16), (31, 1), (32, 5), (63, 16), (200, 3), (1000, 16)])
+def test_qk_rope_attn_decode_same_bits(dt, pos, splits):
+    """tm_qk_rope_attn_decode == tm_qk_rope_kv then tm_attn_decode: the same
+    output bits and the same appended k/v rows, the position at the start,
+    inside and at the end of a 32-row tile and of a split."""
+    from turbomoe import ops
+    nh, nkv, hd, max_len = 32, 4, 128, 1100
+    g = torch.Generator(device="cuda").manual_seed(pos * 3 + splits)
+    qkv = torch.randn(1, (nh + 2 * nkv) * hd, generator=g, device="cuda").to(dt)
+    qn = (1 + 0.1 * torch.randn(hd, generator=g, device="cuda")).to(dt)
+    kn = (1 + 0.1 * torch.randn(hd, generator=g, device="cuda")).to(dt)
+    from turbomoe.decoder import rope_table
+    rope = rope_table(hd, 1e6, max_len, dt).cuda()
+    kc0 = torch.randn(nkv, max_len, hd, generator=g, device="cuda").to(dt)
+    vc0 = torch.randn(nkv, max_len, hd, generator=g, device="cuda").to(dt)
+    p = torch.tensor([pos], device="cuda")
+    L = _lib()
+    code = ops._code(dt)
+    scale = 1.0 / math.sqrt(hd)
+    # separate calls
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    q = torch.empty(1, nh * hd, dtype=dt, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert L.tm_qk_rope_kv(qkv.data_ptr(), 1, nh, nkv, hd, code, qn.data_ptr(), kn.data_ptr(), 1e-6, rope.data_ptr(),
+                           p.data_ptr(), max_len, q.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), st.data_ptr(),
+                           _s()) == 0
+    ws = torch.zeros(L.tm_attn_decode_workspace_bytes(nh, nkv, splits), dtype=torch.uint8, device="cuda")
+    want = torch.empty(nh * hd, dtype=dt, device="cuda")
+    assert L.tm_attn_decode(q.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), p.data_ptr(), max_len, nh, nkv, hd, code,
+                            scale, splits, want.data_ptr(), ws.data_ptr(), ws.numel(), _s()) == 0
+    # fused
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    got = torch.full((nh * hd,), float("nan"), dtype=dt, device="cuda")
+    assert L.tm_qk_rope_attn_decode(qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(), 1e-6, rope.data_ptr(), p.data_ptr(),
+                                    max_len, nh, nkv, hd, code, scale, splits, kc2.data_ptr(), vc2.data_ptr(),
+                                    got.data_ptr(), _s()) == 0
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+    assert torch.equal(got, want)

@@ -159,6 +159,34 @@ __global__ void __launch_bounds__(256) k8_rmsnorm(const TA *x, const TA *w, int 
 // of the fused q/k/v projection).  One warp per (token, head); lane j holds
 // elements 4j..4j+3.  q heads: RMSNorm (q_norm) + rotary -> q_out [T][nh][128];
 // k heads: RMSNorm (k_norm) + rotary -> k_cache[kvh][pos]; v heads -> v_cache.
+// One head of the q/k norm + rotary step for one warp: lane j holds elements
+// 4j..4j+3 in v; RMSNorm over the head (weight nw), then rotate_half with the
+// cos/sin of position pos from the table (Qwen3MoeAttention's q_norm / k_norm
+// and apply_rotary_pos_emb, rounded to the act dtype where they round).
+template <typename TA>
+__device__ __forceinline__ void qk_norm_rope(const float (&v)[4], const TA *nw, float eps, const TA *rope,
+                                             int64_t pos, int lane, float (&out)[4]) {
+  const int e0 = 4 * lane;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)kHeadDim + eps);
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = Act<TA>::round(Act<TA>::round(v[i] * r) * Act<TA>::to_f(nw[e0 + i]));
+  float cs[4], sn[4];
+  Vec4<TA>::load(rope + (pos * 2) * kHeadDim + e0, cs);
+  Vec4<TA>::load(rope + (pos * 2 + 1) * kHeadDim + e0, sn);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // rotate_half: element e pairs with e + 64 (lane j with lane j + 16)
+    const float partner = __shfl_xor_sync(0xffffffffu, n[i], 16);
+    const float rot = lane < 16 ? -partner : partner;
+    out[i] = Act<TA>::round(Act<TA>::round(n[i] * cs[i]) + Act<TA>::round(rot * sn[i]));
+  }
+}
+
 template <typename TA>
 __global__ void __launch_bounds__(256) k8_qk_rope_kv(const TA *qkv, const TA *qn_w, const TA *kn_w, float eps,
                                                      const TA *rope, const int64_t *positions, int nh, int nkv,
@@ -183,25 +211,8 @@ __global__ void __launch_bounds__(256) k8_qk_rope_kv(const TA *qkv, const TA *qn
     return;
   }
   const bool is_q = hh < nh;
-  const TA *nw = is_q ? qn_w : kn_w;
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)kHeadDim + eps);
-  float n[4], out[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) n[i] = Act<TA>::round(Act<TA>::round(v[i] * r) * Act<TA>::to_f(nw[e0 + i]));
-  float cs[4], sn[4];
-  Vec4<TA>::load(rope + (pos * 2) * kHeadDim + e0, cs);
-  Vec4<TA>::load(rope + (pos * 2 + 1) * kHeadDim + e0, sn);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    // rotate_half: element e pairs with e + 64 (lane j with lane j + 16)
-    const float partner = __shfl_xor_sync(0xffffffffu, n[i], 16);
-    const float rot = lane < 16 ? -partner : partner;
-    out[i] = Act<TA>::round(Act<TA>::round(n[i] * cs[i]) + Act<TA>::round(rot * sn[i]));
-  }
+  float out[4];
+  qk_norm_rope<TA>(v, is_q ? qn_w : kn_w, eps, rope, pos, lane, out);
   if (is_q)
     Vec4<TA>::store(q_out + ((int64_t)t * nh + hh) * kHeadDim + e0, out);
   else
@@ -475,13 +486,24 @@ __device__ __forceinline__ void cp_async16_z(uint32_t dst, const void *src, int 
 // Sequence b = blockIdx.z of a batch: its query q + b * nh * 128, its caches
 // k_cache / v_cache + b * kv_bstride, its position position[b], its output
 // out + b * nh * 128 (one sequence: gridDim.z = 1).
-template <typename TA, int NT>
+//
+// kRope (one sequence): q points at the fused q/k/v projection output
+// [(nh + 2 nkv) * 128] of this step instead of the rotated q; each CTA applies
+// q_norm + rotary to its group's query heads itself (qk_norm_rope, the same
+// arithmetic as k8_qk_rope_kv), and the CTA whose split holds this step's
+// position applies k_norm + rotary to its KV head's k, appends k and v to the
+// caches and puts them into its own tile (that row is not read from memory).
+template <typename TA, int NT, bool kRope>
 __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, const TA *k_cache, const TA *v_cache,
                                                                   const int64_t *position, int64_t max_len, int nh,
-                                                                  int nkv, float scale, TA *out, int64_t kv_bstride) {
+                                                                  int nkv, float scale, TA *out, int64_t kv_bstride,
+                                                                  const TA *qn_w, const TA *kn_w, float eps,
+                                                                  const TA *rope) {
   extern __shared__ __align__(128) uint8_t am_smem[];
   __shared__ float s_m[kAttnMmaWarps][16], s_l[kAttnMmaWarps][16];
   __shared__ float c_m[16], c_l[16];   // this CTA's partial (read by the cluster)
+  __shared__ __align__(16) TA s_q[kRope ? 16 * kHeadDim : 8];     // kRope: the group's rotated q heads
+  __shared__ __align__(16) TA s_kv[kRope ? 2 * kHeadDim : 8];     // kRope: this position's k and v
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g8 = lane >> 2, t4 = lane & 3;
   const int G = nh / nkv;
@@ -491,7 +513,7 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
   float *obuf = reinterpret_cast<float *>(am_smem + kAttnObufOff);
   float *c_o = reinterpret_cast<float *>(am_smem + kAttnCtaOOff);
   const int64_t bz = blockIdx.z;
-  q += bz * nh * kHeadDim;
+  q += bz * (kRope ? nh + 2 * nkv : nh) * kHeadDim;
   out += bz * nh * kHeadDim;
   pdl_wait();
   // context length; a position past the cache (refused by tm_qk_rope_kv) is clamped
@@ -502,6 +524,10 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
   const int ntiles = p_begin < p_end ? (int)((p_end - p_begin + kAttnTile - 1) / kAttnTile) : 0;
   const TA *kbase = k_cache + bz * kv_bstride + (int64_t)gk * max_len * kHeadDim;
   const TA *vbase = v_cache + bz * kv_bstride + (int64_t)gk * max_len * kHeadDim;
+  // kRope: the position this step appends, when it falls in this split (a
+  // position at or past the cache lies in no split: nothing is appended)
+  const int64_t praw = kRope ? (int64_t)__ldcg(reinterpret_cast<const long long *>(position) + bz) : -1;
+  const int64_t own_row = (kRope && praw >= p_begin && praw < p_end) ? praw : -1;
   // this warp's tiles: w, w + 4, ...; 32 rows x 16 pieces of 16 B of K and of V
   // (one cp.async group per tile slot, committed by the caller: empty groups
   // keep the count uniform, so the wait below is always "all but the newest
@@ -513,7 +539,7 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
 #pragma unroll 4
     for (int i = lane; i < kAttnTile * 16; i += 32) {
       const int r = i >> 4, c = i & 15;
-      const bool in = r < cnt;
+      const bool in = r < cnt && (!kRope || p0 + r != own_row);
       const int64_t off = (p0 + (in ? r : 0)) * kHeadDim + c * 8;
       cp_async16_z(kd + r * kAttnRow + c * 16, kbase + off, in ? 16 : 0);
       cp_async16_z(vd + r * kAttnRow + c * 16, vbase + off, in ? 16 : 0);
@@ -524,17 +550,47 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
     if (w + j * kAttnMmaWarps < ntiles) issue(w + j * kAttnMmaWarps, j);
     cp_async_commit();
   }
+  if constexpr (kRope) {
+    // the group's query heads: q_norm + rotary at this step's position
+    const int64_t prope = min(max(praw, (int64_t)0), max_len - 1);
+    for (int j = w; j < G; j += kAttnMmaWarps) {
+      float v[4], r4[4];
+      Vec4<TA>::load_cg(q + (int64_t)(gk * G + j) * kHeadDim + 4 * lane, v);
+      qk_norm_rope<TA>(v, qn_w, eps, rope, prope, lane, r4);
+      Vec4<TA>::store(s_q + j * kHeadDim + 4 * lane, r4);
+    }
+    if (own_row >= 0 && w == kAttnMmaWarps - 1) {  // this KV head's k (k_norm + rotary) and v
+      float v[4], r4[4];
+      Vec4<TA>::load_cg(q + (int64_t)(nh + gk) * kHeadDim + 4 * lane, v);
+      qk_norm_rope<TA>(v, kn_w, eps, rope, own_row, lane, r4);
+      Vec4<TA>::store(s_kv + 4 * lane, r4);
+      Vec4<TA>::store(const_cast<TA *>(kbase) + own_row * kHeadDim + 4 * lane, r4);
+      Vec4<TA>::load_cg(q + (int64_t)(nh + nkv + gk) * kHeadDim + 4 * lane, v);
+      Vec4<TA>::store(s_kv + kHeadDim + 4 * lane, v);
+      Vec4<TA>::store(const_cast<TA *>(vbase) + own_row * kHeadDim + 4 * lane, v);
+    }
+    __syncthreads();
+  }
   // Q^T B fragments: column g8 of block nt = query head gk * G + 8 nt + g8 (zero past G);
   // k-step kk: dims 16 kk + 2 t4 (+1) and + 8
   uint32_t qb[NT][8][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int hh = nt * 8 + g8;
-    const TA *qh = q + (int64_t)(gk * G + hh) * kHeadDim;
+    if constexpr (kRope) {
+      const TA *qh = s_q + (hh < G ? hh : 0) * kHeadDim;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      qb[nt][kk][0] = hh < G ? __ldcg(reinterpret_cast<const unsigned *>(qh + kk * 16 + 2 * t4)) : 0u;
-      qb[nt][kk][1] = hh < G ? __ldcg(reinterpret_cast<const unsigned *>(qh + kk * 16 + 8 + 2 * t4)) : 0u;
+      for (int kk = 0; kk < 8; ++kk) {
+        qb[nt][kk][0] = hh < G ? *reinterpret_cast<const unsigned *>(qh + kk * 16 + 2 * t4) : 0u;
+        qb[nt][kk][1] = hh < G ? *reinterpret_cast<const unsigned *>(qh + kk * 16 + 8 + 2 * t4) : 0u;
+      }
+    } else {
+      const TA *qh = q + (int64_t)(gk * G + hh) * kHeadDim;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        qb[nt][kk][0] = hh < G ? __ldcg(reinterpret_cast<const unsigned *>(qh + kk * 16 + 2 * t4)) : 0u;
+        qb[nt][kk][1] = hh < G ? __ldcg(reinterpret_cast<const unsigned *>(qh + kk * 16 + 8 + 2 * t4)) : 0u;
+      }
     }
   }
   pdl_trigger();
@@ -557,6 +613,16 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
       cp_async_wait<kAttnStages - 1>();
     }
     __syncwarp();
+    if constexpr (kRope) {  // this step's k and v into their (zero-filled) row of the tile
+      const int64_t p0 = p_begin + (int64_t)ti * kAttnTile;
+      if (own_row >= p0 && own_row < p0 + kAttnTile) {
+        const int r = (int)(own_row - p0), c = lane & 15;
+        const uint4 val = *reinterpret_cast<const uint4 *>(s_kv + (lane < 16 ? 0 : kHeadDim) + c * 8);
+        *reinterpret_cast<uint4 *>(wbuf + buf * 2 * kAttnTileBytes + (lane < 16 ? 0 : kAttnTileBytes) +
+                                   r * kAttnRow + c * 16) = val;
+        __syncwarp();
+      }
+    }
     const int cnt = (int)min((int64_t)kAttnTile, p_end - (p_begin + (int64_t)ti * kAttnTile));
     const uint32_t kd = smem_u32(wbuf + buf * 2 * kAttnTileBytes), vd = kd + kAttnTileBytes;
     // S^T = K Q^T: row blocks mt (positions 16 mt..) x column blocks nt, 8 steps of 16 dims
@@ -916,15 +982,15 @@ struct RopeLaunch {
 // Cluster size for k8_attn_mma: the requested splits (<= 16), halved until
 // a cluster of that many CTAs (one SM each: the tiles take 136 KiB of shared
 // memory) can be resident.  Sizes above 8 need the non-portable opt-in.
-template <typename TA, int NT> int attn_mma_cluster(int *S) {
+template <typename TA, int NT, bool kRope> int attn_mma_cluster(int *S) {
   static std::mutex mu;
   static int fits[kAttnMaxCluster + 1] = {};   // 0 unknown, 1 fits, -1 does not
   std::lock_guard<std::mutex> g(mu);
-  int rc = ensure_smem(reinterpret_cast<const void *>(k8_attn_mma<TA, NT>), kAttnMmaSmem);
+  int rc = ensure_smem(reinterpret_cast<const void *>(k8_attn_mma<TA, NT, kRope>), kAttnMmaSmem);
   if (rc) return rc;
   static bool opted = false;
   if (!opted) {
-    rc = cuda_check(cudaFuncSetAttribute(k8_attn_mma<TA, NT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+    rc = cuda_check(cudaFuncSetAttribute(k8_attn_mma<TA, NT, kRope>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
                     "cudaFuncSetAttribute(non-portable cluster)");
     if (rc) return rc;
     opted = true;
@@ -943,7 +1009,7 @@ template <typename TA, int NT> int attn_mma_cluster(int *S) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, k8_attn_mma<TA, NT>, &cfg);
+      const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, k8_attn_mma<TA, NT, kRope>, &cfg);
       if (e != cudaSuccess) {
         (void)cudaGetLastError();
         n = 0;
@@ -960,9 +1026,10 @@ struct AttnLaunch {
   const void *q, *kc, *vc; const int64_t *pos; int64_t max_len; int nh, nkv, splits; float scale; void *out;
   float *part; unsigned *counters; cudaStream_t s;
   int batch = 1; int64_t kv_bstride = 0;
-  template <typename TA, int NT> int run_mma() {
+  const void *qn = nullptr, *kn = nullptr, *rope = nullptr; float eps = 0.f;   // q/k norm + rotary fused
+  template <typename TA, int NT, bool kRope = false> int run_mma() {
     int S = std::min(splits, kAttnMaxCluster);
-    int rc = attn_mma_cluster<TA, NT>(&S);
+    int rc = attn_mma_cluster<TA, NT, kRope>(&S);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, nkv, batch);
@@ -978,8 +1045,9 @@ struct AttnLaunch {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    return cuda_check(cudaLaunchKernelEx(&cfg, k8_attn_mma<TA, NT>, (const TA *)q, (const TA *)kc, (const TA *)vc, pos,
-                                         max_len, nh, nkv, scale, (TA *)out, kv_bstride),
+    return cuda_check(cudaLaunchKernelEx(&cfg, k8_attn_mma<TA, NT, kRope>, (const TA *)q, (const TA *)kc,
+                                         (const TA *)vc, pos, max_len, nh, nkv, scale, (TA *)out, kv_bstride,
+                                         (const TA *)qn, (const TA *)kn, eps, (const TA *)rope),
                       "k8_attn_mma launch");
   }
   template <typename TA> int run() {
@@ -1101,6 +1169,36 @@ extern "C" int tm_attn_decode_batched(const void *q, const void *k_cache, const 
              "buffers must be 16-byte aligned");
   AttnBatchLaunch b{AttnLaunch{q, k_cache, v_cache, positions, max_len, n_heads, n_kv_heads, splits, scale, out,
                                nullptr, nullptr, as_stream(stream), batch, kv_batch_stride}};
+  return dispatch_act(act_dtype, b);
+}
+
+// One step's q/k norm + rotary + KV append fused into the attention launch.
+struct AttnRopeLaunch {
+  AttnLaunch f;
+  template <typename TA> int run() {
+    if constexpr (sizeof(TA) == 2) {
+      if (f.nh / f.nkv <= 8) return f.run_mma<TA, 1, true>();
+      return f.run_mma<TA, 2, true>();
+    }
+    return fail(TM_ERR_UNSUPPORTED, "the fused q/k rotary + attention needs 16-bit activations");
+  }
+};
+
+extern "C" int tm_qk_rope_attn_decode(const void *qkv, const void *q_norm_w, const void *k_norm_w, float eps,
+                                      const void *rope_table, const int64_t *position, int64_t max_len, int n_heads,
+                                      int n_kv_heads, int head_dim, int act_dtype, float scale, int splits,
+                                      void *k_cache, void *v_cache, void *out, void *stream) {
+  TM_REQUIRE(qkv && q_norm_w && k_norm_w && rope_table && position && k_cache && v_cache && out, "null pointer");
+  TM_REQUIRE(head_dim == kHeadDim, "head_dim %d unsupported (128)", head_dim);
+  TM_REQUIRE(act_dtype == TM_DTYPE_BF16 || act_dtype == TM_DTYPE_F16, "16-bit activations only");
+  TM_REQUIRE(n_kv_heads >= 1 && n_kv_heads <= 65535 && n_heads % n_kv_heads == 0 && n_heads / n_kv_heads <= 16,
+             "%d query heads over %d KV heads unsupported (at most 16 per KV head)", n_heads, n_kv_heads);
+  TM_REQUIRE(splits >= 1 && max_len >= 1, "bad splits %d / max_len %lld", splits, (long long)max_len);
+  TM_REQUIRE(aligned(qkv, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(out, 16) &&
+                 aligned(rope_table, 16),
+             "buffers must be 16-byte aligned");
+  AttnRopeLaunch b{AttnLaunch{qkv, k_cache, v_cache, position, max_len, n_heads, n_kv_heads, splits, scale, out,
+                              nullptr, nullptr, as_stream(stream), 1, 0, q_norm_w, k_norm_w, rope_table, eps}};
   return dispatch_act(act_dtype, b);
 }
 

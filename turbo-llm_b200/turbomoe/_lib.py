@@ -63,6 +63,8 @@ SIGNATURES = {
     "tm_attn_decode_workspace_bytes": (_i64, [_i, _i, _i]),
     "tm_attn_decode": (_i, [_p, _p, _p, _p, _i64, _i, _i, _i, _i, C.c_float, _i, _p, _p, _i64, _p]),
     "tm_attn_decode_batched": (_i, [_p, _p, _p, _p, _i, _i64, _i64, _i, _i, _i, _i, C.c_float, _i, _p, _p]),
+    "tm_qk_rope_attn_decode": (_i, [_p, _p, _p, C.c_float, _p, _p, _i64, _i, _i, _i, _i, C.c_float, _i, _p, _p, _p,
+                                    _p]),
     "tm_lm_head_workspace_bytes": (_i64, []),
     "tm_lm_head_argmax": (_i, [_p, _i, _i, _p, _i64, _p, _p, _p, _i64, _p]),
     "tm_ep_buffer_bytes": (_i64, [_i, _i64, _i, _i, _i, _i]),

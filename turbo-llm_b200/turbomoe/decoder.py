@@ -114,6 +114,9 @@ class Qwen3MoeDecoder:
         # router (two launches fewer per layer, the same bits)
         self.fused_norms = (dt in (torch.bfloat16, torch.float16) and H == 2048
                             and loader.num_experts <= 128 and self.router.top_k <= 8)
+        # 16-bit: q/k norm, rotary and the KV append run inside the attention
+        # launch (tm_qk_rope_attn_decode; positions are checked on the host)
+        self.fused_rope = dt in (torch.bfloat16, torch.float16) and nh // nkv <= 16
         self.graph = None
         loader.workspace(dev).ensure(1)
 
@@ -135,13 +138,20 @@ class Qwen3MoeDecoder:
                                     self.normed.data_ptr(), s), "tm_rmsnorm")
                 ops.fp8_linear(self.normed, ly["qkv"], out=self.qkv)
             kc, vc = self.kv[l, 0], self.kv[l, 1]
-            check(Lb.tm_qk_rope_kv(self.qkv.data_ptr(), 1, nh, nkv, hd, code, ly["q_norm"].data_ptr(),
-                                   ly["k_norm"].data_ptr(), self.eps, self.rope.data_ptr(), self.pos.data_ptr(),
-                                   self.max_len, self.q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st, s),
-                  "tm_qk_rope_kv")
-            check(Lb.tm_attn_decode(self.q.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.pos.data_ptr(),
-                                    self.max_len, nh, nkv, hd, code, self.scale, self.splits, self.attn.data_ptr(),
-                                    self.attn_ws.data_ptr(), self.attn_ws.numel(), s), "tm_attn_decode")
+            if self.fused_rope:
+                check(Lb.tm_qk_rope_attn_decode(self.qkv.data_ptr(), ly["q_norm"].data_ptr(), ly["k_norm"].data_ptr(),
+                                                self.eps, self.rope.data_ptr(), self.pos.data_ptr(), self.max_len,
+                                                nh, nkv, hd, code, self.scale, self.splits, kc.data_ptr(),
+                                                vc.data_ptr(), self.attn.data_ptr(), s), "tm_qk_rope_attn_decode")
+            else:
+                check(Lb.tm_qk_rope_kv(self.qkv.data_ptr(), 1, nh, nkv, hd, code, ly["q_norm"].data_ptr(),
+                                       ly["k_norm"].data_ptr(), self.eps, self.rope.data_ptr(), self.pos.data_ptr(),
+                                       self.max_len, self.q.data_ptr(), kc.data_ptr(), vc.data_ptr(), st, s),
+                      "tm_qk_rope_kv")
+                check(Lb.tm_attn_decode(self.q.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.pos.data_ptr(),
+                                        self.max_len, nh, nkv, hd, code, self.scale, self.splits,
+                                        self.attn.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel(), s),
+                      "tm_attn_decode")
             ops.fp8_linear(self.attn, ly["o"], residual=x, out=self.x_attn)
             if self.fused_norms:
                 idx, w = ops.rmsnorm_router_topk(self.x_attn, ly["post_norm"], self.eps, self.router.routers[l],
