@@ -381,11 +381,11 @@ __global__ void __launch_bounds__(kHeadMaxAttnWarps * 32) k8_attn_decode(
 // ------------------------------------- decode attention on tensor cores ----
 // 16-bit activations: the same split-K decode attention on mma.sync
 // m16n8k16, the splits of one KV head in one thread-block cluster.  Grid
-// (S, nkv), cluster (S, 1, 1), S <= 16: CTA (split s, KV head g) has 4 warps;
-// warp w takes the 32-position tiles w, w + 4, ... of the split, each tile of
+// (S, nkv), cluster (S, 1, 1), S <= 16: CTA (split s, KV head g) has 8 warps;
+// warp w takes the 16-position tiles w, w + 8, ... of the split, each tile of
 // K and V copied by the warp itself (cp.async, rows padded to 272 B:
 // conflict-free ldmatrix; rows past the context zero-filled) into its own
-// double buffer.  The products are transposed so that the group's G query
+// three-slot ring.  The products are transposed so that the group's G query
 // heads are the MMA's N = 8 columns (NT = ceil(G / 8) column blocks) and the
 // positions / head dims its M = 16 rows: S^T = K Q^T (A = K rows by ldmatrix,
 // B = Q from registers), scaled, masked, online softmax per head (fp32, a
@@ -394,27 +394,30 @@ __global__ void __launch_bounds__(kHeadMaxAttnWarps * 32) k8_attn_decode(
 // memory as [position][head] and read back by ldmatrix.trans).  P is given
 // as two 16-bit terms hi + lo so that the product carries P to about 2^-17
 // relative like the fp32 reference (one 16-bit rounding of P alone moves
-// outputs by more than an act-dtype ulp at short contexts).  Per 32 positions
-// a warp issues 16 NT + 32 NT MMAs.  The warps' (m, l, O) merge through
+// outputs by more than an act-dtype ulp at short contexts).  Per 16 positions
+// a warp issues 8 NT + 16 NT MMAs; two warps per SM sub-partition hide each
+// other's MMA and shuffle latencies.  The warps' (m, l, O) merge through
 // shared memory into the CTA's partial; after a cluster barrier each CTA
 // reads every split's (m, l) and a slice of every split's O from distributed
 // shared memory and writes that slice of
 // out = sum_s O_s e^(m_s - M) / sum_s l_s e^(m_s - M).  No global
 // workspace, fence or atomic: the merge costs one shared::cluster round trip
 // instead of a device-scope release and a pass over L2.
-constexpr int kAttnMmaWarps = 4;
+constexpr int kAttnMmaWarps = 8;
+constexpr int kMmaTile = 16;                          // positions per tile of a warp (one MMA row block)
+constexpr int kMT = kMmaTile / 16;                    // MMA row blocks per tile
 constexpr int kAttnMaxCluster = 16;
 constexpr int kAttnRow = kHeadDim * 2 + 16;            // padded shared-memory row (bytes)
-constexpr int kAttnTileBytes = kAttnTile * kAttnRow;   // one K or V tile
+constexpr int kMmaTileBytes = kMmaTile * kAttnRow;    // one K or V tile
 constexpr int kAttnStages = 3;                                    // tiles in flight per warp
-constexpr int kAttnWarpBytes = kAttnStages * 2 * kAttnTileBytes;  // ring of K and V tiles
+constexpr int kAttnWarpBytes = kAttnStages * 2 * kMmaTileBytes;  // ring of K and V tiles
 // shared memory: the warps' tile rings; each warp's P^T hi and lo [32][16 NT
 // B].  After the loop the ring space holds each warp's O [warp][16][kAttnObRow]
 // fp32 (row stride 132 floats: the scalar stores of a warp, heads 2t and dims
 // g, hit 32 distinct banks) and the CTA's O [16][128] fp32.
 constexpr int kAttnObRow = kHeadDim + 4;
 constexpr int kAttnPOff = kAttnMmaWarps * kAttnWarpBytes;
-constexpr int kAttnPWarpBytes = 2 * kAttnTile * 32;     // hi + lo, NT <= 2
+constexpr int kAttnPWarpBytes = 2 * kMmaTile * 32;      // hi + lo, NT <= 2
 constexpr int kAttnObufOff = 0;
 constexpr int kAttnCtaOOff = kAttnObufOff + kAttnMmaWarps * 16 * kAttnObRow * 4;
 constexpr int kAttnMmaSmem = kAttnPOff + kAttnMmaWarps * kAttnPWarpBytes;
@@ -509,7 +512,7 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
   const int G = nh / nkv;
   const int s = (int)cluster_rank(), S = gridDim.x, gk = blockIdx.y;
   uint8_t *wbuf = am_smem + w * kAttnWarpBytes;
-  const uint32_t p_hi = smem_u32(am_smem + kAttnPOff + w * kAttnPWarpBytes), p_lo = p_hi + kAttnTile * 16 * NT;
+  const uint32_t p_hi = smem_u32(am_smem + kAttnPOff + w * kAttnPWarpBytes), p_lo = p_hi + kMmaTile * 16 * NT;
   float *obuf = reinterpret_cast<float *>(am_smem + kAttnObufOff);
   float *c_o = reinterpret_cast<float *>(am_smem + kAttnCtaOOff);
   const int64_t bz = blockIdx.z;
@@ -518,10 +521,10 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
   pdl_wait();
   // context length; a position past the cache (refused by tm_qk_rope_kv) is clamped
   const int64_t n = min((int64_t)__ldcg(reinterpret_cast<const long long *>(position) + bz) + 1, max_len);
-  const int64_t per = ((n + S - 1) / S + kAttnTile - 1) / kAttnTile * kAttnTile;
+  const int64_t per = ((n + S - 1) / S + kMmaTile - 1) / kMmaTile * kMmaTile;
   const int64_t p_begin = (int64_t)s * per;
   const int64_t p_end = min(n, p_begin + per);
-  const int ntiles = p_begin < p_end ? (int)((p_end - p_begin + kAttnTile - 1) / kAttnTile) : 0;
+  const int ntiles = p_begin < p_end ? (int)((p_end - p_begin + kMmaTile - 1) / kMmaTile) : 0;
   const TA *kbase = k_cache + bz * kv_bstride + (int64_t)gk * max_len * kHeadDim;
   const TA *vbase = v_cache + bz * kv_bstride + (int64_t)gk * max_len * kHeadDim;
   // kRope: the position this step appends, when it falls in this split (a
@@ -533,11 +536,11 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
   // keep the count uniform, so the wait below is always "all but the newest
   // kAttnStages - 1")
   auto issue = [&](int ti, int buf) {
-    const int64_t p0 = p_begin + (int64_t)ti * kAttnTile;
-    const int cnt = (int)min((int64_t)kAttnTile, p_end - p0);
-    const uint32_t kd = smem_u32(wbuf + buf * 2 * kAttnTileBytes), vd = kd + kAttnTileBytes;
+    const int64_t p0 = p_begin + (int64_t)ti * kMmaTile;
+    const int cnt = (int)min((int64_t)kMmaTile, p_end - p0);
+    const uint32_t kd = smem_u32(wbuf + buf * 2 * kMmaTileBytes), vd = kd + kMmaTileBytes;
 #pragma unroll 4
-    for (int i = lane; i < kAttnTile * 16; i += 32) {
+    for (int i = lane; i < kMmaTile * 16; i += 32) {
       const int r = i >> 4, c = i & 15;
       const bool in = r < cnt && (!kRope || p0 + r != own_row);
       const int64_t off = (p0 + (in ? r : 0)) * kHeadDim + c * 8;
@@ -614,32 +617,32 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
     }
     __syncwarp();
     if constexpr (kRope) {  // this step's k and v into their (zero-filled) row of the tile
-      const int64_t p0 = p_begin + (int64_t)ti * kAttnTile;
-      if (own_row >= p0 && own_row < p0 + kAttnTile) {
+      const int64_t p0 = p_begin + (int64_t)ti * kMmaTile;
+      if (own_row >= p0 && own_row < p0 + kMmaTile) {
         const int r = (int)(own_row - p0), c = lane & 15;
         const uint4 val = *reinterpret_cast<const uint4 *>(s_kv + (lane < 16 ? 0 : kHeadDim) + c * 8);
-        *reinterpret_cast<uint4 *>(wbuf + buf * 2 * kAttnTileBytes + (lane < 16 ? 0 : kAttnTileBytes) +
+        *reinterpret_cast<uint4 *>(wbuf + buf * 2 * kMmaTileBytes + (lane < 16 ? 0 : kMmaTileBytes) +
                                    r * kAttnRow + c * 16) = val;
         __syncwarp();
       }
     }
-    const int cnt = (int)min((int64_t)kAttnTile, p_end - (p_begin + (int64_t)ti * kAttnTile));
-    const uint32_t kd = smem_u32(wbuf + buf * 2 * kAttnTileBytes), vd = kd + kAttnTileBytes;
+    const int cnt = (int)min((int64_t)kMmaTile, p_end - (p_begin + (int64_t)ti * kMmaTile));
+    const uint32_t kd = smem_u32(wbuf + buf * 2 * kMmaTileBytes), vd = kd + kMmaTileBytes;
     // S^T = K Q^T: row blocks mt (positions 16 mt..) x column blocks nt, 8 steps of 16 dims
-    float sc[2][NT][4];
+    float sc[kMT][NT][4];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
-      uint32_t a[2][4];
+      uint32_t a[kMT][4];
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)  // matrices: rows +0/+8 x dims +0/+8
+      for (int mt = 0; mt < kMT; ++mt)  // matrices: rows +0/+8 x dims +0/+8
         ldsm_x4(kd + (mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kAttnRow + (kk * 16 + (lane >> 4) * 8) * 2,
                 a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
+      for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) MmaOp<TA>::run(sc[mt][nt], a[mt], qb[nt][kk][0], qb[nt][kk][1]);
     }
@@ -649,7 +652,7 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
     for (int nt = 0; nt < NT; ++nt) {
       mx[nt][0] = mx[nt][1] = -INFINITY;
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
+      for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int pos = mt * 16 + g8 + (j >> 1) * 8;
@@ -675,7 +678,7 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
     for (int nt = 0; nt < NT; ++nt) {
       rs[nt][0] = rs[nt][1] = 0.f;
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
+      for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float v = sc[mt][nt][j];
@@ -702,7 +705,7 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
         for (int j = 0; j < 4; ++j) o[md][nt][j] *= corr[nt][j & 1];
     // P^T to shared memory, [position][head] as hi and lo 16-bit pairs
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -714,17 +717,22 @@ __global__ void __launch_bounds__(kAttnMmaWarps * 32) k8_attn_mma(const TA *q, c
           asm volatile("st.shared.b32 [%0], %1;" ::"r"(p_lo + off), "r"(lo) : "memory");
         }
     __syncwarp();
-    // B fragments of P^T: matrices = positions 0-7, 8-15, 16-23, 24-31 of column block nt
-    uint32_t bh[NT][4], bl[NT][4];
+    // B fragments of P^T (column block nt): one k-step of 16 positions per MMA row block
+    uint32_t bh[NT][2 * kMT], bl[NT][2 * kMT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const uint32_t off = (lane & 31) * (16 * NT) + nt * 16;
-      ldsm_x4_t(p_hi + off, bh[nt][0], bh[nt][1], bh[nt][2], bh[nt][3]);
-      ldsm_x4_t(p_lo + off, bl[nt][0], bl[nt][1], bl[nt][2], bl[nt][3]);
+      if constexpr (kMT == 1) {  // matrices: hi positions 0-7, 8-15, lo positions 0-7, 8-15
+        const uint32_t off = (lane & 15) * (16 * NT) + nt * 16;
+        ldsm_x4_t((lane < 16 ? p_hi : p_lo) + off, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
+      } else {  // matrices: positions 0-7, 8-15, 16-23, 24-31
+        const uint32_t off = (lane & 31) * (16 * NT) + nt * 16;
+        ldsm_x4_t(p_hi + off, bh[nt][0], bh[nt][1], bh[nt][2], bh[nt][3]);
+        ldsm_x4_t(p_lo + off, bl[nt][0], bl[nt][1], bl[nt][2], bl[nt][3]);
+      }
     }
-    // O^T += V^T P^T: 2 steps of 16 positions x 8 row blocks of 16 dims
+    // O^T += V^T P^T: kMT steps of 16 positions x 8 row blocks of 16 dims
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
+    for (int ks = 0; ks < kMT; ++ks) {
       uint32_t a[8][4];
       const int row = ks * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
 #pragma unroll
