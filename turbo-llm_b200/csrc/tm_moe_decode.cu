@@ -1232,13 +1232,17 @@ __global__ void __launch_bounds__(kK3F8Threads) k3_down_t1_f8(DownArgs<TA> a) {
   pdl_wait();  // K2 (h) has completed
   const float shw = (a.has_shared && tid < kRows) ? ld_cg(a.sh_w) : 0.f;  // gate score from K2
   TM_TRACE_EVENT(a.pl.trace, kTrDownT1, kTrWaited);
-  if (tid == 0) {
+  // h (K2's output, in L2): for inner sizes up to 1024 each expert's warp
+  // loads its row straight into registers (one L2 round trip, no CTA-wide
+  // wait); larger rows come in by TMA into shared memory first
+  const bool hreg = max(a.I, a.Is) <= 1024;
+  if (tid == 0 && !hreg) {
     const uint32_t hb = (uint32_t)a.k * a.I * sizeof(float), hsb = (uint32_t)a.Is * sizeof(float);
     mbar_arrive_expect_tx(&hbar, hb + (a.has_shared ? hsb : 0));
     tma_bulk_g2s(hs, a.h, hb, &hbar);  // slots 0..k-1 of the single token
     if (a.has_shared) tma_bulk_g2s(hs + (size_t)a.k * a.I, a.sh_h, hsb, &hbar);
   }
-  const bool hok = mbar_wait_bounded(&hbar, 0);
+  const bool hok = hreg || mbar_wait_bounded(&hbar, 0);
   if (__syncthreads_or(!hok)) {
     if (tid == 0) {
       atomicOr(a.pl.status, TM_STATUS_TIMEOUT);
@@ -1253,6 +1257,37 @@ __global__ void __launch_bounds__(kK3F8Threads) k3_down_t1_f8(DownArgs<TA> a) {
     const int K = sh ? a.Is : a.I;
     const float *hf = sh ? hs + (size_t)a.k * a.I : hs + (size_t)s_rec[e].z * a.I;
     uint8_t *he = h8 + (size_t)e * 3 * KS;
+    if (hreg) {  // lane owns elements 4 lane + 128 u (K % 128 == 0, K <= 1024)
+      const float *hg = sh ? a.sh_h : a.h + (size_t)s_rec[e].z * a.I;
+      float4 hv[8];
+      float m = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (4 * lane + 128 * u < K) hv[u] = __ldcg(reinterpret_cast<const float4 *>(hg + 4 * lane + 128 * u));
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (4 * lane + 128 * u < K)
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(hv[u].x), fabsf(hv[u].y)), fmaxf(fabsf(hv[u].z), fabsf(hv[u].w))));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const int sh_exp = e4m3_shift(m);
+      const float sc = ldexpf(1.0f, sh_exp);
+      if (lane == 0) s_back[e] = ldexpf(1.0f, -sh_exp);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = 4 * lane + 128 * u;
+        if (c < K) {
+          float v[4] = {hv[u].x * sc, hv[u].y * sc, hv[u].z * sc, hv[u].w * sc};
+          uint32_t th, tm, tl;
+          e4m3_split3(v, th, tm, tl);
+          *reinterpret_cast<uint32_t *>(he + c) = th;
+          *reinterpret_cast<uint32_t *>(he + KS + c) = tm;
+          *reinterpret_cast<uint32_t *>(he + 2 * KS + c) = tl;
+        }
+      }
+      __syncwarp();
+      continue;
+    }
     // this expert's h -> three e4m3 terms with a power-of-2 scale (warp-local);
     // K % 128 == 0, so each lane's loads come in groups of 4 (issued together)
     float m4[4] = {0.f, 0.f, 0.f, 0.f};
