@@ -353,3 +353,19 @@ def test_gateup_prefetch_matches_plain_gateup(T, shared_inter):
     assert ws.status() == 0
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+@pytest.mark.parametrize("I", [384, 640, 1536])
+def test_one_token_down_inner_sizes(I):
+    """One token through k3_down_t1_f8 with inner sizes of 3, 5 and 12
+    128-column blocks: K halves of unequal length, and above 1024 the h row
+    staged by TMA instead of loaded straight into registers; against the fp32
+    evaluation of the reference's algorithm."""
+    from turbomoe import synth
+    shape = synth.MoEShape(512, I, 8, 2, 0)
+    lw = synth.make_layer(shape, 900 + I, 0)
+    x = synth.make_hidden(1, 512, I, dtype=torch.bfloat16)
+    layer = O.OracleLayer(lw, torch.bfloat16)
+    idx, w = O.compute_routing(x, layer.router, shape.top_k)
+    y = run_moe(lw, shape, x, idx, w)
+    assert_close(y, oracle_fp32(lw, x, idx, w), 1e-2, 0.99999, f"I={I}")
