@@ -81,10 +81,6 @@ template <> struct Vec4<__nv_bfloat16> : Vec4Half<__nv_bfloat16> {};
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // ------------------------------------------------------------------ embed ----
 // out[t] = table[ids[t]] (bf16 table -> act dtype, exact).  ids are read
@@ -480,10 +476,6 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t 
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
-}
-// 16-byte cp.async of `src_bytes` (16 or 0: zero fill)
-__device__ __forceinline__ void cp_async16_z(uint32_t dst, const void *src, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 
 // Sequence b = blockIdx.z of a batch: its query q + b * nh * 128, its caches

@@ -992,12 +992,26 @@ __device__ __forceinline__ void topk_redux_dispatch(const RouterArgs<TA> &a, con
 }
 
 constexpr int kTcMaxMT = 4;  // m16 tiles per cluster (64 tokens)
+constexpr int kTcPass = 8;   // 32-element chunks of the token tile staged in shared memory per pass
+constexpr int kTcRowB = kTcPass * 64;  // bytes of one staged token row
+
+// Chunks of router weights a lane keeps in flight (NT 16-byte vectors each).
+template <int NT, int MT> struct TcDepth {
+  static constexpr int value = NT <= 2 ? 4 : (NT <= 4 && MT == 1) ? 2 : 1;  // no spills at 128 registers
+};
 
 // MT m16 tiles (16 * MT tokens) per cluster; token j of a tile belongs to CTA
-// j % 8 as its row j / 8.  64-token tiles are held to 128 registers (two CTAs
-// per SM: measured faster than one CTA with more chunks in flight).  Dynamic shared memory: partial logits
-// [kClusterCTAs][2 * MT][Ec] (Ec = 64 * NT experts), later the plan's scratch
-// in CTA 0 of a one-tile call.
+// j % 8 as its row j / 8.  The CTA's slice of the token tile is staged once
+// in shared memory by cp.async (16-byte units, odd rows XOR-swizzled by 64
+// bytes so that the eight rows a warp reads per step fall on distinct banks)
+// and read by all eight warps; each warp's router rows stream from L2 into
+// registers, TcDepth chunks ahead (the first before griddepcontrol.wait).
+// Every accumulator sees the same MMA sequence as a lane loading its 16-byte
+// token and router vectors straight from global memory: chunks ascending, two
+// MMAs per chunk over the same element pairs.  64-token tiles are held to 128
+// registers (two CTAs per SM).  Dynamic shared memory: partial logits
+// [kClusterCTAs][2 * MT][Ec] (Ec = 64 * NT experts; later the plan's scratch
+// in CTA 0 of a one-tile call), then the staged token rows [16 * MT][kTcRowB].
 template <typename TA, int NT, int MT>
 __global__ void __launch_bounds__(kRouterThreads, MT == 4 ? 2 : 1) k1_router_tc(RouterArgs<TA> a) {
   static_assert(sizeof(TA) == 2, "16-bit activations");
@@ -1007,8 +1021,8 @@ __global__ void __launch_bounds__(kRouterThreads, MT == 4 ? 2 : 1) k1_router_tc(
   constexpr int EW = 8 * NT;                 // experts per warp
   constexpr int Ec = kRouterWarps * EW;      // experts per CTA (>= E)
   constexpr int R = 2 * MT;                  // rows (tokens) owned per CTA
-  constexpr int LPC = 2 * MT + NT;           // 16-byte loads per lane per chunk
-  constexpr int G = LPC <= 4 ? 2 : 1;        // chunks in flight per lane
+  constexpr int WD = TcDepth<NT, MT>::value;     // router-weight chunks in flight
+  static_assert(kTcPass % WD == 0 && kTcPass / 2 % WD == 0, "passes split into whole groups");
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -1017,7 +1031,11 @@ __global__ void __launch_bounds__(kRouterThreads, MT == 4 ? 2 : 1) k1_router_tc(
   const int nt = min(kTcTile * MT, a.T - t0);
   const int nchunk = a.H / 32;
   const int c_lo = crank * nchunk / kClusterCTAs, c_hi = (crank + 1) * nchunk / kClusterCTAs;
+  char *xs = reinterpret_cast<char *>(tc_part + kClusterCTAs * R * Ec);
+  const uint32_t xs_u32 = smem_u32(xs);
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrEnter);
+  // every CTA of the cluster has started before any writes into another's shared memory
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   // this CTA's slice of the router weights does not depend on the previous kernel
   {
     const int row_bytes = (c_hi - c_lo) * 64;  // 32 elements x 2 bytes per chunk
@@ -1028,24 +1046,6 @@ __global__ void __launch_bounds__(kRouterThreads, MT == 4 ? 2 : 1) k1_router_tc(
       asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
     }
   }
-  pdl_trigger();
-  pdl_wait();  // x comes from the previous kernel
-  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrWaited);
-  float acc[MT][NT][4];
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int j = 0; j < NT; ++j) acc[m][j][0] = acc[m][j][1] = acc[m][j][2] = acc[m][j][3] = 0.f;
-  const uint4 *xr[MT][2];
-  bool xin[MT][2];
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = 16 * m + 8 * h + g;
-      xin[m][h] = r < nt;
-      xr[m][h] = reinterpret_cast<const uint4 *>(a.x + (int64_t)(t0 + (xin[m][h] ? r : 0)) * a.H) + c;
-    }
   const uint4 *wr[NT];
   bool we[NT];
 #pragma unroll
@@ -1055,30 +1055,70 @@ __global__ void __launch_bounds__(kRouterThreads, MT == 4 ? 2 : 1) k1_router_tc(
     wr[j] = reinterpret_cast<const uint4 *>(a.w + (int64_t)(we[j] ? e : 0) * a.H) + c;
   }
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-  for (int ch = c_lo; ch < c_hi; ch += G) {
-    uint4 xv[G][MT][2], wv[G][NT];
+  uint4 wq[WD][NT];  // chunk c_lo + i * WD + u sits in wq[u]
 #pragma unroll
-    for (int u = 0; u < G; ++u) {
-      const bool in = ch + u < c_hi;
-      const int v = (ch + u) * 4;  // 16-byte vectors before this chunk
+  for (int u = 0; u < WD; ++u)
 #pragma unroll
-      for (int m = 0; m < MT; ++m)
+    for (int j = 0; j < NT; ++j) wq[u][j] = (c_lo + u < c_hi && we[j]) ? __ldg(wr[j] + (c_lo + u) * 4) : z;
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel
+  TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrWaited);
+  float acc[MT][NT][4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) xv[u][m][h] = (in && xin[m][h]) ? __ldcg(xr[m][h] + v) : z;
+  for (int m = 0; m < MT; ++m)
 #pragma unroll
-      for (int j = 0; j < NT; ++j) wv[u][j] = (in && we[j]) ? __ldg(wr[j] + v) : z;
+    for (int j = 0; j < NT; ++j) acc[m][j][0] = acc[m][j][1] = acc[m][j][2] = acc[m][j][3] = 0.f;
+  const uint32_t swz = (uint32_t)(g & 1) << 2;  // rows 16m + 8h + g share g's parity
+  for (int p0 = c_lo; p0 < c_hi; p0 += kTcPass) {
+    const int npc = min(kTcPass, c_hi - p0);
+    if (p0 != c_lo) __syncthreads();  // every warp is done with the previous pass
+    // stage the pass: rows [0, 16 * MT) (zero past the call's tokens), two groups of chunks
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int qa = half * (kTcPass / 2), qb = min(npc, qa + kTcPass / 2);
+      const int per_row = max(0, qb - qa) * 4;  // 16-byte units
+      for (int i = tid; i < kTcTile * MT * per_row; i += kRouterThreads) {
+        const int r = i / per_row, u = qa * 4 + (i - r * per_row);
+        const bool in = r < nt;
+        const TA *src = a.x + (int64_t)(t0 + (in ? r : 0)) * a.H + (p0 + (u >> 2)) * 32 + (u & 3) * 8;
+        cp_async16_z(xs_u32 + r * kTcRowB + ((u ^ ((r & 1) << 2)) << 4), src, in ? 16 : 0);
+      }
+      cp_async_commit();
     }
 #pragma unroll
-    for (int u = 0; u < G; ++u)
+    for (int b = 0; b < kTcPass; b += WD) {
+      if (b >= npc) break;  // uniform over the CTA
+      if (b == 0) {
+        cp_async_wait<1>();
+        __syncthreads();
+      } else if (b == kTcPass / 2) {
+        cp_async_wait<0>();
+        __syncthreads();
+      }
 #pragma unroll
-      for (int m = 0; m < MT; ++m)
+      for (int u = 0; u < WD; ++u) {
+        const int q = b + u;
+        if (q < npc) {
+          const uint32_t col = ((uint32_t)(q * 4 + c) ^ swz) << 4;
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const uint4 &p = xv[u][m][0], &q = xv[u][m][1], &b = wv[u][j];
-          MmaAct<TA>::run(acc[m][j], p.x, q.x, p.y, q.y, b.x, b.y);
-          MmaAct<TA>::run(acc[m][j], p.z, q.z, p.w, q.w, b.z, b.w);
+          for (int m = 0; m < MT; ++m) {
+            const uint4 p = *reinterpret_cast<const uint4 *>(xs + (16 * m + g) * kTcRowB + col);
+            const uint4 qv = *reinterpret_cast<const uint4 *>(xs + (16 * m + 8 + g) * kTcRowB + col);
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+              const uint4 &bv = wq[u][j];
+              MmaAct<TA>::run(acc[m][j], p.x, qv.x, p.y, qv.y, bv.x, bv.y);
+              MmaAct<TA>::run(acc[m][j], p.z, qv.z, p.w, qv.w, bv.z, bv.w);
+            }
+          }
+          const int nch = p0 + q + WD;
+#pragma unroll
+          for (int j = 0; j < NT; ++j) wq[u][j] = (nch < c_hi && we[j]) ? __ldg(wr[j] + nch * 4) : z;
         }
+      }
+    }
   }
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   TM_TRACE_EVENT(a.pp.trace, kTrRouter, kTrData);
   // rows 16m + g and 16m + g + 8 belong to CTA g as its rows 2m and 2m + 1
   float *dst = cluster.map_shared_rank(tc_part, g);
@@ -1140,7 +1180,9 @@ __global__ void __launch_bounds__(kRouterThreads, MT == 4 ? 2 : 1) k1_router_tc(
 }
 
 template <int NT, int MT> static size_t router_tc_smem(int E) {
-  return std::max((size_t)kClusterCTAs * 2 * MT * kRouterWarps * 8 * NT * sizeof(float),
+  const size_t part = (size_t)kClusterCTAs * 2 * MT * kRouterWarps * 8 * NT * sizeof(float);
+  // the plan's scratch (CTA 0, after the last cluster barrier) may run over the dead token rows
+  return std::max(part + (size_t)kTcTile * MT * kTcRowB,
                   std::max(plan_smem(kRouterWarps, E), (size_t)MT * E * sizeof(int)));
 }
 
@@ -1172,6 +1214,7 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
   int *cnt0 = flag + E;             // [E] counts (kept)
   int *hist = cnt0 + E;             // [kScatterWarps][E]
   int *tmp = hist + kScatterWarps * E;  // [33]
+  TM_TRACE_EVENT(pp.trace, kTrPlan, kTrEnter);
   for (int i = tid; i < 2 * E; i += kScatterThreads) sc_sm[i] = 0;
   for (int i = tid; i < kScatterWarps * E; i += kScatterThreads) hist[i] = 0;
   pdl_trigger();
@@ -1222,8 +1265,10 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
     flag[x] = cnt[x] > 0 ? 1 : 0;
   }
   __syncthreads();
+  TM_TRACE_EVENT(pp.trace, kTrPlan, kTrData);  // counts of every unit added up
   const int total = block_excl_scan(cnt, E, tmp);
   const int n_active = block_excl_scan(flag, E, tmp);
+  TM_TRACE_EVENT(pp.trace, kTrPlan, 4);  // offsets known
   if (blockIdx.x == 0) {
     for (int x = tid; x < E; x += kScatterThreads) {
       const int c0 = cnt0[x];
@@ -1262,6 +1307,7 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
     if (e >= 0) atomicAdd(&hist[w * E + e], 1);
   }
   __syncthreads();
+  TM_TRACE_EVENT(pp.trace, kTrPlan, 6);  // this CTA's per-warp histograms
   for (int x = tid; x < E; x += kScatterThreads) {
     int run = cnt[x] + before[x];
     for (int j = 0; j < kScatterWarps; ++j) {
@@ -1291,6 +1337,7 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
   for (int it = 0; it < kKeep; ++it)
     if (wlo + it * 32 < whi) place(wlo + it * 32 + lane, keep[it]);
   for (int b = wlo + kKeep * 32; b < whi; b += 32) place(b + lane, load_e(b + lane));
+  TM_TRACE_EVENT(pp.trace, kTrPlan, kTrExit);
 }
 
 // unit_hist from top-k indices given by the caller: one CTA per 16-token unit.
