@@ -20,11 +20,12 @@
 // Where the bytes go.  A tcgen05.mma with both operands in shared memory is
 // limited by shared-memory bandwidth (128 B/cycle/SM) whenever N < 256: it
 // reads (128 + N) x 32 bytes per K=16 step.  So operand A, the dequantised
-// weights, never touches shared memory: eight converter warps load the raw
-// e4m3 rows of each 64-column K slice from global memory (L2-prefetched by a
-// producer warp), dequantise them in registers and write them to tensor memory
-// with tcgen05.st; the MMA reads A from TMEM and only the token rows (B) from
-// shared memory.
+// weights, never passes through shared memory: a producer warp copies the raw
+// e4m3 rows of each 64-column K slice into a ring of shared-memory stages by
+// TMA bulk copies (several slices in flight, 1 byte per weight), eight
+// converter warps dequantise them in registers and write them to tensor
+// memory with tcgen05.st; the MMA reads A from TMEM and only the token rows
+// (B) from shared memory.
 //
 // Dequantisation.  f16 operands (gate/up always; down for fp16 activations):
 // the hardware e4m3x2 -> f16x2 conversion (exact) and one f16x2 multiply by
@@ -36,7 +37,7 @@
 // dequantisation, round(cast(w) * cast(scale)) (pf_convert4_bf16).  The tensor
 // cores accumulate in fp32, as the reference's F.linear does.
 //
-// Warp roles (20 warps): 0 L2 prefetch of the weights, 1 TMEM owner + MMA
+// Warp roles (20 warps): 0 raw weight slices by TMA, 1 TMEM owner + MMA
 // issuer, 2-3 token-row gather (cp.async into the K-major 128-byte-swizzle
 // layout, several stages in flight), 4-11 converters (warp w: operand
 // (w - 4) / 4, TMEM lane quadrant w % 4), 12-19 epilogue (two warps per lane
@@ -56,15 +57,17 @@ constexpr int kPfNSmall = 96;                    // tiles up to this size double
 constexpr int kPfAStages = 2;                    // dequantised weight slices in TMEM (converters -> MMA)
 constexpr int kPfBStages = 5;                    // token-row slices in shared memory (gather -> MMA)
 constexpr int kPfGatherLag = 3;                  // gather stages in flight (< kPfBStages)
-constexpr int kPfL2Ahead = 6;                    // weight slices prefetched into L2 ahead of the converters
+constexpr int kPfWStages = 6;                    // raw e4m3 weight slices in shared memory (TMA -> converters)
+constexpr int kPfWBytes = 16384;                 // one raw slice: 128 rows x 64 bytes x 2 operands, or 256 x 64
 constexpr int kPfBBytes = kPfNMax * kPfKT * 2;   // token rows of one stage (24 KB)
-constexpr int kPfSmem = kPfBStages * kPfBBytes + 1024;
+constexpr int kPfSmem = kPfBStages * kPfBBytes + kPfWStages * kPfWBytes + 1024;
 constexpr int kPfWPre = 0, kPfWMma = 1, kPfWGather = 2, kPfNGather = 2, kPfWConv = 4, kPfNConv = 8,
               kPfWEpi = 12, kPfNEpi = 8;
 constexpr int kPfThreads = (kPfWEpi + kPfNEpi) * 32;
 constexpr int kPfTmemCols = 512;
 constexpr int kPfAccBase = kPfAStages * 64;      // first accumulator column
-constexpr int kPfSlotCols = 192;                 // one accumulator slot (gate + up of <= 96 tokens)
+constexpr int kPfSlotCols = 2 * kPfNSmall;       // one accumulator slot (gate + up of <= 96 tokens)
+static_assert(kPfAccBase + 2 * kPfSlotCols <= kPfTmemCols, "A ring + two accumulator slots fit in TMEM");
 constexpr int kPfMaxExperts = 1024;
 constexpr int kPfMaxKBlocks = 128;               // K <= 16384
 constexpr int kPfMaxLocalTiles = 32;             // tile descriptors cached in shared memory
@@ -257,13 +260,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   uint8_t *opB = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t a_full[kPfAStages], a_empty[kPfAStages];
   __shared__ __align__(8) uint64_t b_full[kPfBStages], b_empty[kPfBStages];
+  __shared__ __align__(8) uint64_t w_full[kPfWStages], w_empty[kPfWStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
   __shared__ int prefix[kPfMaxExperts + 2];  // active experts (+ the shared expert) + end
   __shared__ int4 tl_a[kPfMaxLocalTiles];  // {e, slot0, nvalid, npad}
   __shared__ int tl_mt[kPfMaxLocalTiles];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
-  __shared__ volatile int conv_done;       // K slices the converters have finished (prefetch throttle)
   __shared__ int s_na, s_na_r, s_tiles;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -306,7 +309,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
       s_na_r = na_r;
       s_tiles = run;
       abort_flag = 0;
-      conv_done = 0;
     }
   }
   __syncthreads();
@@ -329,6 +331,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
     for (int s = 0; s < kPfBStages; ++s) {
       mbar_init(&b_full[s], kPfNGather * 32);
       mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < kPfWStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], kPfNConv * 32);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -369,30 +375,31 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
                          (size_t)kt * 4 * 256;
   };
 
+  uint8_t *wbuf = opB + kPfBStages * kPfBBytes;  // raw weight slices [kPfWStages][kPfWBytes]
   if (warp == kPfWPre) {
-    // ------------------------------------------ L2 prefetch of the weights ----
+    // ------------------------- raw weight slices -> shared memory (TMA) ----
+    // One slice = the tile's 64-column K slice of its 128 (gate, up) or 256
+    // (down) weight rows: ngroups contiguous row-group pieces of the packed
+    // layout, copied as they are; kPfWStages slices stay in flight.
     if (lane == 0) {
-      int i = 0;
-      uint64_t t0;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+      uint32_t i = 0;
       for (int j = 0; j < n_local && !abort_flag; ++j) {
         const PfTile t = tile_at(j);
-        for (int kt = 0; kt < nk && !abort_flag; ++kt, ++i) {
-          // stay at most kPfL2Ahead slices ahead of the converters
-          for (uint32_t it = 0; conv_done + kPfL2Ahead <= i && !abort_flag; ++it) {
-            if ((it & 255) == 255) {
-              uint64_t tn;
-              asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tn));
-              if (tn - t0 > 1000000000ull) break;  // keep prefetching; the converters have their own bounds
-            }
-            __nanosleep(64);
-          }
-          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        bool ok = true;
+        for (int kt = 0; kt < nk; ++kt, ++i) {
+          const int ws = i % kPfWStages;
+          if (!pf_wait(&w_empty[ws], ((i / kPfWStages) & 1) ^ 1, &abort_flag, a.status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&w_full[ws], (uint32_t)ngroups * gbytes);
           const uint8_t *src = slice_src(t, kt);
-          for (int g = 0; g < ngroups; ++g)
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src + g * gstride), "r"(gbytes) : "memory");
+          uint8_t *dst = wbuf + ws * kPfWBytes;
+          for (int g = 0; g < ngroups; ++g) tma_bulk_g2s(dst + g * gbytes, src + g * gstride, gbytes, &w_full[ws]);
         }
+        if (!ok) break;
       }
+      // every issued copy lands before this CTA may exit (the converters took
+      // them all unless the CTA is abandoning its work)
+      for (uint32_t r = i > (uint32_t)kPfWStages ? i - kPfWStages : 0; r < i; ++r)
+        if (!mbar_wait_bounded(&w_full[r % kPfWStages], (r / kPfWStages) & 1)) atomicOr(a.status, TM_STATUS_TIMEOUT);
     }
   } else if (warp == kPfWMma) {
     // ------------------------------------------------------ MMA issuer ----
@@ -482,15 +489,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
   } else if (warp < kPfWEpi) {
     // ------------------------------------------------------ converters ----
     // Thread = one weight row m (TMEM lane) of operand h: its 64-byte K slice
-    // (4 chunks of 16 B) per stage.  Software pipeline over the CTA's slices:
-    // the loads of slice i + 2 are in flight while slice i is converted.
+    // (4 chunks of 16 B) per stage, read from the raw slice the producer warp
+    // staged in shared memory (16 consecutive lanes read 256 contiguous bytes:
+    // no bank conflicts).  The block scales run two slices ahead in registers.
     const int h = (warp - kPfWConv) >> 2;
     const int q = warp & 3;
     const int m = q * 32 + lane;
     const uint32_t tlane = tmem + ((uint32_t)(q * 32) << 16);
-    // byte offset of (row m of operand h, chunk 0) inside a slice; chunk stride
-    const size_t row_off = gate_up ? (size_t)(m >> 4) * 32 * a.H + h * 256 + (m & 15) * 16
-                                   : (size_t)(h * 8 + (m >> 4)) * 16 * a.I + (m & 15) * 16;
+    // byte offset of (row m of operand h, chunk 0) inside a staged slice; chunk stride
+    const int row_off = gate_up ? (m >> 4) * 2048 + h * 256 + (m & 15) * 16 : (h * 8 + (m >> 4)) * 1024 + (m & 15) * 16;
     const int cstride = gate_up ? 512 : 256;
     auto scale_ptr = [&](const PfTile &t) -> const float * {
       if (t.e == a.E)
@@ -498,12 +505,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
       return gate_up ? a.s + ((size_t)(t.e * (a.I / 128) + t.mt) * 2 + h) * KB
                      : a.s + ((size_t)t.e * (a.H / 128) + t.mt * 2 + h) * (a.I / 128);
     };
-    int pj = 0, pkt = 0;  // next slice to load
+    int pj = 0, pkt = 0;  // next slice whose scale to load
     PfTile pt = tile_at(0);
-    auto load_slice = [&](uint4 (&dst)[4], float &sc) {
-      const uint8_t *src = slice_src(pt, pkt) + row_off;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) dst[c] = ldg_stream(src + c * cstride);
+    auto load_scale = [&](float &sc) {
       sc = __ldg(scale_ptr(pt) + (pkt * kPfKT) / 128);
       if (++pkt == nk) {
         pkt = 0;
@@ -511,22 +515,25 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
       }
     };
     const uint32_t total = (uint32_t)n_local * (uint32_t)nk;
-    uint4 b0[4], b1[4], b2[4];
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
-    load_slice(b0, s0);
-    if (total > 1) load_slice(b1, s1);
+    load_scale(s0);
+    if (total > 1) load_scale(s1);
     for (uint32_t i = 0; i < total && !abort_flag; ++i) {
-      if (i + 2 < total) load_slice(b2, s2);
-      const int as = i % kPfAStages;
-      // warp-uniform outcome: the tcgen05.st below is .sync.aligned
-      if (!__all_sync(0xffffffffu, pf_wait(&a_empty[as], ((i / kPfAStages) & 1) ^ 1, &abort_flag, a.status))) break;
-      tc_fence_after();
+      if (i + 2 < total) load_scale(s2);
+      const int wsi = i % kPfWStages;
+      if (!__all_sync(0xffffffffu, pf_wait(&w_full[wsi], (i / kPfWStages) & 1, &abort_flag, a.status))) break;
+      uint4 b0[4];
+      const uint8_t *wsrc = wbuf + wsi * kPfWBytes + row_off;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) b0[c] = *reinterpret_cast<const uint4 *>(wsrc + c * cstride);
+      // dequantise while the A stage may still be read by the MMAs of slice i - kPfAStages
+      uint32_t wv[2][16];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {  // chunks 2*half, 2*half + 1 -> 16 TMEM columns
-        uint32_t w[16];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const uint4 v = b0[2 * half + cc];
+          uint32_t *w = wv[half];
           if constexpr (kF16) {
             const uint32_t S = pf_scale_f16(s0, kw);
             pf_convert4_f16(v.x, S, w[8 * cc + 0], w[8 * cc + 1]);
@@ -541,17 +548,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
             pf_convert4_bf16(v.w, S, w[8 * cc + 6], w[8 * cc + 7]);
           }
         }
-        tc_st16(tlane + as * 64 + h * 32 + half * 16, w);
       }
+      mbar_arrive(&w_empty[wsi]);  // the slice's bytes are in registers
+      const int as = i % kPfAStages;
+      // warp-uniform outcome: the tcgen05.st below is .sync.aligned
+      if (!__all_sync(0xffffffffu, pf_wait(&a_empty[as], ((i / kPfAStages) & 1) ^ 1, &abort_flag, a.status))) break;
+      tc_fence_after();
+      tc_st16(tlane + as * 64 + h * 32, wv[0]);
+      tc_st16(tlane + as * 64 + h * 32 + 16, wv[1]);
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(&a_full[as]);
-      if (tid == kPfWConv * 32) conv_done = (int)i + 1;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        b0[c] = b1[c];
-        b1[c] = b2[c];
-      }
       s0 = s1;
       s1 = s2;
     }
@@ -584,6 +591,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k4_gemm(PfArgs<TA> a) {
         const float cs_cur = cs_next;
         if (gate_up && c0 + 32 < t.nvalid) cs_next = col_scale(c0 + 32);
         float v0[16], v1[16];
+        // the registers of an asynchronous TMEM load are read only after the
+        // wait, with nothing in between (their values land later)
         tc_ld16(tb + c0, v0);
         tc_ld16(tb + t.npad + c0, v1);
         tc_wait_ld();
