@@ -101,6 +101,66 @@ __device__ int block_excl_scan(int *a, int n, int *tmp) {
   return total;
 }
 
+// In-place exclusive scans of a[0..n) and b[0..n) by the whole block in one
+// pass (warp totals scanned by one warp); returns both totals.  tmp holds at
+// least 66 ints.
+__device__ int2 block_excl_scan2(int *a, int *b, int n, int *tmp) {
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, w = tid >> 5, nw = nt >> 5;
+  const int seg = (n + nt - 1) / nt;
+  const int lo = min(n, tid * seg), hi = min(n, lo + seg);
+  int la = 0, lb = 0;
+  for (int i = lo; i < hi; ++i) {
+    la += a[i];
+    lb += b[i];
+  }
+  int ia = la, ib = lb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int va = __shfl_up_sync(0xffffffffu, ia, o), vb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ia += va;
+      ib += vb;
+    }
+  }
+  if (lane == 31) {
+    tmp[w] = ia;
+    tmp[32 + w] = ib;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int xa = lane < nw ? tmp[lane] : 0, xb = lane < nw ? tmp[32 + lane] : 0;
+    int sa = xa, sb = xb;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int va = __shfl_up_sync(0xffffffffu, sa, o), vb = __shfl_up_sync(0xffffffffu, sb, o);
+      if (lane >= o) {
+        sa += va;
+        sb += vb;
+      }
+    }
+    if (lane < nw) {
+      tmp[lane] = sa - xa;
+      tmp[32 + lane] = sb - xb;
+    }
+    if (lane == 31) {
+      tmp[64] = sa;
+      tmp[65] = sb;
+    }
+  }
+  __syncthreads();
+  int ra = tmp[w] + ia - la, rb = tmp[32 + w] + ib - lb;
+  for (int i = lo; i < hi; ++i) {
+    const int ca = a[i], cb = b[i];
+    a[i] = ra;
+    b[i] = rb;
+    ra += ca;
+    rb += cb;
+  }
+  const int2 tot = make_int2(tmp[64], tmp[65]);
+  __syncthreads();
+  return tot;
+}
+
 // Top-k index of pair p: from shared memory when this CTA selected them, else
 // (written by other CTAs of the grid, or by the caller) from global memory.
 struct IdxSource {
@@ -1198,7 +1258,7 @@ static_assert(kUnitTokens == kTcTile, "k1_router_tc writes one unit_hist row per
 constexpr int kScatterThreads = 512;
 constexpr int kScatterWarps = kScatterThreads / 32;
 
-static size_t plan_scatter_smem(int E) { return sizeof(int) * ((size_t)(4 + kScatterWarps) * E + 64); }
+static size_t plan_scatter_smem(int E) { return sizeof(int) * ((size_t)(4 + 2 * kScatterWarps) * E + 96); }
 
 __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t *idx, int T, int k, int E,
                                                                    int U, PlanPtrs pp) {
@@ -1213,7 +1273,8 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
   int *flag = cnt + E;              // [E] active flag, then active index
   int *cnt0 = flag + E;             // [E] counts (kept)
   int *hist = cnt0 + E;             // [kScatterWarps][E]
-  int *tmp = hist + kScatterWarps * E;  // [33]
+  int *tmp = hist + kScatterWarps * E;  // [66]
+  int *part_t = tmp + 96;           // [kScatterWarps][E] partial totals of the column sums
   TM_TRACE_EVENT(pp.trace, kTrPlan, kTrEnter);
   for (int i = tid; i < 2 * E; i += kScatterThreads) sc_sm[i] = 0;
   for (int i = tid; i < kScatterWarps * E; i += kScatterThreads) hist[i] = 0;
@@ -1225,24 +1286,35 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
     for (int i = tid; i < pp.k3_cnt_n; i += kScatterThreads) pp.k3_cnt[i] = 0;
   }
   __syncthreads();
-  // column sums of unit_hist: q threads per group of 4 experts (16-byte loads)
-  // or per expert, each over a strided set of units
-  if ((E & 3) == 0) {
+  // column sums of unit_hist: q <= 16 threads per group of 4 experts (16-byte
+  // loads, each over a strided set of units) leave their partials in the
+  // (still unused) per-warp histogram rows and in part_t, added up per expert
+  // below; or q threads per expert with shared-memory atomics when E % 4 != 0
+  const bool by4 = (E & 3) == 0;
+  const int q4 = by4 ? min(kScatterWarps, max(1, kScatterThreads / (E >> 2))) : 0;
+  if (by4) {
     const int E4 = E >> 2;
-    const int q = max(1, kScatterThreads / E4);
-    for (int col = tid; col < q * E4; col += kScatterThreads) {
+    for (int col = tid; col < q4 * E4; col += kScatterThreads) {
       const int e4 = col % E4, part = col / E4;
       int4 sb = make_int4(0, 0, 0, 0), st = make_int4(0, 0, 0, 0);
 #pragma unroll 8
-      for (int u = part; u < n_units; u += q) {
+      for (int u = part; u < n_units; u += q4) {
         const int4 v = __ldcg(reinterpret_cast<const int4 *>(pp.unit_hist + (int64_t)u * E) + e4);
         st.x += v.x; st.y += v.y; st.z += v.z; st.w += v.w;
         if (u < u_lo) { sb.x += v.x; sb.y += v.y; sb.z += v.z; sb.w += v.w; }
       }
-      atomicAdd(&before[4 * e4 + 0], sb.x); atomicAdd(&before[4 * e4 + 1], sb.y);
-      atomicAdd(&before[4 * e4 + 2], sb.z); atomicAdd(&before[4 * e4 + 3], sb.w);
-      atomicAdd(&cnt[4 * e4 + 0], st.x); atomicAdd(&cnt[4 * e4 + 1], st.y);
-      atomicAdd(&cnt[4 * e4 + 2], st.z); atomicAdd(&cnt[4 * e4 + 3], st.w);
+      reinterpret_cast<int4 *>(hist + part * E)[e4] = sb;
+      reinterpret_cast<int4 *>(part_t + part * E)[e4] = st;
+    }
+    __syncthreads();
+    for (int x = tid; x < E; x += kScatterThreads) {
+      int sb = 0, st = 0;
+      for (int part = 0; part < q4; ++part) {
+        sb += hist[part * E + x];
+        st += part_t[part * E + x];
+      }
+      before[x] = sb;
+      cnt[x] = st;
     }
   } else {
     const int q = max(1, kScatterThreads / E);
@@ -1266,8 +1338,12 @@ __global__ void __launch_bounds__(kScatterThreads) k1_plan_scatter(const int64_t
   }
   __syncthreads();
   TM_TRACE_EVENT(pp.trace, kTrPlan, kTrData);  // counts of every unit added up
-  const int total = block_excl_scan(cnt, E, tmp);
-  const int n_active = block_excl_scan(flag, E, tmp);
+  const int2 tots = block_excl_scan2(cnt, flag, E, tmp);
+  const int total = tots.x, n_active = tots.y;
+  if (by4) {  // the partials are read (barrier inside the scan): clear the histogram rows again
+    for (int i = tid; i < q4 * E; i += kScatterThreads) hist[i] = 0;  // rows written above
+    __syncthreads();
+  }
   TM_TRACE_EVENT(pp.trace, kTrPlan, 4);  // offsets known
   if (blockIdx.x == 0) {
     for (int x = tid; x < E; x += kScatterThreads) {
