@@ -273,8 +273,10 @@ def test_cuda_graph_replay_matches_eager():
 # tile (17, 40), 64-token tiles with a ragged last one (600), experts that do not fill the last warp (60) and 1..16 n-tiles per
 # warp (60, 128, 512, 1024 experts).  Logits against an fp64 dot product of the
 # same act-dtype inputs, rounded once: within one act-dtype ulp.
+# hidden 4096: two staged passes of the token tile per CTA; hidden 2176: CTAs of
+# 8 and 9 chunks (a second pass of one chunk)
 TILE_CASES = [(60, 4, 1024, torch.float16), (128, 8, 2048, torch.bfloat16), (512, 10, 1024, torch.bfloat16),
-              (1024, 8, 512, torch.float16)]
+              (1024, 8, 512, torch.float16), (128, 8, 4096, torch.bfloat16), (256, 8, 2176, torch.float16)]
 
 
 @pytest.mark.parametrize("E,k,H,dt", TILE_CASES)
