@@ -25,7 +25,8 @@ import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(REPO, "turbo-llm_b200")
-REF = os.environ.get("TURBO_LLM_REFERENCE", "/root/reference")
+# the reference checkout: TURBO_LLM_REFERENCE, else a directory `reference` beside this repository
+REF = os.environ.get("TURBO_LLM_REFERENCE", os.path.join(os.path.dirname(REPO), "reference"))
 
 pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "execution")),
                                 reason="no reference checkout")
