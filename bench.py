@@ -173,7 +173,9 @@ def run_ours(args, rank, world, local):
     t0 = time.time()
     loader.upload()
     upload_s = time.time() - t0
-    router = RouterExecutor(loader, LAYERS)
+    # opt-in: speculative L2 prefetch of each next layer's experts (slower as it stands)
+    use_pf = args.tokens <= 8 and args.next_layer_prefetch
+    router = RouterExecutor(loader, LAYERS, prefetch_next_layer=use_pf)
     moe = MoEExecutor(loader, record_timing=False)
     ws = loader.workspace(dev)
     ws.ensure(args.tokens)
@@ -213,6 +215,42 @@ def run_ours(args, rank, world, local):
     ms_per_step = ms / args.steps
     value = world * args.tokens * args.steps / (ms / 1000.0)
     assert torch.isfinite(x_out.float()).all(), "non-finite output"
+
+    # the same step without the next-layer prefetch (same outputs, bit for bit)
+    next_layer_prefetch = None
+    if use_pf:
+        router_plain = RouterExecutor(loader, LAYERS)
+
+        def step_plain(x):
+            for l in range(LAYERS):
+                idx, w = router_plain.compute_routing(l, x)
+                x = moe.execute_layer(l, x, idx, w, residual=x)
+            return x
+
+        graph_p = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_p):
+            x_out_p = step_plain(x_in)
+        for _ in range(args.warmup):
+            graph_p.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0.record()
+        for _ in range(args.steps):
+            graph_p.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        ms_p = max_over_ranks(ev0.elapsed_time(ev1), world)
+        graph.replay()
+        torch.cuda.synchronize()
+        next_layer_prefetch = {
+            "what": "layer l+1's router applied to layer l's input on a side stream names the experts whose "
+                    "gate/up weights are bulk-prefetched into L2 (tm_prefetch_experts_l2) while HBM is idle; "
+                    "a hint only",
+            "value_without": round(world * args.tokens * args.steps / (ms_p / 1000.0), 2),
+            "ms_per_step_without": round(ms_p / args.steps, 4),
+            "same_output_bits": bool(torch.equal(x_out, x_out_p)),
+        }
+        del graph_p
 
     # ---- e2e: public API, host buffers, H2D + D2H inside the timed region ----
     x_host = x0.cpu().pin_memory()
@@ -261,6 +299,18 @@ def run_ours(args, rank, world, local):
     routes = [router.compute_routing(l, xs[l]) for l in range(LAYERS)]
     out = torch.empty_like(x0)
     torch.cuda.synchronize()
+    if next_layer_prefetch is not None and LAYERS > 1:
+        # share of the experts each layer routes to that the prediction from the previous layer's input named
+        pws = ops.Workspace(dev, 128, 8, shape.hidden, shape.inter, 0)
+        pws.ensure(args.tokens)
+        hits = total = 0
+        for l in range(LAYERS - 1):
+            pred, _ = ops.router_topk(xs[l], router.routers[l + 1], 8, pws)
+            act = routes[l + 1][0]
+            for t in range(args.tokens):
+                hits += len(set(pred[t].tolist()) & set(act[t].tolist()))
+                total += act.shape[1]
+        next_layer_prefetch["hit_rate"] = round(hits / max(total, 1), 4)
 
     def run_parts(with_k2, with_k3):
         for l in range(LAYERS):
@@ -485,10 +535,12 @@ def run_ours(args, rank, world, local):
         "moe_layer": {"gbs": round(layer_gbs, 1), "frac": round(layer_gbs / peak, 4),
                       "bytes_per_layer": LAYER_BYTES, "us_per_layer": round(ms_per_step * 1000 / LAYERS, 3),
                       "k3_us": round(k3 * 1000, 3)},
-        "gpu_launches": args.steps * LAYERS * 3,
+        "gpu_launches": args.steps * (LAYERS * 3 + ((LAYERS - 1) * 2 if use_pf else 0)),
         "clocks": clk.summary(),
         "upload_s": round(upload_s, 1),
     }
+    if next_layer_prefetch is not None:
+        res["next_layer_prefetch"] = next_layer_prefetch
     if args.ep_tokens > 0:
         res["ep"] = ep_measure(args, rank, world, local, loader, router)
     if args.loader_layers > 0 and world == 1:
@@ -1069,6 +1121,9 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="MoE layers per step (48 = the model)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--next-layer-prefetch", action="store_true",
+                    help="decode with the speculative L2 prefetch of each next layer's experts (also times the "
+                         "step without it)")
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="also time one prefill layer call of this many tokens (0 = skip)")
     ap.add_argument("--attn-layers", type=int, default=48,

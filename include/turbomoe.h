@@ -193,6 +193,18 @@ int tm_moe_decode_down_combine(int64_t tokens, int hidden, int inter, int n_expe
                                const float *sh_s2, int shared_inter, const void *residual,
                                void *out, void *ws, int64_t ws_bytes, void *stream);
 
+/* L2 prefetch of whole experts' packed weights: for each id in
+ * expert_ids[0..n_ids) (device int64; ids outside [0, n_experts) are
+ * skipped), bulk-prefetches bytes [id * expert_bytes, (id + 1) *
+ * expert_bytes) of `weights` into L2.  A hint only: nothing is read into the
+ * SMs or waited on, and no result depends on it.  Used to pull the experts a
+ * later layer is predicted to route to (the w13 array of that layer,
+ * expert_bytes = tm_packed_w13_bytes) into L2 while HBM would otherwise be
+ * idle; no reference counterpart.  weights 16-byte aligned, expert_bytes a
+ * multiple of 16. */
+int tm_prefetch_experts_l2(const uint8_t *weights, int64_t expert_bytes, int n_experts,
+                           const int64_t *expert_ids, int n_ids, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* K4: prefill (many tokens) as grouped GEMMs on the tcgen05 tensor cores.
  * Replaces the multi-token branch of MoEExecutor.execute_layer

@@ -99,3 +99,19 @@ def test_gateup_prefetch_argument_errors_without_launch():
     assert rc == _lib.TM_ERR_INVALID and b"shared expert" in L.tm_last_error()  # shared w13 without sh_w2
     rc = f(16, 1, 2048, 768, 128, 8, 2, 24, 16, None, None, 0, None, 16, None, 256, 1 << 30, None)
     assert rc == _lib.TM_ERR_INVALID and b"aligned" in L.tm_last_error()
+
+
+def test_prefetch_experts_argument_errors_without_launch():
+    """tm_prefetch_experts_l2 rejects null pointers, bad counts, sizes that
+    are not multiples of 16 and unaligned weights on the host."""
+    L = _lib.lib()
+    f = L.tm_prefetch_experts_l2
+    # weights, expert_bytes, n_experts, expert_ids, n_ids, stream
+    rc = f(None, 3145728, 128, 16, 8, None)
+    assert rc == _lib.TM_ERR_INVALID and b"null" in L.tm_last_error()
+    rc = f(16, 3145728, 128, 16, 0, None)
+    assert rc == _lib.TM_ERR_INVALID and b"expert counts" in L.tm_last_error()
+    rc = f(16, 3145720, 128, 16, 8, None)
+    assert rc == _lib.TM_ERR_INVALID and b"multiple of 16" in L.tm_last_error()
+    rc = f(24, 3145728, 128, 16, 8, None)
+    assert rc == _lib.TM_ERR_INVALID and b"aligned" in L.tm_last_error()

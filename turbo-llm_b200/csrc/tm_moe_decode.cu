@@ -1518,6 +1518,39 @@ struct DownLaunch {
 
 using namespace tmoe;
 
+namespace tmoe {
+// L2 prefetch of whole experts' packed weights (cp.async.bulk.prefetch.L2):
+// block (c, j) covers chunk c of expert ids[j]; each of its threads issues
+// one bulk prefetch of kPfPiece bytes.  No data moves into the SM, nothing is
+// waited on; ids outside [0, E) are skipped.
+constexpr int kPrefetchThreads = 4;
+constexpr int64_t kPrefetchPiece = 16384;
+constexpr int64_t kPrefetchChunk = kPrefetchThreads * kPrefetchPiece;
+__global__ void __launch_bounds__(kPrefetchThreads) k_prefetch_experts_l2(const uint8_t *w, int64_t expert_bytes,
+                                                                          const int64_t *ids, int E) {
+  const int64_t e = __ldg(ids + blockIdx.y);
+  if (e < 0 || e >= E) return;
+  const int64_t off = (int64_t)blockIdx.x * kPrefetchChunk + (int64_t)threadIdx.x * kPrefetchPiece;
+  if (off >= expert_bytes) return;
+  const uint32_t n = (uint32_t)min(kPrefetchPiece, expert_bytes - off);
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w + e * expert_bytes + off), "r"(n) : "memory");
+}
+}  // namespace tmoe
+
+extern "C" int tm_prefetch_experts_l2(const uint8_t *weights, int64_t expert_bytes, int n_experts,
+                                      const int64_t *expert_ids, int n_ids, void *stream) {
+  TM_REQUIRE(weights && expert_ids, "null pointer");
+  TM_REQUIRE(n_experts > 0 && n_ids > 0 && n_ids <= 65535, "bad expert counts (%d experts, %d ids)", n_experts, n_ids);
+  TM_REQUIRE(expert_bytes > 0 && expert_bytes % 16 == 0, "expert_bytes (%lld) must be a positive multiple of 16",
+             (long long)expert_bytes);
+  TM_REQUIRE(reinterpret_cast<uintptr_t>(weights) % 16 == 0, "weights must be 16-byte aligned");
+  const int64_t chunks = (expert_bytes + tmoe::kPrefetchChunk - 1) / tmoe::kPrefetchChunk;
+  TM_REQUIRE(chunks <= 0x7fffffff, "expert too large");
+  tmoe::k_prefetch_experts_l2<<<dim3((unsigned)chunks, (unsigned)n_ids), tmoe::kPrefetchThreads, 0,
+                                tmoe::as_stream(stream)>>>(weights, expert_bytes, expert_ids, n_experts);
+  return tmoe::cuda_check(cudaGetLastError(), "k_prefetch_experts_l2 launch");
+}
+
 extern "C" int tm_moe_decode_gateup(const void *x, int64_t tokens, int hidden, int inter,
                                     int n_experts, int top_k, int act_dtype, const uint8_t *w13,
                                     const float *s13, const uint8_t *sh_w13, const float *sh_s13,

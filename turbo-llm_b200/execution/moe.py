@@ -70,6 +70,9 @@ class MoEExecutor:
             start.record()
         y = ops.moe_experts(hidden_states, top_k_indices, top_k_weights, pl.experts, ws,
                             shared=pl.shared, shared_gate_w=pl.shared_gate, residual=residual, out=out)
+        spec = getattr(self.loader, "next_layer_prefetch", None)
+        if spec is not None:  # the speculative prefetch branch forked by RouterExecutor rejoins here
+            spec.join()
         if timing:
             end.record()
             self._events = (start, end)

@@ -48,6 +48,7 @@ SIGNATURES = {
                                            _i64, _p]),
     "tm_moe_decode_down_combine": (_i, [_i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _i, _p, _p, _p,
                                         _i64, _p]),
+    "tm_prefetch_experts_l2": (_i, [_p, _i64, _i, _p, _i, _p]),
     "tm_moe_prefill_grouped": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p,
                                     _p, _p, _p, _i64, _p]),
     "tm_moe_grouped_f8": (_i, [_p, _i64, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p,

@@ -311,6 +311,18 @@ def moe_gateup(x: torch.Tensor, top_k: int, packed: PackedExperts, ws: Workspace
         check(lib().tm_moe_decode_gateup(*head, buf.data_ptr(), buf.numel(), _stream(x)), "tm_moe_decode_gateup")
 
 
+def prefetch_experts_l2(packed: PackedExperts, expert_ids: torch.Tensor):
+    """Bulk-prefetch the gate/up weights of ``expert_ids`` (device int64, any
+    shape; ids outside [0, E) skipped) of one packed layer into L2 on the
+    current stream.  A hint: no result depends on it."""
+    ids = expert_ids.reshape(-1)
+    if ids.dtype != torch.int64 or not ids.is_contiguous():
+        raise TurboMoEError("expert ids must be a contiguous int64 tensor")
+    n13 = lib().tm_packed_w13_bytes(packed.hidden, packed.inter)
+    check(lib().tm_prefetch_experts_l2(packed.w13.data_ptr(), n13, packed.n_experts, ids.data_ptr(), ids.numel(),
+                                       _stream(ids)), "tm_prefetch_experts_l2")
+
+
 def moe_down_combine(w: torch.Tensor, packed: PackedExperts, ws: Workspace, out: torch.Tensor,
                      shared: PackedExperts | None = None, residual: torch.Tensor | None = None):
     """K3 alone: down projection + weighted combine into ``out`` (after K2)."""
