@@ -175,7 +175,7 @@ def run_ours(args, rank, world, local):
     upload_s = time.time() - t0
     # opt-in: speculative L2 prefetch of each next layer's experts (slower as it stands)
     use_pf = args.tokens <= 8 and args.next_layer_prefetch
-    router = RouterExecutor(loader, LAYERS, prefetch_next_layer=use_pf)
+    router = RouterExecutor(loader, LAYERS, prefetch_next_layer=use_pf, prefetch_join_every=args.prefetch_join_every)
     moe = MoEExecutor(loader, record_timing=False)
     ws = loader.workspace(dev)
     ws.ensure(args.tokens)
@@ -249,6 +249,7 @@ def run_ours(args, rank, world, local):
             "value_without": round(world * args.tokens * args.steps / (ms_p / 1000.0), 2),
             "ms_per_step_without": round(ms_p / args.steps, 4),
             "same_output_bits": bool(torch.equal(x_out, x_out_p)),
+            "join_every": args.prefetch_join_every,
         }
         del graph_p
 
@@ -1124,6 +1125,8 @@ def main():
     ap.add_argument("--next-layer-prefetch", action="store_true",
                     help="decode with the speculative L2 prefetch of each next layer's experts (also times the "
                          "step without it)")
+    ap.add_argument("--prefetch-join-every", type=int, default=1,
+                    help="with --next-layer-prefetch: rejoin the prefetch branch every this many layers")
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="also time one prefill layer call of this many tokens (0 = skip)")
     ap.add_argument("--attn-layers", type=int, default=48,

@@ -72,7 +72,7 @@ class MoEExecutor:
                             shared=pl.shared, shared_gate_w=pl.shared_gate, residual=residual, out=out)
         spec = getattr(self.loader, "next_layer_prefetch", None)
         if spec is not None:  # the speculative prefetch branch forked by RouterExecutor rejoins here
-            spec.join()
+            spec.layer_done(layer_id)
         if timing:
             end.record()
             self._events = (start, end)

@@ -24,14 +24,16 @@ class NextLayerPrefetch:
     runs while the current layer's expert kernels read from L2, and layer
     l+1's gate/up kernel then finds the experts predicted correctly in L2.
     The prediction is a hint only: routing and outputs are unchanged.
-    ``MoEExecutor.execute_layer`` joins the side stream after its kernels
-    (``join``), so a graph captured over whole layers has no loose branch.
+    ``MoEExecutor.execute_layer`` rejoins the side stream after its kernels
+    (``layer_done``) every ``join_every`` layers and after the last one, so a
+    graph captured over whole layers has no loose branch.
     """
 
-    def __init__(self, loader, routers, top_k):
+    def __init__(self, loader, routers, top_k, join_every=1):
         self.loader = loader
         self.routers = routers
         self.top_k = top_k
+        self.join_every = max(1, int(join_every))
         self.stream = None
         self.ws = None
         self.pending = None
@@ -40,7 +42,6 @@ class NextLayerPrefetch:
         nxt = layer_id + 1
         if nxt not in self.routers or flat.shape[0] > 8:
             return
-        self.join()
         dev = flat.device
         if self.stream is None:
             self.stream = torch.cuda.Stream(device=dev)
@@ -64,10 +65,16 @@ class NextLayerPrefetch:
             torch.cuda.current_stream().wait_event(self.pending)
             self.pending = None
 
+    def layer_done(self, layer_id):
+        """After a layer's expert kernels: rejoin the side stream every
+        ``join_every`` layers and after the last layer with a router."""
+        if (layer_id + 1) % self.join_every == 0 or layer_id + 1 >= len(self.routers):
+            self.join()
+
 
 class RouterExecutor:
 
-    def __init__(self, loader, num_layers, top_k=8, prefetch_next_layer=False):
+    def __init__(self, loader, num_layers, top_k=8, prefetch_next_layer=False, prefetch_join_every=1):
         self.loader = loader
         self.num_layers = num_layers
         self.top_k = top_k
@@ -75,7 +82,8 @@ class RouterExecutor:
         for i in range(self.num_layers):
             self.routers[i] = self.loader.load_weight(self.loader.layout.router_tensor(i)).contiguous()
         # decode calls (<= 8 tokens): speculative L2 prefetch of layer l+1's experts
-        self.next_layer_prefetch = NextLayerPrefetch(loader, self.routers, top_k) if prefetch_next_layer else None
+        self.next_layer_prefetch = (NextLayerPrefetch(loader, self.routers, top_k, prefetch_join_every)
+                                    if prefetch_next_layer else None)
         if self.next_layer_prefetch is not None:
             loader.next_layer_prefetch = self.next_layer_prefetch
 
