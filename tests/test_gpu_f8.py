@@ -7,7 +7,7 @@ F.linear / F.silu / * round them (execution/moe.py:157-202).  `emulate`
 restates that on the CPU with the exactly dequantised weights (fp32), so the
 kernels must agree with it up to the order of the fp32 sums: max-abs <= 1e-2,
 cosine >= 0.99999 and most elements bitwise equal.  Against the reference's
-own golden outputs the north-star bar applies (max-abs 2e-2, cosine 0.9995).
+own golden outputs the layer-output tolerance applies (max-abs 2e-2, cosine 0.9995).
 """
 import pytest
 import torch

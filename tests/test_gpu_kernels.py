@@ -1,7 +1,7 @@
 """GPU parity of the CUDA kernels against the oracle and the reference's
 golden outputs (tests/golden, recorded from the reference itself).
 
-Tolerances (north star): bit-exact for dequantised FP8 -> fp32 weights,
+Tolerances: bit-exact for dequantised FP8 -> fp32 weights,
 top-k indices and the permutation; max-abs <= 2e-2 and cosine >= 0.9995 for
 bf16 layer outputs against the reference.  Against the fp32 evaluation of
 the same algorithm (what the kernels compute), the bar is tighter.
@@ -15,7 +15,7 @@ from oracle import moe_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-REF_MAXABS, REF_COS = 2e-2, 0.9995        # north-star bar vs the reference outputs
+REF_MAXABS, REF_COS = 2e-2, 0.9995        # layer-output tolerance vs the reference outputs
 FP32_COS = 0.99999                       # vs the fp32 oracle (output rounding only; see fp32_cos)
 
 
@@ -145,7 +145,7 @@ LAYER_CASES = [("q3_small", 1), ("q3_small", 5), ("q3_small", 64), ("q3_small_fp
 
 @pytest.mark.parametrize("name,T", LAYER_CASES)
 def test_layer_vs_reference_golden(name, T):
-    """Same idx/w as the reference run -> layer output within the north-star
+    """Same idx/w as the reference run -> layer output within the layer-output
     tolerance of the reference's own output, and tight vs the fp32 oracle."""
     shape, lw, info = case_layer(name)
     fx = fixture(name)

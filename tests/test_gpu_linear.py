@@ -6,8 +6,8 @@ accumulation, one rounding to the act dtype: against an fp32 evaluation of
 the same product it must agree to one act-dtype rounding (max-abs within one
 ulp of the largest output, at least 1e-2; cosine >= 0.99999).  The reference's own path
 (load_weight dequantises W to the act dtype, then F.linear in that dtype,
-loader/expert_loader.py:109-112) rounds W first; against it the north-star
-bar applies (cosine >= 0.9995).
+loader/expert_loader.py:109-112) rounds W first; against it the layer-output
+tolerance applies (cosine >= 0.9995).
 """
 import pytest
 import torch

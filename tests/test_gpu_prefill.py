@@ -9,7 +9,7 @@ reference's bf16).  `emulate` restates exactly that on the CPU, so the
 kernels must agree with it up to fp32 accumulation order: max-abs <= 1e-2,
 cosine >= 0.99999 and most elements bitwise equal.  Against the reference's
 own golden output (2048-token prefill of a Qwen3-30B-A3B layer) the
-north-star bar applies (max-abs 2e-2, cosine 0.9995).
+layer-output tolerance applies (max-abs 2e-2, cosine 0.9995).
 """
 import pytest
 import torch
@@ -186,7 +186,7 @@ def test_prefill_shared_expert(dt, T):
     """Qwen3.5-style layer (FP8 shared expert of the routed experts' size):
     the shared expert runs as one more group of the grouped GEMMs; the output
     matches the CPU restatement of that arithmetic and, within the
-    north-star bar, the fp32 oracle of the reference's layer."""
+    layer-output tolerance, the fp32 oracle of the reference's layer."""
     from turbomoe import ops, synth
     from gpu_util import oracle_fp32
     shape = synth.MoEShape(512, 256, 16, 4, 256)
