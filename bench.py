@@ -554,7 +554,86 @@ def run_ours(args, rank, world, local):
         res["qwen35_layer"] = c3
     if attn is not None:
         res["attention_linears"] = attn
+    if args.gdn_batches and world == 1:
+        try:
+            res["qwen35_linear_attention"] = gdn_measure(args, local)
+        except Exception as e:  # recorded on the line; the measurements above stand
+            res["qwen35_linear_attention"] = {"error": f"{type(e).__name__}: {e}"}
     return res
+
+
+def gdn_measure(args, local):
+    """Qwen3.5 linear-attention decode step (tm_gdn_decode) at 16 key heads,
+    32 value heads of 128, conv kernel 4, bf16: one launch per layer, batch B
+    sequences per launch, timed with CUDA events around a CUDA graph of
+    L layers' launches (L layers' distinct states: >= 256 MB, more than L2).
+    Algorithmic bytes per launch: the fp32 recurrent state read and written
+    (B x 32 x 64 KB x 2), the conv state read and written, this token's
+    qkv/z/a/b rows and the output, and the conv and norm weights."""
+    from turbomoe import ops
+    dev = torch.device("cuda", local)
+    Hk, Hv, K, dt = 16, 32, 4, torch.bfloat16
+    C = 2 * Hk * 128 + Hv * 128
+    hbm, src = _peaks()
+    g = torch.Generator(device=dev).manual_seed(SEED + 9)
+    conv_w = (torch.randn(C, K, generator=g, device=dev) * 0.5).to(dt)
+    A_log = torch.log(torch.rand(Hv, generator=g, device=dev) * 16 + 1e-3)
+    dt_bias = torch.randn(Hv, generator=g, device=dev) * 0.5
+    norm_w = torch.ones(128, dtype=dt, device=dev)
+    out = {}
+    for B in [int(b) for b in args.gdn_batches.split(",") if b]:
+        state_bytes = B * Hv * 128 * 128 * 4
+        L = max(2, -(-(256 << 20) // state_bytes))
+        layers = []
+        for _ in range(L):
+            layers.append(dict(
+                qkv=torch.randn(B, C, generator=g, device=dev).to(dt),
+                z=torch.randn(B, Hv * 128, generator=g, device=dev).to(dt),
+                a=torch.randn(B, Hv, generator=g, device=dev).to(dt),
+                b=torch.randn(B, Hv, generator=g, device=dev).to(dt),
+                cin=torch.randn(B, C, K, generator=g, device=dev).to(dt),
+                cout=torch.empty(B, C, K, dtype=dt, device=dev),
+                S=torch.randn(B, Hv, 128, 128, generator=g, device=dev) * 0.05,
+                o=torch.empty(B, Hv * 128, dtype=dt, device=dev)))
+
+        def run():
+            for t in layers:
+                ops.gdn_decode(t["qkv"], t["z"], t["a"], t["b"], conv_w, A_log, dt_bias, norm_w, t["cin"],
+                               t["cout"], t["S"], Hk, 1e-6, out=t["o"])
+
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                run()
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                run()
+            for _ in range(3):
+                graph.replay()
+            reps = max(3, (20 << 30) // (L * state_bytes * 2 + 1))
+            reps = min(reps, 200)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            e0.record(s)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(s)
+            torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1000.0 / (reps * L)
+        per_seq = 2 * Hv * 128 * 128 * 4 + 2 * C * K * 2 + (C + 2 * Hv * 128 + 2 * Hv) * 2
+        nbytes = B * per_seq + C * K * 2 + 128 * 2 + 2 * Hv * 4
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[f"batch_{B}"] = {"us_per_layer": round(us, 3), "algorithmic_bytes": nbytes, "gbs": round(gbs, 1),
+                             "frac": round(gbs / hbm, 4), "layers_rotated": L, "replays": reps}
+        del graph, layers
+        torch.cuda.empty_cache()
+    out["workload"] = ("Qwen3.5 linear-attention decode step (gated delta rule: conv update, q/k l2norm, "
+                       "gates, fp32 state update, gated RMSNorm; 16 key / 32 value heads of 128, conv 4, bf16), "
+                       "one launch per layer, states rotated over more than L2")
+    out["peak"] = {"hbm_gbs": hbm, "source": src}
+    return out
 
 
 # ------------------------------------------ full-model greedy decode ----
@@ -1148,6 +1227,9 @@ def main():
                          "at this KV context (0 = skip)")
     ap.add_argument("--ep-zipf", type=float, default=1.2,
                     help="expert-parallel decode: also time Zipf-skewed routing with this exponent (0 = skip)")
+    ap.add_argument("--gdn-batches", default="1,256",
+                    help="also time the Qwen3.5 linear-attention decode step at these batch sizes, comma-separated "
+                         "(empty = skip; 1 GPU only)")
     ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",
                     help="ep workload: NVLink peer-memory kernels (tm_ep_*) or NCCL all-to-all")
     args = ap.parse_args()

@@ -393,6 +393,36 @@ int tm_lm_head_argmax(const void *x, int hidden, int act_dtype, const void *w_bf
                       int64_t *token, void *ws, int64_t ws_bytes, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Qwen3.5 linear attention, one decode token per sequence (batch rows).
+ * Replaces, for a "linear_attention" layer with a cached state, the core of
+ * Qwen3_5MoeGatedDeltaNet.forward that execution/layer_executor.py:134-139
+ * calls with the reference's Qwen35Cache (cache/qwen35_cache.py:43-64):
+ * torch_causal_conv1d_update, the gates beta = sigmoid(b) and
+ * g = -exp(A_log) * softplus(a + dt_bias), torch_recurrent_gated_delta_rule
+ * with q/k l2-normalised in the act dtype and q scaled by 1/sqrt(128), and
+ * Qwen3_5MoeRMSNormGated (transformers 5.5.0 modeling_qwen3_5_moe.py:176-191,
+ * :211-226, :315-354, :484-533).  The in_proj_* and out_proj GEMMs stay with
+ * the caller.
+ *   qkv [batch][2*n_k_heads*128 + n_v_heads*128] (q heads, k heads, v heads);
+ *   z [batch][n_v_heads*128]; a, b [batch][n_v_heads]; conv_w
+ *   [conv_dim][conv_kernel] (conv1d.weight without its middle axis); norm_w
+ *   [128]; all act dtype.  A_log, dt_bias: fp32 [n_v_heads].
+ *   conv_state_in -> conv_state_out: [batch][conv_dim][conv_kernel] act, the
+ *   state shifted left with this token appended; the two must not overlap
+ *   (value heads that share a key head read the old q/k columns while one of
+ *   them writes the new ones): keep two buffers and swap them per step.
+ *   recurrent_state: fp32 [batch][n_v_heads][128][128] (S[d_k][d_v]), updated
+ *   in place, 16-byte aligned.
+ *   out: [batch][n_v_heads*128] act, the gated-normed output (out_proj input).
+ * head_k_dim = head_v_dim = 128, n_v_heads a multiple of n_k_heads,
+ * conv_kernel 1..8, batch <= 65535. */
+int tm_gdn_decode(const void *qkv, const void *z, const void *a, const void *b, int64_t batch, int n_k_heads,
+                  int n_v_heads, int head_k_dim, int head_v_dim, int conv_kernel, int act_dtype,
+                  const void *conv_w, const float *A_log, const float *dt_bias, const void *norm_w, float eps,
+                  const void *conv_state_in, void *conv_state_out, float *recurrent_state, void *out,
+                  void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Expert parallelism over NVLink peer memory (no counterpart in the reference,
  * which runs batch 1 on one device: runtime/engine.py:103-107,158; per token
  * the arithmetic is MoEExecutor.execute_layer, execution/moe.py:99-208).

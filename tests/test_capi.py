@@ -115,3 +115,28 @@ def test_prefetch_experts_argument_errors_without_launch():
     assert rc == _lib.TM_ERR_INVALID and b"multiple of 16" in L.tm_last_error()
     rc = f(24, 3145728, 128, 16, 8, None)
     assert rc == _lib.TM_ERR_INVALID and b"aligned" in L.tm_last_error()
+
+
+def test_gdn_decode_argument_errors_without_launch():
+    """tm_gdn_decode rejects null pointers, head dims other than 128, value
+    heads that are not a multiple of the key heads, an unaligned recurrent
+    state and overlapping conv-state buffers on the host."""
+    L = _lib.lib()
+    f = L.tm_gdn_decode
+    BF16 = _lib.TM_DTYPE_BF16
+
+    def call(qkv=256, batch=1, hk=16, hv=32, dk=128, dv=128, K=4, dt=BF16, cin=1 << 20, cout=1 << 24,
+             state=1 << 26):
+        # qkv, z, a, b, batch, Hk, Hv, dk, dv, K, dtype, conv_w, A_log, dt_bias, norm_w, eps, conv_in,
+        # conv_out, state, out, stream
+        return f(qkv, 512, 768, 1024, batch, hk, hv, dk, dv, K, dt, 2048, 4096, 8192, 16384, 1e-6, cin, cout,
+                 state, 1 << 28, None)
+
+    assert call(qkv=None) == _lib.TM_ERR_INVALID and b"null" in L.tm_last_error()
+    assert call(dk=64) == _lib.TM_ERR_INVALID and b"head dims" in L.tm_last_error()
+    assert call(hv=24) == _lib.TM_ERR_INVALID and b"value heads" in L.tm_last_error()
+    assert call(K=9) == _lib.TM_ERR_INVALID and b"conv kernel" in L.tm_last_error()
+    assert call(batch=0) == _lib.TM_ERR_INVALID and b"batch" in L.tm_last_error()
+    assert call(dt=7) == _lib.TM_ERR_INVALID and b"dtype" in L.tm_last_error()
+    assert call(state=(1 << 26) + 8) == _lib.TM_ERR_INVALID and b"16-byte" in L.tm_last_error()
+    assert call(cout=(1 << 20) + 4096) == _lib.TM_ERR_INVALID and b"overlap" in L.tm_last_error()

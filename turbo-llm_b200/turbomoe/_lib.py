@@ -68,6 +68,8 @@ SIGNATURES = {
                                     _p]),
     "tm_lm_head_workspace_bytes": (_i64, []),
     "tm_lm_head_argmax": (_i, [_p, _i, _i, _p, _i64, _p, _p, _p, _i64, _p]),
+    "tm_gdn_decode": (_i, [_p, _p, _p, _p, _i64, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, C.c_float, _p, _p,
+                          _p, _p, _p]),
     "tm_ep_buffer_bytes": (_i64, [_i, _i64, _i, _i, _i, _i]),
     "tm_ep_create": (_i, [_i, _i, _i, _i, _i, _i, _i, _i64, _p, C.POINTER(_p)]),
     "tm_ep_connect": (_i, [_p, _p]),

@@ -494,3 +494,49 @@ def fp8_linear(x: torch.Tensor, pl: PackedLinear, residual: torch.Tensor | None 
     check(lib().tm_fp8_linear(x.data_ptr(), T, K, pl.out_features, _code(x.dtype), pl.w.data_ptr(),
                               pl.s.data_ptr(), _ptr(res), out.data_ptr(), None, _stream(x)), "tm_fp8_linear")
     return out
+
+
+# ------------------------------------------------------------------ K9 ----
+def gdn_decode(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: torch.Tensor, conv_w: torch.Tensor,
+               A_log: torch.Tensor, dt_bias: torch.Tensor, norm_w: torch.Tensor, conv_state: torch.Tensor,
+               conv_state_out: torch.Tensor, recurrent_state: torch.Tensor, n_k_heads: int, eps: float = 1e-6,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode token of Qwen3.5 linear attention per batch row
+    (tm_gdn_decode): conv-state update + depthwise conv + SiLU, q/k l2norm,
+    gates, gated delta rule on the fp32 ``recurrent_state`` [B, Hv, 128, 128]
+    (updated in place) and the gated RMSNorm.  ``conv_state`` [B, conv_dim,
+    K] is read; the shifted state goes to ``conv_state_out`` (a different
+    buffer).  qkv [B, conv_dim], z [B, Hv*128], a/b [B, Hv], conv_w
+    [conv_dim, K], norm_w [128] in the act dtype; A_log, dt_bias [Hv] (any
+    float dtype, passed as fp32).  Returns [B, Hv*128] in the act dtype."""
+    _need_cuda(qkv, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, conv_state_out, recurrent_state)
+    B, conv_dim = qkv.shape
+    Hv = a.shape[-1]
+    K = conv_w.shape[-1]
+    dt = qkv.dtype
+    if recurrent_state.dtype != torch.float32 or tuple(recurrent_state.shape) != (B, Hv, 128, 128):
+        raise TurboMoEError(f"recurrent_state must be fp32 [{B}, {Hv}, 128, 128]")
+    if not recurrent_state.is_contiguous():
+        raise TurboMoEError("recurrent_state must be contiguous (it is updated in place)")
+    if conv_dim != 2 * n_k_heads * 128 + Hv * 128 or tuple(conv_w.shape) != (conv_dim, K):
+        raise TurboMoEError(f"qkv [{B}, {conv_dim}] / conv_w {tuple(conv_w.shape)} do not match "
+                            f"{n_k_heads} key heads and {Hv} value heads of 128")
+    for name, t, shape in (("z", z, (B, Hv * 128)), ("a", a, (B, Hv)), ("b", b, (B, Hv)),
+                           ("conv_state", conv_state, (B, conv_dim, K)),
+                           ("conv_state_out", conv_state_out, (B, conv_dim, K)), ("norm_w", norm_w, (128,))):
+        if tuple(t.shape) != shape or t.dtype != dt:
+            raise TurboMoEError(f"{name} must be {dt} {list(shape)}, got {t.dtype} {list(t.shape)}")
+    if not conv_state_out.is_contiguous():
+        raise TurboMoEError("conv_state_out must be contiguous")
+    if A_log.numel() != Hv or dt_bias.numel() != Hv:
+        raise TurboMoEError(f"A_log and dt_bias must hold {Hv} values (one per value head)")
+    if out is None:
+        out = torch.empty(B, Hv * 128, dtype=dt, device=qkv.device)
+    qkv, z, a, b, conv_w, conv_state = (t.contiguous() for t in (qkv, z, a, b, conv_w, conv_state))
+    A32 = A_log.float().contiguous()
+    dt32 = dt_bias.float().contiguous()
+    check(lib().tm_gdn_decode(qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(), B, n_k_heads, Hv, 128, 128,
+                              K, _code(dt), conv_w.data_ptr(), A32.data_ptr(), dt32.data_ptr(),
+                              norm_w.contiguous().data_ptr(), eps, conv_state.data_ptr(), conv_state_out.data_ptr(),
+                              recurrent_state.data_ptr(), out.data_ptr(), _stream(qkv)), "tm_gdn_decode")
+    return out
