@@ -11,8 +11,10 @@ in_proj_* and out_proj GEMMs stay the module's own ``nn.Linear`` calls.
 State handling follows the cache's interface: the recurrent state (fp32
 [B, Hv, 128, 128]) is updated in place; the conv state is written to a second
 buffer that replaces the cache's through ``update_conv_state`` (the kernel
-cannot shift it in place), and the replaced buffer becomes the next step's
-output buffer, so a step allocates nothing after the first.
+cannot shift it in place), and the replaced buffer becomes the module's
+output buffer for its next decode step, whichever cache that step uses, so a
+step allocates nothing after the first.  Caches must therefore not share
+conv-state tensors (clone the states to copy a cache).
 
 ``install(module)`` routes the module's decode calls here.  Calls without a
 cached state or with more than one token (the prompt, which the module runs
