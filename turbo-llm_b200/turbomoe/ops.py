@@ -532,6 +532,8 @@ def gdn_decode(qkv: torch.Tensor, z: torch.Tensor, a: torch.Tensor, b: torch.Ten
         raise TurboMoEError(f"A_log and dt_bias must hold {Hv} values (one per value head)")
     if out is None:
         out = torch.empty(B, Hv * 128, dtype=dt, device=qkv.device)
+    elif tuple(out.shape) != (B, Hv * 128) or out.dtype != dt or not out.is_contiguous():
+        raise TurboMoEError(f"out must be a contiguous {dt} [{B}, {Hv * 128}] tensor")
     qkv, z, a, b, conv_w, conv_state = (t.contiguous() for t in (qkv, z, a, b, conv_w, conv_state))
     A32 = A_log.float().contiguous()
     dt32 = dt_bias.float().contiguous()
