@@ -118,3 +118,54 @@ class _TinySource:
 
     def close(self):
         pass
+
+
+LINEAR_ATTN = r"""
+import copy, json, sys
+import torch
+sys.path[:0] = [sys.argv[1], sys.argv[2]]
+import cache.qwen35_cache as qc
+from turbomoe import linear_attn
+from turbomoe._lib import TurboMoEError
+from transformers import Qwen3_5MoeTextConfig
+from transformers.models.qwen3_5_moe import modeling_qwen3_5_moe as M
+cfg = Qwen3_5MoeTextConfig(hidden_size=256, linear_num_key_heads=1, linear_num_value_heads=2,
+                           linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=4)
+torch.manual_seed(0)
+ref = M.Qwen3_5MoeGatedDeltaNet(cfg, layer_idx=0).eval()
+mod = copy.deepcopy(ref)
+linear_attn.install(mod)
+ca, cb = qc.Qwen35Cache(num_layers=1), qc.Qwen35Cache(num_layers=1)
+x = torch.randn(1, 4, 256)
+out = {"cache_module": qc.__file__}
+with torch.no_grad():
+    ya = ref(hidden_states=x, cache_params=ca, attention_mask=None)
+    yb = mod(hidden_states=x, cache_params=cb, attention_mask=None)
+    out["prompt_equal"] = bool(torch.equal(ya, yb))
+    out["state_equal"] = bool(torch.equal(ca.layers[0].recurrent_states, cb.layers[0].recurrent_states))
+    try:
+        mod(hidden_states=x[:, :1], cache_params=cb, attention_mask=None)
+        out["decode"] = "ran"
+    except TurboMoEError as e:
+        out["decode"] = str(e)
+print(json.dumps(out))
+"""
+
+
+def test_linear_attention_call_site_with_the_reference_cache():
+    """execution/layer_executor.py:134-139 calls ``layer_module.linear_attn(
+    hidden_states=..., cache_params=kv_cache, attention_mask=...)`` with the
+    reference's Qwen35Cache.  After ``turbomoe.linear_attn.install`` the call
+    site binds, the prompt runs the module's own forward with that cache (same
+    outputs and states as the unmodified module), and a decode step goes to
+    tm_gdn_decode, which on the CPU refuses (no CPU fallback)."""
+    sites = _calls(os.path.join(REF, "execution", "layer_executor.py"), "linear_attn")
+    assert sites and all(npos == 0 and set(kws) == {"hidden_states", "cache_params", "attention_mask"}
+                         for npos, kws in sites), sites
+    r = subprocess.run([sys.executable, "-c", LINEAR_ATTN, PKG, REF], capture_output=True, text=True, check=True,
+                       timeout=600)
+    import json
+    got = json.loads(r.stdout.strip().splitlines()[-1])
+    assert got["cache_module"].startswith(REF + os.sep), got
+    assert got["prompt_equal"] and got["state_equal"], got
+    assert "CUDA" in got["decode"], got
