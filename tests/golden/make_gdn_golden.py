@@ -1,6 +1,6 @@
 """Record decode steps of Qwen3.5 linear attention as the reference runs them.
 
-    python tests/golden/make_gdn_golden.py <path to the reference checkout> [--dtype fp32|bf16]
+    python tests/golden/make_gdn_golden.py <path to the reference checkout> [--dtype fp32|bf16|fp16]
 
 The reference's Qwen3.5 "linear_attention" layers call Hugging Face's
 ``Qwen3_5MoeGatedDeltaNet`` with the reference's ``Qwen35Cache``
@@ -34,7 +34,7 @@ BATCH, HIDDEN, HK, HV, KCONV, PREFILL, STEPS, SEED = 2, 256, 1, 2, 4, 5, 3, 7
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("reference", help="path to the reference checkout")
-    ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32")
+    ap.add_argument("--dtype", choices=["fp32", "bf16", "fp16"], default="fp32")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     from cache.qwen35_cache import Qwen35Cache
@@ -43,7 +43,7 @@ def main():
     from transformers.models.qwen3_5_moe import modeling_qwen3_5_moe as M
 
     assert not M.is_fast_path_available, "the fused linear-attention libraries changed the path"
-    dt = {"fp32": torch.float32, "bf16": torch.bfloat16}[args.dtype]
+    dt = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[args.dtype]
     cfg = Qwen3_5MoeTextConfig(hidden_size=HIDDEN, linear_num_key_heads=HK, linear_num_value_heads=HV,
                                linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=KCONV,
                                rms_norm_eps=1e-6)

@@ -104,7 +104,7 @@ def test_golden_meta_records_torch():
     assert "torch" in meta() and meta()["cases"]
 
 
-@pytest.mark.parametrize("name", ["fp32", "bf16"])
+@pytest.mark.parametrize("name", ["fp32", "bf16", "fp16"])
 def test_gdn_oracle_matches_reference(name):
     """oracle/gdn_oracle.py replays the Qwen3.5 linear-attention decode steps
     recorded from Hugging Face's Qwen3_5MoeGatedDeltaNet with the reference's
