@@ -140,3 +140,26 @@ def test_gdn_decode_argument_errors_without_launch():
     assert call(dt=7) == _lib.TM_ERR_INVALID and b"dtype" in L.tm_last_error()
     assert call(state=(1 << 26) + 8) == _lib.TM_ERR_INVALID and b"16-byte" in L.tm_last_error()
     assert call(cout=(1 << 20) + 4096) == _lib.TM_ERR_INVALID and b"overlap" in L.tm_last_error()
+
+
+# Destroying a NULL context is a no-op (like free(NULL)); the version query takes no arguments.
+_NULL_OK = {"tm_abi_version", "tm_ep_destroy"}
+
+
+@pytest.mark.skipif(__import__("torch").cuda.is_available(),
+                    reason="all-NULL calls are only made where no device could be reached")
+def test_every_entry_point_rejects_null_arguments_on_the_host():
+    """Every int-returning entry point, called with NULL pointers and zero
+    sizes, returns TM_ERR_INVALID with a message before any CUDA call (on a
+    machine without a GPU a call that got as far as the runtime would return
+    TM_ERR_CUDA instead)."""
+    L = _lib.lib()
+    checked = 0
+    for name, (res, args) in sorted(_lib.SIGNATURES.items()):
+        if res is not _lib._i or name in _NULL_OK:
+            continue
+        vals = [0.0 if a is ctypes.c_float else (0 if a in (_lib._i, _lib._i64) else None) for a in args]
+        rc = getattr(L, name)(*vals)
+        assert rc == _lib.TM_ERR_INVALID and L.tm_last_error(), (name, rc, L.tm_last_error())
+        checked += 1
+    assert checked >= 30
